@@ -1,0 +1,250 @@
+"""Fusion strategies (API of cacheblend-hf-v7 ``fusor.py``).
+
+``fuse_selective`` is CacheBlend's selective KV recompute, with its five
+data-parallel stages on the sm_100a kernels:
+
+  (a)+(b) ``assemble_kernel``   chunk K/V of every cached layer gathered into one
+          token-major fused cache [L][S][Hkv*D], K rotated to its fused
+          position in the same pass (one launch for all layers, on a side
+          stream that overlaps the dense layers before the check layer);
+  (c)     ``deviation_kernel`` + ``topk_kernel``  HKVD at the check layer,
+          force-include of the last position on the device (no host sync);
+  (b)+(d) ``rope_scatter_kernel``  RoPE of the fresh Q/K rows and their
+          scatter into the fused cache, per layer;
+  (e)     ``partial_attn_kernel``  selected queries against the full fused KV
+          on tcgen05 tensor cores (causal by position, GQA without expansion).
+
+Projections, norms and MLPs stay in the HF modules (cuBLAS through torch).
+The returned cache holds views of the fused buffers (no staging copy).
+``fuse_full_recompute`` / ``fuse_full_reuse`` / ``fuse_prefix_cache`` keep the
+reference's behaviour (they are the ratio==0 / ratio>=1 / single-chunk
+shortcuts of ``fuse_selective``) and run through the HF forward.
+"""
+from __future__ import annotations
+
+import torch
+
+from cacheblend import ops
+from cacheblend.chunker import Chunk, chunk_offsets, fused_input_ids
+from cacheblend.kv_store import KVStore
+from cacheblend.model import LayerwiseOutput, attach_cache_layers, new_dynamic_cache
+from cacheblend.rope import rope_table_for
+
+
+def fuse_full_recompute(layerwise_model, chunks: list[Chunk], return_layerwise_output: bool = False):
+    """Plain prefill over the fused ids (reference fusor.py:25-38)."""
+    ids = fused_input_ids(chunks, device=layerwise_model.device)
+    with torch.inference_mode():
+        out = layerwise_model.forward_layerwise(input_ids=ids, use_cache=True)
+    return out if return_layerwise_output else out.logits
+
+
+def _store_entries(kv_store: KVStore, chunks, who: str):
+    entries = []
+    for c in chunks:
+        if not kv_store.has(c.chunk_id):
+            raise KeyError(f"{who}: chunk {c.chunk_id!r} not in KVStore")
+        entries.append(kv_store.get(c.chunk_id))
+    return entries
+
+
+def _run_with_kv_hooks(layerwise_model, chunks, k_for_layer, v_for_layer, return_layerwise_output):
+    handles = []
+    for li, layer in enumerate(layerwise_model._inner.layers):
+        handles.append(layer.self_attn.k_proj.register_forward_hook(
+            lambda _m, _i, out, _li=li: k_for_layer(_li, out)))
+        handles.append(layer.self_attn.v_proj.register_forward_hook(
+            lambda _m, _i, out, _li=li: v_for_layer(_li, out)))
+    try:
+        return fuse_full_recompute(layerwise_model, chunks, return_layerwise_output)
+    finally:
+        for h in handles:
+            h.remove()
+
+
+def fuse_full_reuse(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
+                    return_layerwise_output: bool = False):
+    """Every chunk token reuses its stored pre-RoPE K and V; HF RoPE then places
+    them at fused positions (reference fusor.py:41-117)."""
+    if len(chunks) <= 1:
+        return fuse_full_recompute(layerwise_model, chunks, return_layerwise_output)
+    entries = _store_entries(kv_store, chunks, "fuse_full_reuse")
+    K = [torch.cat([e["K"][l] for e in entries], dim=1) for l in range(layerwise_model.num_layers)]
+    V = [torch.cat([e["V"][l] for e in entries], dim=1) for l in range(layerwise_model.num_layers)]
+    return _run_with_kv_hooks(layerwise_model, chunks, lambda l, _o: K[l], lambda l, _o: V[l],
+                              return_layerwise_output)
+
+
+def fuse_prefix_cache(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
+                      return_layerwise_output: bool = False):
+    """Only the first chunk's K/V come from the store (reference fusor.py:120-185)."""
+    if len(chunks) <= 1:
+        return fuse_full_recompute(layerwise_model, chunks, return_layerwise_output)
+    first = chunks[0]
+    if not kv_store.has(first.chunk_id):
+        raise KeyError(f"fuse_prefix_cache: first chunk {first.chunk_id!r} not in KVStore")
+    entry = kv_store.get(first.chunk_id)
+    n0 = first.length
+
+    def patch(src):
+        def f(l, out):
+            res = out.clone()
+            res[:, :n0, :] = src[l]
+            return res
+        return f
+    return _run_with_kv_hooks(layerwise_model, chunks, patch(entry["K"]), patch(entry["V"]),
+                              return_layerwise_output)
+
+
+# ---------------------------------------------------------------------------
+# selective recompute
+# ---------------------------------------------------------------------------
+def _side_stream(layerwise_model, device):
+    s = getattr(layerwise_model, "_cbk_side_stream", None)
+    if s is None or s.device != device:
+        s = torch.cuda.Stream(device=device)
+        try:
+            layerwise_model._cbk_side_stream = s
+        except AttributeError:
+            pass
+    return s
+
+
+class _Geometry:
+    def __init__(self, layerwise_model):
+        attn0 = layerwise_model._inner.layers[0].self_attn
+        cfg = attn0.config
+        self.n_kv = cfg.num_key_value_heads
+        self.n_q = cfg.num_attention_heads
+        self.head_dim = attn0.head_dim
+        self.kv_dim = self.n_kv * self.head_dim
+        self.q_dim = self.n_q * self.head_dim
+        self.scaling = float(attn0.scaling)
+
+
+def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_mode):
+    """q/k/v projections -> (b)+(d) RoPE + scatter into the fused cache ->
+    (e) partial attention -> o_proj.  Returns the attention output rows."""
+    attn = layer.self_attn
+    q = attn.q_proj(hn)
+    k_pre = attn.k_proj(hn)
+    v = attn.v_proj(hn)
+    q_rot = ops.rope_scatter(q[0], k_pre[0], v[0], pos, gather, S, geo.n_q, geo.n_kv, geo.head_dim,
+                             rope, kc, vc, mode=rope_mode, status=status)
+    a = ops.partial_attn(q_rot, kc, vc, pos, geo.n_q, geo.n_kv, geo.head_dim, geo.scaling,
+                         status=status)
+    return attn.o_proj(a.unsqueeze(0)), k_pre
+
+
+def _mlp_block(layer, h):
+    return h + layer.mlp(layer.post_attention_layernorm(h))
+
+
+def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
+                   recompute_ratio: float = 0.15, check_layer: int = 1,
+                   return_layerwise_output: bool = False, return_hkvd_indices: bool = False,
+                   rope_mode: str = "ref", status: torch.Tensor | None = None):
+    """CacheBlend selective recompute (reference fusor.py:193-497).
+
+    Layers < check_layer: full forward.  Check layer: HKVD picks the
+    max(1, int(S * ratio)) tokens whose fresh pre-RoPE K deviates most from the
+    cached K (the last position is always included); from there on only those
+    rows are recomputed, against the full fused cache (cached, RoPE-shifted K/V
+    elsewhere).  Returns logits (1, S, vocab) with rows outside the selection
+    zero, or a LayerwiseOutput with the full-length cache; optionally the
+    selected indices.
+
+    ``rope_mode`` "ref" reproduces HF's 16-bit RoPE rounding, "fp32" rotates in
+    fp32 with one rounding.  ``status`` (int32 CUDA tensor) collects device-side
+    error bits."""
+    if recompute_ratio == 0:
+        return fuse_full_reuse(layerwise_model, chunks, kv_store, return_layerwise_output)
+    if recompute_ratio >= 1:
+        return fuse_full_recompute(layerwise_model, chunks, return_layerwise_output)
+    if len(chunks) <= 1:
+        return fuse_full_recompute(layerwise_model, chunks, return_layerwise_output)
+
+    lw = layerwise_model
+    inner = lw._inner
+    n_layers = lw.num_layers
+    ck = int(check_layer)
+    if not 0 <= ck < n_layers:
+        raise IndexError(f"check_layer {ck} out of range for {n_layers} layers")
+    device = lw.device
+    if device.type != "cuda":
+        raise RuntimeError("fuse_selective runs on the sm_100a kernels: the model must be on CUDA")
+    dtype = lw.dtype
+    ops.dtype_code(dtype)
+    geo = _Geometry(lw)
+
+    entries = _store_entries(kv_store, chunks, "fuse_selective")
+    offsets = chunk_offsets(chunks)
+    S = offsets[-1][1]
+    k_sel = max(1, min(S, int(S * recompute_ratio)))
+    cur = torch.cuda.current_stream(device)
+
+    with torch.inference_mode():
+        table = ops.ChunkTable(entries, range(ck, n_layers), device)
+        if table.S != S:
+            raise ValueError(f"stored chunk lengths sum to {table.S}, chunks say {S}")
+        rope = rope_table_for(lw, S, device)
+        fused_k = torch.empty((n_layers, S, geo.kv_dim), dtype=dtype, device=device)
+        fused_v = torch.empty_like(fused_k)
+
+        # (a)+(b): all cached layers in one launch, overlapped with layers < ck
+        side = _side_stream(lw, device)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            ops.assemble_kv(table, ck, n_layers, geo.n_kv, geo.head_dim, rope, fused_k, fused_v,
+                            mode=rope_mode, status=status)
+        assembled = torch.cuda.Event()
+        assembled.record(side)
+        fused_k.record_stream(side)
+        fused_v.record_stream(side)
+
+        ids = fused_input_ids(chunks, device=device)
+        lw._pre_rope_k = {}
+        pos_all = torch.arange(S, device=device, dtype=torch.int64)
+        h = inner.embed_tokens(ids)
+
+        for li in range(ck):                                  # dense layers
+            layer = inner.layers[li]
+            a, _ = _attention_block(layer, geo, layer.input_layernorm(h), pos_all, S, rope,
+                                    fused_k[li], fused_v[li], False, status, rope_mode)
+            h = _mlp_block(layer, h + a)
+
+        # check layer: full projections, HKVD, then sparse from here on
+        layer = inner.layers[ck]
+        attn = layer.self_attn
+        hn = layer.input_layernorm(h)
+        q = attn.q_proj(hn)
+        k_pre = attn.k_proj(hn)
+        v = attn.v_proj(hn)
+        idx, deviations = ops.hkvd_select(k_pre[0], table, ck, k_sel, force_last=True, status=status)
+        cur.wait_event(assembled)
+        q_rot = ops.rope_scatter(q[0], k_pre[0], v[0], idx, True, S, geo.n_q, geo.n_kv, geo.head_dim,
+                                 rope, fused_k[ck], fused_v[ck], mode=rope_mode, status=status)
+        a = ops.partial_attn(q_rot, fused_k[ck], fused_v[ck], idx, geo.n_q, geo.n_kv, geo.head_dim,
+                             geo.scaling, status=status)
+        hs = h.index_select(1, idx) + attn.o_proj(a.unsqueeze(0))
+        hs = _mlp_block(layer, hs)
+
+        for li in range(ck + 1, n_layers):                    # sparse layers
+            layer = inner.layers[li]
+            a, _ = _attention_block(layer, geo, layer.input_layernorm(hs), idx, S, rope,
+                                    fused_k[li], fused_v[li], False, status, rope_mode)
+            hs = _mlp_block(layer, hs + a)
+
+        logits_sparse = lw.model.lm_head(inner.norm(hs))      # (1, k, vocab)
+        logits = torch.zeros((1, S, logits_sparse.shape[-1]), dtype=logits_sparse.dtype, device=device)
+        logits[0].index_copy_(0, idx, logits_sparse[0])
+
+    result = logits
+    if return_layerwise_output:
+        kv = [(fused_k[l].view(S, geo.n_kv, geo.head_dim).permute(1, 0, 2).unsqueeze(0),
+               fused_v[l].view(S, geo.n_kv, geo.head_dim).permute(1, 0, 2).unsqueeze(0))
+              for l in range(n_layers)]
+        result = LayerwiseOutput(logits=logits, past_key_values=attach_cache_layers(new_dynamic_cache(), kv))
+    if return_hkvd_indices:
+        return result, idx
+    return result

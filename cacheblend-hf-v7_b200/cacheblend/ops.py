@@ -1,0 +1,267 @@
+"""torch-facing wrappers of the libcbk kernels.
+
+Each wrapper validates devices, dtypes, shapes and contiguity, passes raw
+device pointers plus the current CUDA stream to the C ABI, and maps return
+codes to Python exceptions.  Nothing here runs on the CPU: a non-CUDA tensor is
+an error.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Sequence
+
+import torch
+
+from cacheblend import _native as N
+
+_DT = {torch.bfloat16: N.CBK_BF16, torch.float16: N.CBK_F16}
+ROPE_MODES = {"ref": N.CBK_ROPE_REF, "fp32": N.CBK_ROPE_FP32}
+
+
+def _vp(x) -> ctypes.c_void_p:
+    if x is None:
+        return ctypes.c_void_p(0)
+    return ctypes.c_void_p(x.data_ptr() if isinstance(x, torch.Tensor) else int(x))
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt not in _DT:
+        raise NotImplementedError(f"libcbk kernels support bfloat16/float16 tensors, got {dt}")
+    return _DT[dt]
+
+
+def require_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("cacheblend kernels need CUDA tensors (no CPU path); got a "
+                               f"{t.device} tensor")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _rows(t: torch.Tensor, name: str) -> torch.Tensor:
+    """Flatten to 2-D rows with unit inner stride and 16-byte aligned rows."""
+    t2 = t.reshape(-1, t.shape[-1])
+    if t2.stride(-1) != 1 or t2.stride(0) % 8 or t2.data_ptr() % 16:
+        t2 = t2.contiguous()
+    return t2
+
+
+# ---------------------------------------------------------------------------
+# RoPE
+# ---------------------------------------------------------------------------
+def rope_table(inv_freq: torch.Tensor, n_pos: int, scaling: float = 1.0) -> torch.Tensor:
+    """(n_pos, D/2, 2) fp32 cos/sin table for positions 0..n_pos-1."""
+    dev = require_cuda(inv_freq)
+    inv = inv_freq.to(device=dev, dtype=torch.float32).contiguous()
+    half = inv.numel()
+    table = torch.empty((int(n_pos), half, 2), dtype=torch.float32, device=dev)
+    N.check(N.LIB.cbk_rope_table(_vp(inv), half, int(n_pos), float(scaling), _vp(table), _stream(dev)),
+            "cbk_rope_table")
+    return table
+
+
+def rope_rows(x: torch.Tensor, positions: torch.Tensor, table: torch.Tensor, head_dim: int,
+              mode: str = "ref", out: torch.Tensor | None = None, status=None) -> torch.Tensor:
+    """out[r] = RoPE(x[r], positions[r]) for rows of n_heads*head_dim elements."""
+    dev = require_cuda(x, positions, table)
+    xr = _rows(x, "x")
+    pos = positions.reshape(-1).to(device=dev, dtype=torch.int64).contiguous()
+    if pos.numel() != xr.shape[0]:
+        raise ValueError(f"positions ({pos.numel()}) must match rows ({xr.shape[0]})")
+    if out is None:
+        out = torch.empty_like(xr)
+    n_heads = xr.shape[1] // head_dim
+    if n_heads * head_dim != xr.shape[1]:
+        raise ValueError(f"row width {xr.shape[1]} is not a multiple of head_dim {head_dim}")
+    N.check(N.LIB.cbk_rope_rows(_vp(xr), _vp(out), xr.shape[0], n_heads, head_dim,
+                                dtype_code(x.dtype), _vp(table), table.shape[0], _vp(pos),
+                                ROPE_MODES[mode], _vp(status), _stream(dev)), "cbk_rope_rows")
+    return out.view(x.shape)
+
+
+# ---------------------------------------------------------------------------
+# chunk tables
+# ---------------------------------------------------------------------------
+class ChunkTable:
+    """Device descriptor table of chunk tensors: [layer][chunk] -> (K ptr, V ptr),
+    plus the chunk start offsets (n_chunks + 1) in the fused sequence.
+
+    Holds references to the chunk tensors so they outlive the kernels."""
+
+    def __init__(self, entries: Sequence[dict], layers: Sequence[int], device: torch.device):
+        self.n_chunks = len(entries)
+        self.layers = list(layers)
+        lens = []
+        self._keep = []
+        host = torch.empty((len(self.layers), self.n_chunks, 2), dtype=torch.int64, pin_memory=True)
+        hv = host.numpy()
+        kv_dim = None
+        for c, e in enumerate(entries):
+            for li, l in enumerate(self.layers):
+                k = _chunk_rows(e["K"][l], device)
+                v = _chunk_rows(e["V"][l], device)
+                if k.shape != v.shape:
+                    raise ValueError("chunk K and V shapes differ")
+                if kv_dim is None:
+                    kv_dim = k.shape[1]
+                if k.shape[1] != kv_dim:
+                    raise ValueError("chunk tensors have different widths")
+                self._keep += [k, v]
+                hv[li, c, 0] = k.data_ptr()
+                hv[li, c, 1] = v.data_ptr()
+                if li == 0:
+                    lens.append(k.shape[0])
+                elif k.shape[0] != lens[c]:
+                    raise ValueError("chunk length differs across layers")
+        starts = [0]
+        for n in lens:
+            starts.append(starts[-1] + n)
+        hs = torch.tensor(starts, dtype=torch.int64).pin_memory()
+        self.kv_dim = kv_dim
+        self.S = starts[-1]
+        self.lengths = lens
+        self.srcs = host.to(device, non_blocking=True)
+        self.starts = hs.to(device, non_blocking=True)
+        self.dtype = self._keep[0].dtype
+
+    def layer_ptr(self, layer: int) -> int:
+        """Device address of the srcs row of one layer (n_chunks entries)."""
+        li = self.layers.index(layer)
+        return self.srcs.data_ptr() + li * self.n_chunks * 16
+
+
+def _chunk_rows(t: torch.Tensor, device) -> torch.Tensor:
+    if t.device != device:
+        raise RuntimeError(f"chunk tensor on {t.device}, model on {device}")
+    t2 = t.reshape(-1, t.shape[-1])
+    if not t2.is_contiguous() or t2.data_ptr() % 16:
+        t2 = t2.contiguous()
+    return t2
+
+
+# ---------------------------------------------------------------------------
+# (a)+(b) assemble, (b)+(d) fresh-row scatter
+# ---------------------------------------------------------------------------
+def assemble_kv(table: ChunkTable, layer_lo: int, layer_hi: int, n_kv_heads: int, head_dim: int,
+                rope: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor, mode: str = "ref",
+                positions: torch.Tensor | None = None, status=None) -> None:
+    """Fill k_out[l], v_out[l] (l in [layer_lo, layer_hi)) of [L][S][kv_dim]
+    buffers from the chunk tensors, K rotated to its fused positions."""
+    dev = require_cuda(k_out, v_out, rope)
+    n_layers = layer_hi - layer_lo
+    if n_layers <= 0:
+        return
+    li0 = table.layers.index(layer_lo)
+    if table.layers[li0:li0 + n_layers] != list(range(layer_lo, layer_hi)):
+        raise ValueError("chunk table does not hold the requested consecutive layers")
+    srcs = table.srcs.data_ptr() + li0 * table.n_chunks * 16
+    lstride = k_out.stride(0)
+    kb = k_out.data_ptr() + layer_lo * lstride * k_out.element_size()
+    vb = v_out.data_ptr() + layer_lo * lstride * v_out.element_size()
+    N.check(N.LIB.cbk_assemble_kv(_vp(srcs), _vp(table.starts), table.n_chunks, n_layers, table.S,
+                                  n_kv_heads, head_dim, dtype_code(k_out.dtype), _vp(rope),
+                                  rope.shape[0], _vp(positions), ROPE_MODES[mode], _vp(kb), _vp(vb),
+                                  lstride, _vp(status), _stream(dev)), "cbk_assemble_kv")
+
+
+def rope_scatter(q_src: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor, idx: torch.Tensor,
+                 gather: bool, S: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
+                 rope: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                 q_out: torch.Tensor | None = None, mode: str = "ref", status=None) -> torch.Tensor:
+    """RoPE of fresh Q (-> q_out, [n_sel][Hq*D]) and K at positions idx; K and V
+    rows written into the fused cache of one layer at rows idx."""
+    dev = require_cuda(q_src, k_src, v_src, idx, rope, k_cache, v_cache)
+    q2, k2, v2 = _rows(q_src, "q"), _rows(k_src, "k"), _rows(v_src, "v")
+    n_sel = idx.numel()
+    if q_out is None:
+        q_out = torch.empty((n_sel, n_q_heads * head_dim), dtype=q_src.dtype, device=dev)
+    N.check(N.LIB.cbk_rope_scatter(_vp(q2), q2.stride(0), _vp(k2), k2.stride(0), _vp(v2), v2.stride(0),
+                                   int(bool(gather)), _vp(idx), n_sel, int(S), n_q_heads, n_kv_heads,
+                                   head_dim, dtype_code(q_src.dtype), _vp(rope), rope.shape[0],
+                                   ROPE_MODES[mode], _vp(q_out), _vp(k_cache), _vp(v_cache),
+                                   _vp(status), _stream(dev)), "cbk_rope_scatter")
+    return q_out
+
+
+# ---------------------------------------------------------------------------
+# (c) HKVD
+# ---------------------------------------------------------------------------
+def kv_deviation_rows(k_new: torch.Tensor, table: ChunkTable, layer: int) -> torch.Tensor:
+    dev = require_cuda(k_new)
+    kn = _rows(k_new, "K_new")
+    out = torch.empty((table.S,), dtype=torch.float32, device=dev)
+    N.check(N.LIB.cbk_kv_deviation(_vp(kn), kn.stride(0), _vp(table.layer_ptr(layer)),
+                                   _vp(table.starts), table.n_chunks, table.S, kn.shape[1],
+                                   dtype_code(k_new.dtype), _vp(out), _stream(dev)),
+            "cbk_kv_deviation")
+    return out
+
+
+def topk_count(S: int, ratio: float) -> int:
+    return int(N.LIB.cbk_topk_count(int(S), float(ratio)))
+
+
+def topk_select(dev_scores: torch.Tensor, k: int, force_last: bool = False, status=None) -> torch.Tensor:
+    dev = require_cuda(dev_scores)
+    if dev_scores.dtype != torch.float32:
+        dev_scores = dev_scores.float()
+    d = dev_scores.contiguous()
+    idx = torch.empty((int(k),), dtype=torch.int64, device=dev)
+    N.check(N.LIB.cbk_topk_select(_vp(d), d.numel(), int(k), int(bool(force_last)), _vp(idx),
+                                  _vp(status), _stream(dev)), "cbk_topk_select")
+    return idx
+
+
+def hkvd_select(k_new: torch.Tensor, table: ChunkTable, layer: int, k: int, force_last: bool = True,
+                workspace: torch.Tensor | None = None, status=None):
+    """Deviation of fresh K against the cached chunk K of `layer`, then top-K.
+    Returns (indices, deviations) -- deviations live in the workspace."""
+    dev = require_cuda(k_new)
+    kn = _rows(k_new, "K_new")
+    S = table.S
+    need = int(N.LIB.cbk_hkvd_workspace_bytes(S))
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty((need // 4,), dtype=torch.float32, device=dev)
+    idx = torch.empty((int(k),), dtype=torch.int64, device=dev)
+    N.check(N.LIB.cbk_hkvd_select(_vp(kn), kn.stride(0), _vp(table.layer_ptr(layer)),
+                                  _vp(table.starts), table.n_chunks, S, kn.shape[1],
+                                  dtype_code(k_new.dtype), int(k), int(bool(force_last)), _vp(idx),
+                                  _vp(workspace), need, _vp(status), _stream(dev)),
+            "cbk_hkvd_select")
+    return idx, workspace.view(torch.float32)[:S]
+
+
+# ---------------------------------------------------------------------------
+# (e) partial attention
+# ---------------------------------------------------------------------------
+def partial_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor,
+                 n_q_heads: int, n_kv_heads: int, head_dim: int, scale: float,
+                 out: torch.Tensor | None = None, status=None) -> torch.Tensor:
+    """softmax(scale q k^T, keys <= pos) v for selected rows.
+
+    q: [n_sel][Hq*D] (rotated); k_cache/v_cache: [S][Hkv*D]; pos: int64 [n_sel]
+    ascending.  Returns [n_sel][Hq*D]."""
+    dev = require_cuda(q, k_cache, v_cache, pos)
+    n_sel = pos.numel()
+    S = k_cache.shape[0]
+    for t, name in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        if not t.is_contiguous():
+            raise ValueError(f"partial_attn: {name} must be contiguous")
+    if out is None:
+        out = torch.empty((n_sel, n_q_heads * head_dim), dtype=q.dtype, device=dev)
+    N.check(N.LIB.cbk_partial_attn(_vp(q), _vp(k_cache), _vp(v_cache), _vp(pos), n_sel, S,
+                                   n_q_heads, n_kv_heads, head_dim, float(scale),
+                                   dtype_code(q.dtype), _vp(out), _vp(status), _stream(dev)),
+            "cbk_partial_attn")
+    return out

@@ -1,0 +1,265 @@
+// HKVD: per-token K deviation and top-K selection with the force-include rule.
+//
+// Deviation order (reproduced bit-for-bit by the oracle):
+//   one warp per token; lane l owns the 16-byte vectors v = l, l+32, l+64, ...
+//   of the row (8 elements each).  acc_l = 0; for each owned vector in
+//   increasing v, for e = 0..7: acc_l = acc_l + (d_e * d_e), d_e = new - old,
+//   every operation a separately rounded fp32 op (no FMA).  Then a butterfly
+//   acc_l += acc_(l xor o) for o = 16, 8, 4, 2, 1; lane 0 writes the result.
+//
+// Top-K: one CTA.  Order keys are the fp32 bit patterns mapped to a monotone
+// unsigned order; four 8-bit radix passes find the k-th largest key T and how
+// many elements equal to T are taken (lowest index first).  A tiled,
+// order-preserving compaction then writes the ascending index list.
+#include "cbk_common.cuh"
+
+namespace cbk {
+
+constexpr int kDevThreads = 256;
+
+template <int DT>
+__global__ void __launch_bounds__(kDevThreads)
+deviation_kernel(const uint16_t* __restrict__ k_new, int64_t new_stride,
+                 const cbk_chunk_src* __restrict__ old_srcs, const int64_t* __restrict__ chunk_start,
+                 int n_chunks, int64_t S, int64_t feat, float* __restrict__ dev) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (static_cast<int64_t>(blockIdx.x) * kDevThreads + threadIdx.x) >> 5;
+  if (t >= S) return;
+  int lo = 0, hi = n_chunks - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (chunk_start[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  const uint16_t* a = k_new + t * new_stride;
+  const uint16_t* b = static_cast<const uint16_t*>(old_srcs[lo].k) + (t - chunk_start[lo]) * feat;
+  const int nvec = static_cast<int>(feat >> 3);
+  float acc = 0.f;
+  for (int v = lane; v < nvec; v += 32) {
+    const uint4 x = ld_vec(a + v * 8);
+    const uint4 y = ld_stream(b + v * 8);
+    const uint16_t* xs = reinterpret_cast<const uint16_t*>(&x);
+    const uint16_t* ys = reinterpret_cast<const uint16_t*>(&y);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float d = __fsub_rn(Elem<DT>::to_f(xs[e]), Elem<DT>::to_f(ys[e]));
+      acc = __fadd_rn(acc, __fmul_rn(d, d));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+  if (lane == 0) dev[t] = acc;
+}
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+constexpr int kTopkThreads = 1024;
+constexpr int kTopkWarps = kTopkThreads / 32;
+constexpr int64_t kTopkSmemKeys = 40960;   // keys cached in shared memory up to this S
+
+__global__ void __launch_bounds__(kTopkThreads, 1)
+topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
+            int64_t* __restrict__ idx, int32_t* status) {
+  extern __shared__ uint32_t s_keys[];   // S keys when S <= kTopkSmemKeys
+  __shared__ uint32_t s_hist[256];
+  __shared__ uint32_t s_wcount[kTopkWarps];
+  __shared__ uint32_t s_prefix, s_mask;
+  __shared__ int64_t s_krem, s_total_eq;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool cached = S <= kTopkSmemKeys;
+  if (cached)
+    for (int64_t i = tid; i < S; i += kTopkThreads) s_keys[i] = order_key(dev[i]);
+  if (tid == 0) { s_prefix = 0; s_mask = 0; s_krem = k; }
+  __syncthreads();
+
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int b = tid; b < 256; b += kTopkThreads) s_hist[b] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix, mask = s_mask;
+    for (int64_t i = tid; i < S; i += kTopkThreads) {
+      const uint32_t key = cached ? s_keys[i] : order_key(dev[i]);
+      if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l sums the 8 digits 255-8l .. 248-8l (descending digit order)
+      uint32_t c[8], sum = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) { c[e] = s_hist[255 - 8 * lane - e]; sum += c[e]; }
+      uint32_t incl = sum;   // inclusive scan over lanes: counts of digits >= this lane's lowest
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const uint32_t excl = incl - sum;
+      const int64_t krem = s_krem;
+      const bool here = (excl < krem) && (incl >= krem);
+      const unsigned who = __ballot_sync(0xffffffffu, here);
+      if (here && lane == __ffs(who) - 1) {
+        uint32_t above = excl;
+        for (int e = 0; e < 8; ++e) {
+          if (above + c[e] >= krem) {
+            const uint32_t digit = 255 - 8 * lane - e;
+            s_prefix = prefix | (digit << shift);
+            s_mask = mask | (255u << shift);
+            s_krem = krem - above;
+            s_total_eq = c[e];
+            break;
+          }
+          above += c[e];
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  const uint32_t T = s_prefix;
+  const int64_t k_eq = s_krem;          // elements equal to T that are taken
+  const int64_t total_eq = s_total_eq;  // elements equal to T in total
+  const uint32_t last_key = cached ? s_keys[S - 1] : order_key(dev[S - 1]);
+  const bool last_sel = last_key > T || (last_key == T && total_eq <= k_eq);
+  const bool force = force_last && !last_sel;
+
+  int64_t eq_seen = 0, out_base = 0;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int64_t base = 0; base < S; base += kTopkThreads) {
+    const int64_t i = base + tid;
+    const bool valid = i < S;
+    const uint32_t key = valid ? (cached ? s_keys[i] : order_key(dev[i])) : 0u;
+    const bool eq = valid && key == T;
+    const unsigned eq_bal = __ballot_sync(0xffffffffu, eq);
+    if (lane == 0) s_wcount[warp] = __popc(eq_bal);
+    __syncthreads();
+    uint32_t eq_before = 0, eq_tile = 0;
+    for (int w = 0; w < kTopkWarps; ++w) {
+      const uint32_t c = s_wcount[w];
+      if (w < warp) eq_before += c;
+      eq_tile += c;
+    }
+    const int64_t eq_rank = eq_seen + eq_before + __popc(eq_bal & lt_mask);
+    bool sel = valid && (key > T || (eq && eq_rank < k_eq && !(force && eq_rank == 0)));
+    if (force && i == S - 1) sel = true;
+    __syncthreads();
+    const unsigned sel_bal = __ballot_sync(0xffffffffu, sel);
+    if (lane == 0) s_wcount[warp] = __popc(sel_bal);
+    __syncthreads();
+    uint32_t sel_before = 0, sel_tile = 0;
+    for (int w = 0; w < kTopkWarps; ++w) {
+      const uint32_t c = s_wcount[w];
+      if (w < warp) sel_before += c;
+      sel_tile += c;
+    }
+    if (sel) {
+      const int64_t pos = out_base + sel_before + __popc(sel_bal & lt_mask);
+      if (pos < k) idx[pos] = i; else report(status, CBK_STATUS_COUNT);
+    }
+    eq_seen += eq_tile;
+    out_base += sel_tile;
+    __syncthreads();
+  }
+  if (tid == 0 && out_base != k) report(status, CBK_STATUS_COUNT);
+}
+
+int ensure_smem_attr(const void* func, int bytes);   // cbk_api.cu
+
+static size_t topk_smem_bytes(int64_t S) {
+  return S <= kTopkSmemKeys ? static_cast<size_t>(S) * sizeof(uint32_t) : 0;
+}
+
+static int launch_topk(const float* dev, int64_t S, int64_t k, int force_last, int64_t* idx,
+                       int32_t* status, cudaStream_t st) {
+  if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(topk_kernel),
+                                static_cast<int>(kTopkSmemKeys * sizeof(uint32_t))))
+    return rc;
+  topk_kernel<<<1, kTopkThreads, topk_smem_bytes(S), st>>>(dev, S, k, force_last, idx, status);
+  return check_launch("topk_kernel");
+}
+
+static int launch_deviation(const void* k_new, int64_t new_stride, const cbk_chunk_src* old_srcs,
+                            const int64_t* chunk_start, int n_chunks, int64_t S, int64_t feat,
+                            int dtype, float* dev, cudaStream_t st) {
+  const int64_t blocks = (S * 32 + kDevThreads - 1) / kDevThreads;
+  if (dtype == CBK_BF16)
+    deviation_kernel<CBK_BF16><<<static_cast<unsigned>(blocks), kDevThreads, 0, st>>>(
+        static_cast<const uint16_t*>(k_new), new_stride, old_srcs, chunk_start, n_chunks, S, feat, dev);
+  else
+    deviation_kernel<CBK_F16><<<static_cast<unsigned>(blocks), kDevThreads, 0, st>>>(
+        static_cast<const uint16_t*>(k_new), new_stride, old_srcs, chunk_start, n_chunks, S, feat, dev);
+  return check_launch("deviation_kernel");
+}
+
+static int check_dev_args(const char* fn, const void* k_new, int64_t new_stride,
+                          const cbk_chunk_src* old_srcs, const int64_t* chunk_start, int n_chunks,
+                          int64_t S, int64_t feat, int dtype) {
+  if (dtype != CBK_BF16 && dtype != CBK_F16)
+    return set_error(CBK_ERR_UNSUPPORTED, "%s: dtype %d not supported (bf16/fp16 only)", fn, dtype);
+  if (!k_new || !old_srcs || !chunk_start)
+    return set_error(CBK_ERR_INVALID, "%s: null pointer argument", fn);
+  if (S <= 0 || n_chunks <= 0 || feat <= 0 || feat % 8 != 0 || new_stride < feat || new_stride % 8)
+    return set_error(CBK_ERR_INVALID, "%s: bad sizes (S %lld, chunks %d, feat %lld, stride %lld)",
+                     fn, (long long)S, n_chunks, (long long)feat, (long long)new_stride);
+  if (reinterpret_cast<uintptr_t>(k_new) & 15u)
+    return set_error(CBK_ERR_INVALID, "%s: K_new must be 16-byte aligned", fn);
+  return CBK_OK;
+}
+
+}  // namespace cbk
+
+using namespace cbk;
+
+extern "C" int cbk_kv_deviation(const void* k_new, int64_t new_row_stride,
+                                const cbk_chunk_src* old_srcs, const int64_t* chunk_start,
+                                int n_chunks, int64_t S, int64_t feat, int dtype, float* dev,
+                                void* stream) {
+  if (int rc = check_dev_args("cbk_kv_deviation", k_new, new_row_stride, old_srcs, chunk_start,
+                              n_chunks, S, feat, dtype))
+    return rc;
+  if (!dev) return set_error(CBK_ERR_INVALID, "cbk_kv_deviation: null output");
+  return launch_deviation(k_new, new_row_stride, old_srcs, chunk_start, n_chunks, S, feat, dtype,
+                          dev, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t cbk_topk_count(int64_t S, double ratio) {
+  int64_t k = static_cast<int64_t>(static_cast<double>(S) * ratio);   // truncation, like int()
+  if (k < 1) k = 1;
+  if (k > S) k = S;
+  return k;
+}
+
+extern "C" int cbk_topk_select(const float* dev, int64_t S, int64_t k, int force_last,
+                               int64_t* idx, int32_t* status, void* stream) {
+  if (!dev || !idx) return set_error(CBK_ERR_INVALID, "cbk_topk_select: null pointer argument");
+  if (S <= 0 || k <= 0 || k > S)
+    return set_error(CBK_ERR_INVALID, "cbk_topk_select: need 0 < k <= S (k %lld, S %lld)",
+                     (long long)k, (long long)S);
+  return launch_topk(dev, S, k, force_last, idx, status, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t cbk_hkvd_workspace_bytes(int64_t S) {
+  return S <= 0 ? 0 : ((static_cast<size_t>(S) * sizeof(float) + 255) / 256) * 256;
+}
+
+extern "C" int cbk_hkvd_select(const void* k_new, int64_t new_row_stride,
+                               const cbk_chunk_src* old_srcs, const int64_t* chunk_start,
+                               int n_chunks, int64_t S, int64_t feat, int dtype, int64_t k,
+                               int force_last, int64_t* idx, void* workspace,
+                               size_t workspace_bytes, int32_t* status, void* stream) {
+  if (int rc = check_dev_args("cbk_hkvd_select", k_new, new_row_stride, old_srcs, chunk_start,
+                              n_chunks, S, feat, dtype))
+    return rc;
+  if (!idx || !workspace) return set_error(CBK_ERR_INVALID, "cbk_hkvd_select: null output/workspace");
+  if (k <= 0 || k > S) return set_error(CBK_ERR_INVALID, "cbk_hkvd_select: need 0 < k <= S");
+  if (workspace_bytes < cbk_hkvd_workspace_bytes(S))
+    return set_error(CBK_ERR_WORKSPACE, "cbk_hkvd_select: workspace %zu < %zu bytes", workspace_bytes,
+                     cbk_hkvd_workspace_bytes(S));
+  auto st = static_cast<cudaStream_t>(stream);
+  float* dev = static_cast<float*>(workspace);
+  if (int rc = launch_deviation(k_new, new_row_stride, old_srcs, chunk_start, n_chunks, S, feat,
+                                dtype, dev, st))
+    return rc;
+  return launch_topk(dev, S, k, force_last, idx, status, st);
+}

@@ -1,0 +1,162 @@
+/*
+ * cbk.h -- C ABI of libcbk, the sm_100a kernels behind CacheBlend's
+ * selective-KV-recompute path.
+ *
+ * All tensor arguments are DEVICE pointers on the current CUDA device; every
+ * call is asynchronous on `stream` (a cudaStream_t / CUstream handle) and never
+ * synchronises the host.  Nothing here allocates device memory: buffers,
+ * descriptor tables and workspaces are owned by the caller.  Calls are
+ * re-entrant (no mutable global state other than the per-thread error text).
+ *
+ * Return value: CBK_OK (0) or a negative CBK_ERR_* code; cbk_last_error()
+ * returns a message for the most recent failure on the calling thread.
+ * Errors that can only be seen on the device (an index outside the fused
+ * sequence, a bounded wait that gave up) are OR-ed into the optional
+ * `status` word (device int32, may be NULL) as CBK_STATUS_* bits; the kernel
+ * skips the offending access instead of faulting.
+ *
+ * Element types: CBK_BF16 or CBK_F16 for every K/V/Q tensor of one call.
+ * Layouts follow the reference's memory layout:
+ *   - a chunk's cached K (pre-RoPE) and V for one layer: [len][kv_dim] row-major,
+ *     kv_dim = n_kv_heads * head_dim (cacheblend/kv_store.py:7-9, one
+ *     `(1, Lc, Hkv*D)` tensor per chunk per layer);
+ *   - the fused cache of one layer: [S][n_kv_heads][head_dim] (token-major),
+ *     which is the memory order of the reference's DynamicCache tensors
+ *     (fusor.py:439-460 builds them as transposed views of `(1, S, Hkv*D)`);
+ *   - selected queries: [n_sel][n_q_heads][head_dim]; attention output:
+ *     [n_sel][n_q_heads * head_dim] (the o_proj input of fusor.py:471-474).
+ */
+#ifndef CBK_H_
+#define CBK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CBK_ABI_VERSION 1
+
+enum {
+  CBK_OK = 0,
+  CBK_ERR_INVALID = -1,      /* bad argument: NULL, size, stride or alignment */
+  CBK_ERR_UNSUPPORTED = -2,  /* dtype / head_dim / GQA group not supported */
+  CBK_ERR_CUDA = -3,         /* CUDA runtime or launch error */
+  CBK_ERR_WORKSPACE = -4     /* caller workspace too small */
+};
+
+enum { CBK_BF16 = 0, CBK_F16 = 1 };
+
+/* RoPE rounding modes for K/Q rotation.
+ * CBK_ROPE_REF:  reproduce HF `apply_rotary_pos_emb` on 16-bit tensors: cos/sin
+ *                rounded to the element type, each product rounded, the sum
+ *                rounded (modeling_mistral.py rotate_half / apply_rotary_pos_emb,
+ *                MistralRotaryEmbedding.forward casts cos/sin to x.dtype).
+ * CBK_ROPE_FP32: rotate in fp32 with one final rounding (more accurate). */
+enum { CBK_ROPE_REF = 0, CBK_ROPE_FP32 = 1 };
+
+/* Device status bits (OR-ed into *status). */
+enum {
+  CBK_STATUS_BAD_INDEX = 1,     /* a position / row index outside its buffer; access skipped */
+  CBK_STATUS_TIMEOUT = 2,       /* a bounded wait inside a kernel gave up */
+  CBK_STATUS_COUNT = 4          /* top-K count check failed */
+};
+
+/* One chunk's cached tensors for one layer (device pointers, row-major
+ * [len][kv_dim], rows contiguous). */
+typedef struct {
+  const void* k;
+  const void* v;
+} cbk_chunk_src;
+
+const char* cbk_last_error(void);
+int cbk_abi_version(void);
+
+/* RoPE table: table[p * half_dim + i] = (cos, sin)(inv_freq[i] * p) * attention_scaling,
+ * fp32, for p in [0, n_pos).  inv_freq is the model's own buffer (device, fp32).
+ * Replaces the per-call `rotary_emb(x, position_ids)` of fusor.py:285 and
+ * rope.py:54 (MistralRotaryEmbedding.forward, angle = fp32(inv_freq) * fp32(pos)). */
+int cbk_rope_table(const float* inv_freq, int half_dim, int64_t n_pos,
+                   float attention_scaling, void* table /* float2[n_pos][half_dim] */,
+                   void* stream);
+
+/* (a)+(b) chunk-KV concatenation with RoPE shift, all layers in one launch.
+ * For every layer l < n_layers and fused row t in [0, S): find chunk c with
+ * chunk_start[c] <= t < chunk_start[c+1]; then
+ *   k_out[l][t] = RoPE(srcs[l*n_chunks+c].k[t - chunk_start[c]], pos(t))
+ *   v_out[l][t] = srcs[l*n_chunks+c].v[t - chunk_start[c]]
+ * with pos(t) = positions ? positions[t] : t.  Output rows have kv_dim
+ * elements; layer l starts at element l * out_layer_stride.
+ * Replaces fusor.py:258-272 (zeros + per-chunk slice copies) together with the
+ * cached-K rotation of fusor.py:439-447 (rope.py:33-64 applied to the concat). */
+int cbk_assemble_kv(const cbk_chunk_src* srcs, const int64_t* chunk_start, int n_chunks,
+                    int n_layers, int64_t S, int n_kv_heads, int head_dim, int dtype,
+                    const void* rope_table, int64_t table_rows, const int64_t* positions,
+                    int rope_mode, void* k_out, void* v_out, int64_t out_layer_stride,
+                    int32_t* status, void* stream);
+
+/* apply_rope_shift (rope.py:33-64) on plain rows: out[r] = RoPE(in[r], positions[r])
+ * for r < n_rows, rows of n_heads*head_dim elements (in/out may alias). */
+int cbk_rope_rows(const void* in, void* out, int64_t n_rows, int n_heads, int head_dim,
+                  int dtype, const void* rope_table, int64_t table_rows,
+                  const int64_t* positions, int rope_mode, int32_t* status, void* stream);
+
+/* (b)+(d) fresh rows of one layer.  For j < n_sel, with src row
+ * r = gather ? idx[j] : j and position p = idx[j]:
+ *   q_out[j]      = RoPE(q_src[r], p)              [n_sel][n_q_heads*head_dim]
+ *   k_cache[p]    = RoPE(k_src[r], p)              fused [S][kv_dim]
+ *   v_cache[p]    = v_src[r]
+ * Row strides are in elements.  Replaces fusor.py:355-361 + 370-376 (check
+ * layer: mixed K, RoPE of Q and K, Q sliced to the selection) and
+ * fusor.py:432-458 (sparse layers: RoPE of sparse Q/K, clone + index_put of K/V). */
+int cbk_rope_scatter(const void* q_src, int64_t q_row_stride, const void* k_src,
+                     int64_t k_row_stride, const void* v_src, int64_t v_row_stride,
+                     int gather, const int64_t* idx, int64_t n_sel, int64_t S,
+                     int n_q_heads, int n_kv_heads, int head_dim, int dtype,
+                     const void* rope_table, int64_t table_rows, int rope_mode,
+                     void* q_out, void* k_cache, void* v_cache, int32_t* status, void* stream);
+
+/* (c) HKVD deviation (hkvd.py:23-55, kv_deviation):
+ *   dev[t] = sum_f (K_new[t][f] - K_old[t][f])^2 in fp32, fixed order
+ * (see the kernel for the exact order).  K_new rows have stride new_row_stride
+ * elements; K_old rows come from the chunk table (srcs[c].k, c < n_chunks,
+ * rows chunk_start[c] .. chunk_start[c+1]). */
+int cbk_kv_deviation(const void* k_new, int64_t new_row_stride, const cbk_chunk_src* old_srcs,
+                     const int64_t* chunk_start, int n_chunks, int64_t S, int64_t feat,
+                     int dtype, float* dev, void* stream);
+
+/* k selected count of select_top_k (hkvd.py:70-73): max(1, min(S, (int64)(S * ratio))). */
+int64_t cbk_topk_count(int64_t S, double ratio);
+
+/* (c) top-K select (hkvd.py:58-77) + optional force-include of S-1 (fusor.py:344-353).
+ * idx[0..k) = the k largest dev values' indices, ascending.  Ties at the k-th
+ * value are taken lowest index first.  With force_last != 0 and S-1 not
+ * selected, the lowest-index selected element equal to the k-th value (the
+ * reference's argmin pick) is dropped and S-1 appended.  One CTA, no workspace. */
+int cbk_topk_select(const float* dev, int64_t S, int64_t k, int force_last, int64_t* idx,
+                    int32_t* status, void* stream);
+
+/* (c) deviation + select in one call.  `workspace` (device, >= cbk_hkvd_workspace_bytes(S))
+ * receives dev[S] (readable afterwards as float[S]). */
+size_t cbk_hkvd_workspace_bytes(int64_t S);
+int cbk_hkvd_select(const void* k_new, int64_t new_row_stride, const cbk_chunk_src* old_srcs,
+                    const int64_t* chunk_start, int n_chunks, int64_t S, int64_t feat, int dtype,
+                    int64_t k, int force_last, int64_t* idx, void* workspace, size_t workspace_bytes,
+                    int32_t* status, void* stream);
+
+/* (e) partial-query attention on tcgen05 (fusor.py:381-399, 462-474):
+ *   out[j][h] = softmax_t<=pos[j]( scale * q[j][h] . k[t][h/G] ) . v[t][h/G]
+ * for j < n_sel, h < n_q_heads, G = n_q_heads / n_kv_heads, keys t in [0, pos[j]].
+ * q: [n_sel][n_q_heads][head_dim]; k/v: [S][n_kv_heads][head_dim]; pos ascending
+ * (int64), each in [0, S).  head_dim 64 or 128; G in {1,2,4,8,16}.
+ * fp32 accumulation in TMEM, fp32 online softmax, 16-bit P and output. */
+int cbk_partial_attn(const void* q, const void* k, const void* v, const int64_t* pos,
+                     int64_t n_sel, int64_t S, int n_q_heads, int n_kv_heads, int head_dim,
+                     float scale, int dtype, void* out, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CBK_H_ */
