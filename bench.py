@@ -1,0 +1,447 @@
+"""Blended-prefill benchmark: CacheBlend selective recompute at Mistral-7B shape.
+
+Workload (one step = one blended prefill of one request, per GPU): Mistral-7B
+architecture with random-init bf16 weights (32 layers, hidden 4096, 32 q / 8 KV
+heads, head_dim 128, rope_theta 1e6, vocab 32000); prompt = 6 chunks x 1024
+uniform-random token ids + a 64-token query chunk (S = 6208); chunk K/V
+precomputed per chunk (untimed, like the reference's collect phase);
+recompute ratio 0.15 (k = 931), check layer 1.  Synthetic ids stand in for the
+reference's musique passages (about 6-7K tokens per prompt).
+
+  value   fused prompt tokens / s over all ranks, device-timed (CUDA events)
+          over K steps of ``fuse_selective`` + argmax of the last position,
+          inputs resident in HBM
+  e2e     the same through the public API with the token ids copied from
+          pinned host memory and the first decoded token read back each step
+  roofline  the dominant libcbk kernel (partial attention): algorithmic FLOPs
+          of its launches / their CUDA-event time inside the timed region
+
+Multi-GPU: one process per GPU (torchrun), each rank runs its own requests
+(independent units, no data-path collective); the step time is the max over
+ranks.  ``--impl reference`` times the reference's algorithm on the host CPU
+(the oracle restatement) for the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "cacheblend-hf-v7_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "blended-prefill TTFT (ms) & tokens/s at Mistral-7B 7K ctx; KV-kernel HBM GB/s"
+MISTRAL_7B = dict(vocab_size=32000, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                  num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
+                  rms_norm_eps=1e-5, max_position_embeddings=32768, sliding_window=None)
+N_CHUNKS, CHUNK_LEN, QUERY_LEN, RATIO, CHECK_LAYER = 6, 1024, 64, 0.15, 1
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p["bf16_tflops_sustained"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler
+# ---------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except Exception:
+            self.p.kill()
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def build_request(model, cb, seed, device):
+    import torch
+    gen = torch.Generator().manual_seed(seed)
+    lens = [CHUNK_LEN] * N_CHUNKS + [QUERY_LEN]
+    ids = [torch.randint(0, MISTRAL_7B["vocab_size"], (n,), generator=gen).tolist() for n in lens]
+    chunks = [cb.Chunk(text=f"r{seed}c{i}", token_ids=t, chunk_id=cb.chunker._stable_id(f"r{seed}c{i}", t))
+              for i, t in enumerate(ids)]
+    return chunks
+
+
+def build_model(device):
+    import torch
+    from transformers import MistralConfig, MistralForCausalLM
+    cfg = MistralConfig(**MISTRAL_7B)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = MistralForCausalLM(cfg).to(torch.bfloat16)
+    return model.eval()
+
+
+def attn_flops(idx_list, S, Hq, D, ck, n_layers):
+    """Algorithmic FLOPs of the partial-attention launches of one step:
+    4 * Hq * D * sum(pos + 1) per layer (QK^T and PV over the causal prefix)."""
+    sel = sum(int(p) + 1 for p in idx_list)
+    dense = S * (S + 1) // 2
+    return 4 * Hq * D * (dense * ck + sel * (n_layers - ck))
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import cacheblend as cb
+    from cacheblend._timing import TIMES
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    model = build_model(device)
+    lw = cb.LayerwiseModel.from_hf(model)
+    store = cb.KVStore()
+    reqs = [build_request(model, cb, seed=1000 * rank + r, device=device) for r in range(args.requests)]
+    for chunks in reqs:
+        for c in chunks:
+            K, V = cb.precompute_chunk_kv(lw, c)
+            store.put(c.chunk_id, K, V)
+    S = sum(c.length for c in reqs[0])
+    stream = torch.cuda.current_stream(device)
+
+    dev_ids = [torch.tensor([t for c in chunks for t in c.token_ids], dtype=torch.int64, device=device)
+               for chunks in reqs]
+
+    def step(i):
+        chunks = reqs[i % len(reqs)]
+        logits = cb.fuse_selective(lw, chunks, store, recompute_ratio=RATIO, check_layer=CHECK_LAYER,
+                                   input_ids=dev_ids[i % len(reqs)])
+        return logits[0, -1].argmax()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # --- device-timed region --------------------------------------------------
+    clocks = Clocks(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    TIMES.reset()
+    TIMES.active = True
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
+    t0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    t1.record(stream)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    TIMES.active = False
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1))
+    kern = TIMES.summary()
+
+    # --- end to end through the public API (host ids in, first token out) -----
+    pinned = [torch.tensor([t for c in chunks for t in c.token_ids], dtype=torch.int64).pin_memory()
+              for chunks in reqs]
+    e2e_ms = []
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        chunks = reqs[i % len(reqs)]
+        a = time.perf_counter()
+        logits = cb.fuse_selective(lw, chunks, store, recompute_ratio=RATIO, check_layer=CHECK_LAYER,
+                                   input_ids=pinned[i % len(reqs)])         # H2D of this step's ids
+        int(logits[0, -1].argmax().item())                                   # first token to host
+        e2e_ms.append((time.perf_counter() - a) * 1e3)
+    barrier()
+    e2e_step = max_over_ranks(sum(e2e_ms) / len(e2e_ms))
+
+    # --- kernel accounting -----------------------------------------------------
+    _, idx = cb.fuse_selective(lw, reqs[0], store, recompute_ratio=RATIO, check_layer=CHECK_LAYER,
+                               return_hkvd_indices=True)
+    idx_l = idx.cpu().tolist()
+    cfg = model.config
+    D, Hq, Hkv, L = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.num_hidden_layers
+    kv_dim = Hkv * D
+    hbm_peak, tf_burst, tf_sust, peak_src = load_peaks()
+    n_attn, attn_ms = kern.get("partial_attn", (0, 0.0))
+    flops_step = attn_flops(idx_l, S, Hq, D, CHECK_LAYER, L)
+    per_launch_flops = flops_step / L
+    attn_avg_ms = attn_ms / max(n_attn, 1)
+    achieved_tf = per_launch_flops / (attn_avg_ms * 1e-3) / 1e12 if n_attn else None
+    n_asm, asm_ms = kern.get("assemble_kv", (0, 0.0))
+    asm_bytes = (L - CHECK_LAYER) * 2 * 2 * S * kv_dim * 2        # read chunk K/V + write fused K/V
+    n_hk, hk_ms = kern.get("hkvd_select", (0, 0.0))
+    hk_bytes = 2 * S * kv_dim * 2 + S * 4
+    n_sc, sc_ms = kern.get("rope_scatter", (0, 0.0))
+    k_sel = len(idx_l)
+    sc_bytes_sparse = k_sel * (cfg.hidden_size + 2 * kv_dim) * 2 * 2
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "partial_attn_traffic.json")
+    if os.path.exists(prof):
+        try:
+            traffic = json.load(open(prof)).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    launches = sum(n for n, _ in kern.values())
+    res = {
+        "metric": METRIC,
+        "value": round(world * S * args.steps / (ms * 1e-3), 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3),
+        "ttft_ms": round(ms / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (uniform-random token ids; random-init weights)",
+        "config": {"workload": "mistral7b-7k-blend", "model": "Mistral-7B architecture, random init",
+                   "chunks": f"{N_CHUNKS}x{CHUNK_LEN}+{QUERY_LEN}", "S": S, "recompute_ratio": RATIO,
+                   "k_selected": k_sel, "check_layer": CHECK_LAYER, "global_batch": world,
+                   "requests_per_rank": args.requests, "parallelism": f"by-request x{world}",
+                   "l2": "inputs larger than L2 (14.5 GB weights, 0.81 GB fused KV per step)"},
+        "e2e": {"value": round(world * S / (e2e_step * 1e-3), 1), "unit": "tokens/s",
+                "ttft_ms": round(e2e_step, 3), "h2d_bytes_per_step": S * 8, "d2h_bytes_per_step": 8},
+        "roofline": {"kernel": "partial_attn_kernel", "bound": "tensor",
+                     "achieved": round(achieved_tf, 1) if achieved_tf else None,
+                     "peak": tf_sust, "unit": "TFLOP/s",
+                     "frac": round(achieved_tf / tf_sust, 4) if achieved_tf else None,
+                     "peak_kind": f"{peak_src} bf16 sustained (kernel timed inside a long step)",
+                     "flops_per_launch": per_launch_flops, "launches": n_attn,
+                     "avg_launch_ms": round(attn_avg_ms, 5), "traffic": traffic},
+        "kernels": {
+            "assemble_kv": {"launches": n_asm, "avg_ms": round(asm_ms / max(n_asm, 1), 4),
+                            "bytes": asm_bytes,
+                            "GB/s": round(asm_bytes / (asm_ms / max(n_asm, 1) * 1e-3) / 1e9, 1) if n_asm else None,
+                            "frac_hbm": round(asm_bytes / (asm_ms / max(n_asm, 1) * 1e-3) / 1e9 / hbm_peak, 3) if n_asm else None},
+            "hkvd_select": {"launches": n_hk, "avg_ms": round(hk_ms / max(n_hk / 2, 1), 4), "bytes": hk_bytes,
+                            "GB/s": round(hk_bytes / (hk_ms / max(n_hk / 2, 1) * 1e-3) / 1e9, 1) if n_hk else None},
+            "rope_scatter": {"launches": n_sc, "avg_ms": round(sc_ms / max(n_sc, 1), 4),
+                             "bytes_sparse_layer": sc_bytes_sparse},
+            "partial_attn": {"launches": n_attn, "avg_ms": round(attn_avg_ms, 4),
+                             "TFLOP/s": round(achieved_tf, 1) if achieved_tf else None},
+            "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_src,
+        },
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(model, lw, store, reqs[0], budget_s=args.cpu_budget)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle restatement of fuse_selective
+# ---------------------------------------------------------------------------
+class OracleTTFT:
+    """CPU TTFT of the reference's algorithm (the oracle, numpy fp32) on a layer
+    sample: the fixed part (concat, layers < check layer, check layer with HKVD,
+    final norm + lm_head) is timed once; each sample() times one sparse layer;
+    TTFT = fixed + sparse * (n_layers - check_layer - 1)."""
+
+    def __init__(self, W, ids, ck_k, ck_v, n_layers_full):
+        from oracle import model as om
+        self.om, self.W, self.full = om, W, n_layers_full
+        t = time.perf_counter()
+        self.state = om.selective_begin(ids, ck_k, ck_v, W, RATIO, CHECK_LAYER, n_layers=CHECK_LAYER + 2)
+        hs = self.state.hs
+        om.selective_end(self.state, W)
+        self.t_fixed = time.perf_counter() - t
+        self.hs0 = hs
+
+    def sample(self):
+        self.state.hs = self.hs0
+        t = time.perf_counter()
+        self.om.selective_layer(self.state, CHECK_LAYER + 1, self.W, keep_cache=False)
+        t_sparse = time.perf_counter() - t
+        return self.t_fixed + t_sparse * (self.full - CHECK_LAYER - 1), t_sparse
+
+
+def _oracle_weights_from_model(model, n_layers):
+    from oracle import model as om
+    cfg = om.Config.from_hf(model.config)
+    sd = {}
+    for n, t in model.state_dict().items():
+        if n.startswith("model.layers."):
+            if int(n.split(".")[2]) >= n_layers:
+                continue
+        sd[n] = t.float().cpu().numpy()
+    cfg.num_hidden_layers = n_layers
+    return om.Weights(sd, cfg, model.model.rotary_emb.inv_freq.float().cpu().numpy())
+
+
+def cpu_baseline(model, lw, store, chunks, budget_s=30.0):
+    import numpy as np
+    nl = CHECK_LAYER + 2
+    W = _oracle_weights_from_model(model, nl)
+    ids = [np.asarray(c.token_ids) for c in chunks]
+    ents = [store.get(c.chunk_id) for c in chunks]
+    ck_k = [[e["K"][l][0].float().cpu().numpy() for l in range(nl)] for e in ents]
+    ck_v = [[e["V"][l][0].float().cpu().numpy() for l in range(nl)] for e in ents]
+    S = sum(len(x) for x in ids)
+    o = OracleTTFT(W, ids, ck_k, ck_v, model.config.num_hidden_layers)
+    ttft, t_sparse = o.sample()
+    return {"value": round(S / ttft, 2), "unit": "tokens/s", "ttft_s": round(ttft, 3),
+            "cores": _blas_threads(), "kind": "port",
+            "sample": (f"oracle fuse_selective (numpy fp32) on the same request: fixed part (concat, "
+                       f"layer 0, check layer + HKVD, lm_head) {o.t_fixed:.2f} s once, one sparse "
+                       f"layer {t_sparse:.2f} s, TTFT extrapolated to {model.config.num_hidden_layers} layers")}
+
+
+def _blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    """Reference arm: the reference's algorithm (oracle restatement, numpy on the
+    host cores) on the same workload; each step is one layer-sampled blended
+    prefill with the TTFT extrapolated to 32 layers."""
+    import numpy as np
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from oracle import model as om
+    rng = np.random.default_rng(0)
+    c = MISTRAL_7B
+    nl = CHECK_LAYER + 2
+    cfg = om.Config(c["vocab_size"], c["hidden_size"], c["intermediate_size"], nl,
+                    c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"], c["rope_theta"],
+                    c["rms_norm_eps"])
+    H, I, kvd = c["hidden_size"], c["intermediate_size"], c["num_key_value_heads"] * c["head_dim"]
+
+    def w(*shape):
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02))
+    sd = {"model.embed_tokens.weight": w(c["vocab_size"], H), "lm_head.weight": w(c["vocab_size"], H),
+          "model.norm.weight": np.ones(H, np.float32)}
+    for l in range(nl):
+        p = f"model.layers.{l}."
+        sd.update({p + "self_attn.q_proj.weight": w(H, H), p + "self_attn.k_proj.weight": w(kvd, H),
+                   p + "self_attn.v_proj.weight": w(kvd, H), p + "self_attn.o_proj.weight": w(H, H),
+                   p + "mlp.gate_proj.weight": w(I, H), p + "mlp.up_proj.weight": w(I, H),
+                   p + "mlp.down_proj.weight": w(H, I), p + "input_layernorm.weight": np.ones(H, np.float32),
+                   p + "post_attention_layernorm.weight": np.ones(H, np.float32)})
+    W = om.Weights(sd, cfg)
+    lens = [CHUNK_LEN] * N_CHUNKS + [QUERY_LEN]
+    ids = [rng.integers(0, c["vocab_size"], n) for n in lens]
+    ck_k = [[rng.standard_normal((n, kvd), dtype=np.float32) for _ in range(nl)] for n in lens]
+    ck_v = [[rng.standard_normal((n, kvd), dtype=np.float32) for _ in range(nl)] for n in lens]
+    S = sum(lens)
+    o = OracleTTFT(W, ids, ck_k, ck_v, c["num_hidden_layers"])
+    for _ in range(args.warmup):
+        o.sample()
+    ttfts = [o.sample()[0] for _ in range(args.steps)]
+    ttft = sum(ttfts) / len(ttfts)
+    value = round(S / ttft, 2)
+    cores = _blas_threads()
+    sample = (f"oracle fuse_selective (numpy fp32, BLAS {cores} threads): fixed part (concat, layer 0, "
+              f"check layer + HKVD, lm_head) timed once ({o.t_fixed:.2f} s); each step times one sparse "
+              f"layer; TTFT = fixed + 30 x sparse")
+    print(json.dumps({
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ttft * 1e3, 1), "ttft_ms": round(ttft * 1e3, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "mistral7b-7k-blend", "S": S, "recompute_ratio": RATIO,
+                   "check_layer": CHECK_LAYER, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--requests", type=int, default=1, help="distinct requests per rank (cycled)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=30.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -143,7 +143,8 @@ def _mlp_block(layer, h):
 def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
                    recompute_ratio: float = 0.15, check_layer: int = 1,
                    return_layerwise_output: bool = False, return_hkvd_indices: bool = False,
-                   rope_mode: str = "ref", status: torch.Tensor | None = None):
+                   rope_mode: str = "ref", status: torch.Tensor | None = None,
+                   input_ids: torch.Tensor | None = None):
     """CacheBlend selective recompute (reference fusor.py:193-497).
 
     Layers < check_layer: full forward.  Check layer: HKVD picks the
@@ -156,7 +157,8 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
 
     ``rope_mode`` "ref" reproduces HF's 16-bit RoPE rounding, "fp32" rotates in
     fp32 with one rounding.  ``status`` (int32 CUDA tensor) collects device-side
-    error bits."""
+    error bits.  ``input_ids`` (1-D or (1, S) int64, host -- preferably pinned --
+    or device) replaces the ids gathered from ``chunks``."""
     if recompute_ratio == 0:
         return fuse_full_reuse(layerwise_model, chunks, kv_store, return_layerwise_output)
     if recompute_ratio >= 1:
@@ -202,7 +204,12 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
         fused_k.record_stream(side)
         fused_v.record_stream(side)
 
-        ids = fused_input_ids(chunks, device=device)
+        if input_ids is None:
+            ids = fused_input_ids(chunks, device=device)
+        else:
+            ids = input_ids.reshape(1, -1).to(device, non_blocking=True)
+            if ids.shape[1] != S:
+                raise ValueError(f"input_ids has {ids.shape[1]} tokens, chunks have {S}")
         lw._pre_rope_k = {}
         pos_all = torch.arange(S, device=device, dtype=torch.int64)
         h = inner.embed_tokens(ids)

@@ -13,6 +13,7 @@ from typing import Sequence
 import torch
 
 from cacheblend import _native as N
+from cacheblend._timing import TIMES
 
 _DT = {torch.bfloat16: N.CBK_BF16, torch.float16: N.CBK_F16}
 ROPE_MODES = {"ref": N.CBK_ROPE_REF, "fp32": N.CBK_ROPE_FP32}
@@ -66,7 +67,8 @@ def rope_table(inv_freq: torch.Tensor, n_pos: int, scaling: float = 1.0) -> torc
     inv = inv_freq.to(device=dev, dtype=torch.float32).contiguous()
     half = inv.numel()
     table = torch.empty((int(n_pos), half, 2), dtype=torch.float32, device=dev)
-    N.check(N.LIB.cbk_rope_table(_vp(inv), half, int(n_pos), float(scaling), _vp(table), _stream(dev)),
+    with TIMES.span("rope_table", dev):
+      N.check(N.LIB.cbk_rope_table(_vp(inv), half, int(n_pos), float(scaling), _vp(table), _stream(dev)),
             "cbk_rope_table")
     return table
 
@@ -84,7 +86,8 @@ def rope_rows(x: torch.Tensor, positions: torch.Tensor, table: torch.Tensor, hea
     n_heads = xr.shape[1] // head_dim
     if n_heads * head_dim != xr.shape[1]:
         raise ValueError(f"row width {xr.shape[1]} is not a multiple of head_dim {head_dim}")
-    N.check(N.LIB.cbk_rope_rows(_vp(xr), _vp(out), xr.shape[0], n_heads, head_dim,
+    with TIMES.span("rope_rows", dev):
+      N.check(N.LIB.cbk_rope_rows(_vp(xr), _vp(out), xr.shape[0], n_heads, head_dim,
                                 dtype_code(x.dtype), _vp(table), table.shape[0], _vp(pos),
                                 ROPE_MODES[mode], _vp(status), _stream(dev)), "cbk_rope_rows")
     return out.view(x.shape)
@@ -169,7 +172,8 @@ def assemble_kv(table: ChunkTable, layer_lo: int, layer_hi: int, n_kv_heads: int
     lstride = k_out.stride(0)
     kb = k_out.data_ptr() + layer_lo * lstride * k_out.element_size()
     vb = v_out.data_ptr() + layer_lo * lstride * v_out.element_size()
-    N.check(N.LIB.cbk_assemble_kv(_vp(srcs), _vp(table.starts), table.n_chunks, n_layers, table.S,
+    with TIMES.span("assemble_kv", dev):
+      N.check(N.LIB.cbk_assemble_kv(_vp(srcs), _vp(table.starts), table.n_chunks, n_layers, table.S,
                                   n_kv_heads, head_dim, dtype_code(k_out.dtype), _vp(rope),
                                   rope.shape[0], _vp(positions), ROPE_MODES[mode], _vp(kb), _vp(vb),
                                   lstride, _vp(status), _stream(dev)), "cbk_assemble_kv")
@@ -186,7 +190,8 @@ def rope_scatter(q_src: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor, 
     n_sel = idx.numel()
     if q_out is None:
         q_out = torch.empty((n_sel, n_q_heads * head_dim), dtype=q_src.dtype, device=dev)
-    N.check(N.LIB.cbk_rope_scatter(_vp(q2), q2.stride(0), _vp(k2), k2.stride(0), _vp(v2), v2.stride(0),
+    with TIMES.span("rope_scatter", dev):
+      N.check(N.LIB.cbk_rope_scatter(_vp(q2), q2.stride(0), _vp(k2), k2.stride(0), _vp(v2), v2.stride(0),
                                    int(bool(gather)), _vp(idx), n_sel, int(S), n_q_heads, n_kv_heads,
                                    head_dim, dtype_code(q_src.dtype), _vp(rope), rope.shape[0],
                                    ROPE_MODES[mode], _vp(q_out), _vp(k_cache), _vp(v_cache),
@@ -201,7 +206,8 @@ def kv_deviation_rows(k_new: torch.Tensor, table: ChunkTable, layer: int) -> tor
     dev = require_cuda(k_new)
     kn = _rows(k_new, "K_new")
     out = torch.empty((table.S,), dtype=torch.float32, device=dev)
-    N.check(N.LIB.cbk_kv_deviation(_vp(kn), kn.stride(0), _vp(table.layer_ptr(layer)),
+    with TIMES.span("kv_deviation", dev):
+      N.check(N.LIB.cbk_kv_deviation(_vp(kn), kn.stride(0), _vp(table.layer_ptr(layer)),
                                    _vp(table.starts), table.n_chunks, table.S, kn.shape[1],
                                    dtype_code(k_new.dtype), _vp(out), _stream(dev)),
             "cbk_kv_deviation")
@@ -218,7 +224,8 @@ def topk_select(dev_scores: torch.Tensor, k: int, force_last: bool = False, stat
         dev_scores = dev_scores.float()
     d = dev_scores.contiguous()
     idx = torch.empty((int(k),), dtype=torch.int64, device=dev)
-    N.check(N.LIB.cbk_topk_select(_vp(d), d.numel(), int(k), int(bool(force_last)), _vp(idx),
+    with TIMES.span("topk_select", dev):
+      N.check(N.LIB.cbk_topk_select(_vp(d), d.numel(), int(k), int(bool(force_last)), _vp(idx),
                                   _vp(status), _stream(dev)), "cbk_topk_select")
     return idx
 
@@ -234,7 +241,8 @@ def hkvd_select(k_new: torch.Tensor, table: ChunkTable, layer: int, k: int, forc
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty((need // 4,), dtype=torch.float32, device=dev)
     idx = torch.empty((int(k),), dtype=torch.int64, device=dev)
-    N.check(N.LIB.cbk_hkvd_select(_vp(kn), kn.stride(0), _vp(table.layer_ptr(layer)),
+    with TIMES.span("hkvd_select", dev, 2):
+      N.check(N.LIB.cbk_hkvd_select(_vp(kn), kn.stride(0), _vp(table.layer_ptr(layer)),
                                   _vp(table.starts), table.n_chunks, S, kn.shape[1],
                                   dtype_code(k_new.dtype), int(k), int(bool(force_last)), _vp(idx),
                                   _vp(workspace), need, _vp(status), _stream(dev)),
@@ -260,7 +268,8 @@ def partial_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
             raise ValueError(f"partial_attn: {name} must be contiguous")
     if out is None:
         out = torch.empty((n_sel, n_q_heads * head_dim), dtype=q.dtype, device=dev)
-    N.check(N.LIB.cbk_partial_attn(_vp(q), _vp(k_cache), _vp(v_cache), _vp(pos), n_sel, S,
+    with TIMES.span("partial_attn", dev):
+      N.check(N.LIB.cbk_partial_attn(_vp(q), _vp(k_cache), _vp(v_cache), _vp(pos), n_sel, S,
                                    n_q_heads, n_kv_heads, head_dim, float(scale),
                                    dtype_code(q.dtype), _vp(out), _vp(status), _stream(dev)),
             "cbk_partial_attn")

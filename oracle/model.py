@@ -83,7 +83,7 @@ def attention(q_post, k_post, v, pos_q, W: Weights):
     """GQA causal attention of query rows (positions pos_q) over all keys."""
     D = W.cfg.head_dim
     o = hp.partial_attention(_heads(q_post, D), _heads(k_post, D), _heads(v, D), pos_q,
-                             D ** -0.5)
+                             D ** -0.5, dtype=np.float32)
     return o.astype(np.float32)
 
 
@@ -129,14 +129,23 @@ class SelectiveResult:
     cache_v: list               # per layer (S, Hkv*D) fused V
 
 
-def fuse_selective(chunk_ids, chunk_k, chunk_v, W: Weights, recompute_ratio=0.15, check_layer=1,
-                   force_idx=None, n_layers=None):
-    """fusor.py:193-497 for >1 chunk and 0 < ratio < 1 (the selective path).
+@dataclass
+class SelectiveState:
+    """Running state of the selective forward after the check layer."""
+    S: int
+    idx: np.ndarray
+    deviations: np.ndarray
+    hs: np.ndarray              # (k, hidden) hidden rows of the selected tokens
+    K_st: list                  # per layer (S, Hkv*D) concatenated cached pre-RoPE K
+    V_st: list
+    cache_k: list
+    cache_v: list
 
-    chunk_ids: list of per-chunk token id lists; chunk_k / chunk_v: [chunk][layer]
-    (Lc, Hkv*D) pre-RoPE K / V.  ``force_idx`` replaces the HKVD selection (to
-    compare a device run that selected from its own deviations).  ``n_layers``
-    truncates the stack (the CPU baseline times a sample of layers)."""
+
+def selective_begin(chunk_ids, chunk_k, chunk_v, W: Weights, recompute_ratio=0.15, check_layer=1,
+                    force_idx=None, n_layers=None) -> SelectiveState:
+    """fusor.py:258-406: concat of the cached K/V, the dense layers before the
+    check layer, HKVD + force-include, and the check layer itself."""
     c = W.cfg
     ck = check_layer
     nl = c.num_hidden_layers if n_layers is None else n_layers
@@ -170,20 +179,48 @@ def fuse_selective(chunk_ids, chunk_k, chunk_v, W: Weights, recompute_ratio=0.15
     a = attention(qp[idx], kp, v_mixed, idx, W) @ L["o"].T
     hs = (h[idx] + a).astype(np.float32)
     hs = (hs + mlp(rmsnorm(hs, L["ln2"], c.rms_norm_eps), L)).astype(np.float32)
-    # sparse layers (fusor.py:415-480)
-    for l in range(ck + 1, nl):
-        L = W.layers[l]
-        hn = rmsnorm(hs, L["ln1"], c.rms_norm_eps)
-        q, k_pre, v = hn @ L["q"].T, hn @ L["k"].T, hn @ L["v"].T
-        qp, kp_sparse = rope(q, idx, W), rope(k_pre, idx, W)
-        kfull = hp.scatter_rows(rope(K_st[l], pos_full, W), idx, kp_sparse)
-        vfull = hp.scatter_rows(V_st[l], idx, v)
-        cache_k.append(kfull)
-        cache_v.append(vfull)
-        a = attention(qp, kfull, vfull, idx, W) @ L["o"].T
-        hs = (hs + a).astype(np.float32)
-        hs = (hs + mlp(rmsnorm(hs, L["ln2"], c.rms_norm_eps), L)).astype(np.float32)
-    logits_sparse = rmsnorm(hs, W.norm, c.rms_norm_eps) @ W.lm_head.T
-    logits = np.zeros((S, logits_sparse.shape[1]), np.float32)
-    logits[idx] = logits_sparse
-    return SelectiveResult(logits, idx, dev, cache_k, cache_v)
+    return SelectiveState(S, idx, dev, hs, K_st, V_st, cache_k, cache_v)
+
+
+def selective_layer(st: SelectiveState, l: int, W: Weights, keep_cache: bool = True) -> None:
+    """One sparse layer (fusor.py:415-480): selected rows only, attending over
+    the full fused cache (RoPE-shifted cached K/V with the fresh rows scattered in)."""
+    c = W.cfg
+    L = W.layers[l]
+    idx = st.idx
+    pos_full = np.arange(st.S)
+    hn = rmsnorm(st.hs, L["ln1"], c.rms_norm_eps)
+    q, k_pre, v = hn @ L["q"].T, hn @ L["k"].T, hn @ L["v"].T
+    qp, kp_sparse = rope(q, idx, W), rope(k_pre, idx, W)
+    kfull = hp.scatter_rows(rope(st.K_st[l], pos_full, W), idx, kp_sparse)
+    vfull = hp.scatter_rows(st.V_st[l], idx, v)
+    if keep_cache:
+        st.cache_k.append(kfull)
+        st.cache_v.append(vfull)
+    a = attention(qp, kfull, vfull, idx, W) @ L["o"].T
+    hs = (st.hs + a).astype(np.float32)
+    st.hs = (hs + mlp(rmsnorm(hs, L["ln2"], c.rms_norm_eps), L)).astype(np.float32)
+
+
+def selective_end(st: SelectiveState, W: Weights) -> SelectiveResult:
+    """fusor.py:483-491: final norm + lm_head on the selected rows, scattered
+    into zero logits of the full length."""
+    logits_sparse = rmsnorm(st.hs, W.norm, W.cfg.rms_norm_eps) @ W.lm_head.T
+    logits = np.zeros((st.S, logits_sparse.shape[1]), np.float32)
+    logits[st.idx] = logits_sparse
+    return SelectiveResult(logits, st.idx, st.deviations, st.cache_k, st.cache_v)
+
+
+def fuse_selective(chunk_ids, chunk_k, chunk_v, W: Weights, recompute_ratio=0.15, check_layer=1,
+                   force_idx=None, n_layers=None):
+    """fusor.py:193-497 for >1 chunk and 0 < ratio < 1 (the selective path).
+
+    chunk_ids: list of per-chunk token id lists; chunk_k / chunk_v: [chunk][layer]
+    (Lc, Hkv*D) pre-RoPE K / V.  ``force_idx`` replaces the HKVD selection (to
+    compare a device run that selected from its own deviations).  ``n_layers``
+    truncates the stack."""
+    nl = W.cfg.num_hidden_layers if n_layers is None else n_layers
+    st = selective_begin(chunk_ids, chunk_k, chunk_v, W, recompute_ratio, check_layer, force_idx, nl)
+    for l in range(check_layer + 1, nl):
+        selective_layer(st, l, W)
+    return selective_end(st, W)
