@@ -1,0 +1,57 @@
+"""Multi-GPU partitioning of the blend path.
+
+By request: requests are independent, so each rank (one process per GPU) runs
+its own requests end to end with no collective on the data path.
+
+By KV head (long contexts that one GPU cannot hold): rank r of N keeps KV heads
+[r*Hkv/N, (r+1)*Hkv/N) and the q heads of their groups.  Concat + RoPE shift,
+the fresh-row scatter and partial attention are head-local.  HKVD needs the
+per-token deviation summed over all heads: every rank computes its partial
+over its own heads, the partials are all-gathered (S fp32 per rank) and summed
+in rank order on every rank, so every rank selects the identical index set
+without a broadcast.  The sum is a deterministic function of N (a different
+rounding order than the single-GPU kernel, so the single-GPU selection can
+differ only where two deviations tie to fp32 rounding).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def head_shard(n_kv_heads: int, world: int, rank: int) -> tuple[int, int]:
+    """[lo, hi) KV heads of `rank`; heads must divide evenly."""
+    if n_kv_heads % world:
+        raise ValueError(f"{n_kv_heads} KV heads do not split over {world} ranks")
+    per = n_kv_heads // world
+    return rank * per, (rank + 1) * per
+
+
+def combine_partials(parts) -> torch.Tensor:
+    """Sum per-rank deviation partials in rank order (elementwise fp32 adds)."""
+    total = parts[0].clone()
+    for p in parts[1:]:
+        total = total + p
+    return total
+
+
+def exchange_deviation(partial: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather per-rank deviation partials (S,) fp32 and sum them in rank
+    order; every rank returns the same tensor."""
+    world = dist.get_world_size(group)
+    if world == 1:
+        return partial
+    flat = partial.reshape(-1).contiguous()
+    gathered = torch.empty((world * flat.numel(),), dtype=flat.dtype, device=flat.device)
+    dist.all_gather_into_tensor(gathered, flat, group=group)
+    return combine_partials(list(gathered.view(world, -1).unbind(0)))
+
+
+def sharded_hkvd_select(k_new_shard: torch.Tensor, table_shard, layer: int, k: int, group=None,
+                        force_last: bool = True) -> torch.Tensor:
+    """HKVD over KV heads spread across ranks: partial deviation of this rank's
+    heads (deviation_kernel), exchange, then the same top-K on every rank."""
+    from cacheblend import ops
+    partial = ops.kv_deviation_rows(k_new_shard, table_shard, layer)
+    total = exchange_deviation(partial, group)
+    return ops.topk_select(total, k, force_last=force_last)

@@ -47,7 +47,7 @@ def _setup(cfg_kwargs=None, n_chunks=4, chunk_len=128, q_len=32, seed=0):
 def _oracle_weights(model):
     cfg = om.Config.from_hf(model.config)
     sd = {n: t.float().cpu().numpy() for n, t in model.state_dict().items()}
-    return om.Weights(sd, cfg, model.model.rotary_emb.inv_freq.cpu().numpy())
+    return om.Weights(sd, cfg, model.model.rotary_emb.inv_freq.float().cpu().numpy())
 
 
 def _check_selective(cb, lw, model, chunks, store, ratio=0.15, ck=1):
@@ -74,7 +74,7 @@ def _check_selective(cb, lw, model, chunks, store, ratio=0.15, ck=1):
     # (a)+(b)+(d) the fused cache of every cached layer
     rot = model.model.rotary_emb
     tab = cb.ops.rope_table(rot.inv_freq, S).cpu().numpy()
-    invf = rot.inv_freq.cpu().numpy()
+    invf = rot.inv_freq.float().cpu().numpy()
     attn0 = model.model.layers[0].self_attn
     D, Hkv = attn0.head_dim, model.config.num_key_value_heads
     rest = np.setdiff1d(np.arange(S), idx_np)
@@ -165,7 +165,7 @@ def test_apply_rope_shift_api():
     out = cb.apply_rope_shift(K, pos, lw)
     assert out.shape == K.shape and out.dtype == K.dtype
     D = model.model.layers[0].self_attn.head_dim
-    exp = hp.apply_rope(to_bits(K[0]), np.arange(128, 256), model.model.rotary_emb.inv_freq.cpu().numpy(),
+    exp = hp.apply_rope(to_bits(K[0]), np.arange(128, 256), model.model.rotary_emb.inv_freq.float().cpu().numpy(),
                         D, "bf16", "ref")
     from helpers import ulp_diff_bf16
     ud = ulp_diff_bf16(to_bits(out[0]), f32_to_bf16(exp))
