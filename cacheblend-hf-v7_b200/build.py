@@ -1,9 +1,10 @@
 """Build libcbk.so (the sm_100a kernels + C ABI) in-tree with nvcc.
 
-    python -m cacheblend._build        # from cacheblend-hf-v7_b200/
+    python cacheblend-hf-v7_b200/build.py [--force]
 
-The library lands next to this file (``cacheblend/lib/libcbk.so``) so that it
-travels with the source tree; nothing is installed into site-packages.
+The library lands in the package (``cacheblend/lib/libcbk.so``) so that it
+travels with the source tree; nothing is installed into site-packages.  This
+script never imports the package (which would load the old library).
 """
 from __future__ import annotations
 
@@ -13,8 +14,8 @@ import shutil
 import subprocess
 import sys
 
-PKG_DIR = os.path.dirname(os.path.abspath(__file__))
-ROOT = os.path.dirname(PKG_DIR)                      # cacheblend-hf-v7_b200/
+ROOT = os.path.dirname(os.path.abspath(__file__))   # cacheblend-hf-v7_b200/
+PKG_DIR = os.path.join(ROOT, "cacheblend")
 CSRC = os.path.join(ROOT, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libcbk.so")

@@ -46,7 +46,7 @@ SIGNATURES = {
 def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(
-            f"libcbk.so not found at {LIB_PATH}; build it with `python -m cacheblend._build` "
+            f"libcbk.so not found at {LIB_PATH}; build it with `python cacheblend-hf-v7_b200/build.py` "
             "(needs nvcc).  There is no CPU fallback.")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (res, args) in SIGNATURES.items():

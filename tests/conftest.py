@@ -17,7 +17,7 @@ def pytest_configure(config):
     # would load the old library before it is replaced.
     import importlib.util
     spec = importlib.util.spec_from_file_location(
-        "_cbk_build", os.path.join(PKG, "cacheblend", "_build.py"))
+        "_cbk_build", os.path.join(PKG, "build.py"))
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     mod.build()
