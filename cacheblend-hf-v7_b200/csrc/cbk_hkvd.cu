@@ -11,6 +11,8 @@
 // unsigned order; four 8-bit radix passes find the k-th largest key T and how
 // many elements equal to T are taken (lowest index first).  A tiled,
 // order-preserving compaction then writes the ascending index list.
+#include <mutex>
+
 #include "cbk_common.cuh"
 
 namespace cbk {
@@ -258,6 +260,78 @@ extern "C" int cbk_hkvd_select(const void* k_new, int64_t new_row_stride,
                      cbk_hkvd_workspace_bytes(S));
   auto st = static_cast<cudaStream_t>(stream);
   float* dev = static_cast<float*>(workspace);
+  if (int rc = launch_deviation(k_new, new_row_stride, old_srcs, chunk_start, n_chunks, S, feat,
+                                dtype, dev, st))
+    return rc;
+  return launch_topk(dev, S, k, force_last, idx, status, st);
+}
+
+// ---------------------------------------------------------------------------
+// HKVD selection without any allocation.
+//
+// Some callers cannot allocate device memory at the moment they select tokens:
+// a serving engine that reserves nearly all HBM for its own KV-cache pool up
+// front (an extra cudaMalloc then fails or fragments that pool), or a
+// latency-critical step where cudaMalloc / cudaFree would synchronise the
+// device.  For them the deviation scores live in a fixed scratch array that the
+// library owns: kNoAllocMaxTokens fp32 (1 MiB) in device memory, held on every
+// GPU that loads the library until the process exits.
+//
+// The array's host-side name is only a stand-in for the device address, so the
+// address is looked up with cudaGetSymbolAddress once per device, on the first
+// call made with that device current; make that first call before any stream
+// capture.  All calls share the array and it keeps the previous call's
+// contents; nothing in it is read before this call writes it (positions
+// [0, S) are written by the deviation kernel before the top-K kernel reads
+// them), so nothing needs clearing.  Calls that overlap on the GPU (two streams,
+// or two threads on different streams of one device) race on the array: order
+// them on one stream.
+// ---------------------------------------------------------------------------
+namespace cbk {
+
+constexpr int64_t kNoAllocMaxTokens = 262144;
+static __device__ __align__(256) float g_hkvd_noalloc_scratch[kNoAllocMaxTokens];
+
+static int noalloc_scratch(float** out) {
+  static std::mutex mu;
+  static float* addr[64] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return set_error(CBK_ERR_CUDA, "cbk_hkvd_select_noalloc: cudaGetDevice failed");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_hkvd_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(CBK_ERR_CUDA, "cbk_hkvd_select_noalloc: cudaGetSymbolAddress failed: %s",
+                       cudaGetErrorString(e));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return CBK_OK;
+}
+
+}  // namespace cbk
+
+extern "C" int64_t cbk_hkvd_noalloc_max_tokens(void) { return kNoAllocMaxTokens; }
+
+extern "C" int cbk_hkvd_select_noalloc(const void* k_new, int64_t new_row_stride,
+                                       const cbk_chunk_src* old_srcs, const int64_t* chunk_start,
+                                       int n_chunks, int64_t S, int64_t feat, int dtype, int64_t k,
+                                       int force_last, int64_t* idx, int32_t* status, void* stream) {
+  if (int rc = check_dev_args("cbk_hkvd_select_noalloc", k_new, new_row_stride, old_srcs,
+                              chunk_start, n_chunks, S, feat, dtype))
+    return rc;
+  if (!idx) return set_error(CBK_ERR_INVALID, "cbk_hkvd_select_noalloc: null output");
+  if (S > kNoAllocMaxTokens)
+    return set_error(CBK_ERR_INVALID,
+                     "cbk_hkvd_select_noalloc: S = %lld tokens exceeds the fixed scratch of %lld "
+                     "tokens; use cbk_hkvd_select with a caller workspace",
+                     (long long)S, (long long)kNoAllocMaxTokens);
+  if (k <= 0 || k > S) return set_error(CBK_ERR_INVALID, "cbk_hkvd_select_noalloc: need 0 < k <= S");
+  float* dev = nullptr;
+  if (int rc = noalloc_scratch(&dev)) return rc;
+  auto st = static_cast<cudaStream_t>(stream);
   if (int rc = launch_deviation(k_new, new_row_stride, old_srcs, chunk_start, n_chunks, S, feat,
                                 dtype, dev, st))
     return rc;

@@ -145,6 +145,22 @@ int cbk_hkvd_select(const void* k_new, int64_t new_row_stride, const cbk_chunk_s
                     int64_t k, int force_last, int64_t* idx, void* workspace, size_t workspace_bytes,
                     int32_t* status, void* stream);
 
+/* (c) deviation + select with no allocation at all: the deviation scores live in
+ * a fixed device array owned by the library (cbk_hkvd_noalloc_max_tokens() fp32
+ * entries, 1 MiB, kept on every GPU that loads the library until exit).  For
+ * callers that cannot allocate device memory when they select (an engine that
+ * has reserved the HBM for its own pools, or a step where cudaMalloc would
+ * synchronise the device).  No counterpart in the reference.  Same arguments
+ * and results as cbk_hkvd_select without the workspace; S above the maximum is
+ * rejected (CBK_ERR_INVALID).  The first call on a device looks up the array's
+ * address (make it before any stream capture); calls that overlap on the GPU
+ * share the array and race. */
+int64_t cbk_hkvd_noalloc_max_tokens(void);
+int cbk_hkvd_select_noalloc(const void* k_new, int64_t new_row_stride, const cbk_chunk_src* old_srcs,
+                            const int64_t* chunk_start, int n_chunks, int64_t S, int64_t feat,
+                            int dtype, int64_t k, int force_last, int64_t* idx, int32_t* status,
+                            void* stream);
+
 /* (e) partial-query attention on tcgen05 (fusor.py:381-399, 462-474):
  *   out[j][h] = softmax_t<=pos[j]( scale * q[j][h] . k[t][h/G] ) . v[t][h/G]
  * for j < n_sel, h < n_q_heads, G = n_q_heads / n_kv_heads, keys t in [0, pos[j]].
