@@ -537,10 +537,12 @@ def run_attn_layers(args):
     vc = torch.randn((L, S, Hkv * D), generator=g, device=device).to(torch.bfloat16)
     q = torch.randn((L, k, Hq * D), generator=g, device=device).to(torch.bfloat16)
     out = torch.empty((k, Hq * D), dtype=torch.bfloat16, device=device)
+    ws = ops.attn_workspace(k, S, Hq, Hkv, D, device)
 
     def step(i):
-        for l in range(L):
-            ops.partial_attn(q[l], kc[l], vc[l], pos, Hq, Hkv, D, D ** -0.5, out=out)
+        for l in range(L):   # one plan per step, reused by the other layers (as in fuse_selective)
+            ops.partial_attn(q[l], kc[l], vc[l], pos, Hq, Hkv, D, D ** -0.5, out=out, workspace=ws,
+                             reuse_plan=l > 0)
 
     ms, kern, clk = _timed(step, args.steps, args.warmup, device)
     n, t = kern["partial_attn"]

@@ -41,8 +41,9 @@ SIGNATURES = {
     "cbk_hkvd_noalloc_max_tokens": (_i64, []),
     "cbk_hkvd_select_noalloc": (_i32, [_vp, _i64, _vp, _vp, _i32, _i64, _i64, _i32, _i64, _i32, _vp,
                                        _vp, _vp]),
+    "cbk_partial_attn_workspace_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32]),
     "cbk_partial_attn": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _f32, _i32, _vp,
-                                _vp, _vp]),
+                                _vp, _sz, _i32, _vp, _vp]),
 }
 
 

@@ -122,7 +122,7 @@ class _Geometry:
         self.scaling = float(attn0.scaling)
 
 
-def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_mode):
+def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_mode, ws, reuse):
     """q/k/v projections -> (b)+(d) RoPE + scatter into the fused cache ->
     (e) partial attention -> o_proj.  Returns the attention output rows."""
     attn = layer.self_attn
@@ -132,7 +132,7 @@ def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_
     q_rot = ops.rope_scatter(q[0], k_pre[0], v[0], pos, gather, S, geo.n_q, geo.n_kv, geo.head_dim,
                              rope, kc, vc, mode=rope_mode, status=status)
     a = ops.partial_attn(q_rot, kc, vc, pos, geo.n_q, geo.n_kv, geo.head_dim, geo.scaling,
-                         status=status)
+                         status=status, workspace=ws, reuse_plan=reuse)
     return attn.o_proj(a.unsqueeze(0)), k_pre
 
 
@@ -214,10 +214,11 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
         pos_all = torch.arange(S, device=device, dtype=torch.int64)
         h = inner.embed_tokens(ids)
 
-        for li in range(ck):                                  # dense layers
+        ws_dense = ops.attn_workspace(S, S, geo.n_q, geo.n_kv, geo.head_dim, device) if ck else None
+        for li in range(ck):                                  # dense layers (one shared plan)
             layer = inner.layers[li]
             a, _ = _attention_block(layer, geo, layer.input_layernorm(h), pos_all, S, rope,
-                                    fused_k[li], fused_v[li], False, status, rope_mode)
+                                    fused_k[li], fused_v[li], False, status, rope_mode, ws_dense, li > 0)
             h = _mlp_block(layer, h + a)
 
         # check layer: full projections, HKVD, then sparse from here on
@@ -231,15 +232,16 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
         cur.wait_event(assembled)
         q_rot = ops.rope_scatter(q[0], k_pre[0], v[0], idx, True, S, geo.n_q, geo.n_kv, geo.head_dim,
                                  rope, fused_k[ck], fused_v[ck], mode=rope_mode, status=status)
+        ws_sparse = ops.attn_workspace(k_sel, S, geo.n_q, geo.n_kv, geo.head_dim, device)
         a = ops.partial_attn(q_rot, fused_k[ck], fused_v[ck], idx, geo.n_q, geo.n_kv, geo.head_dim,
-                             geo.scaling, status=status)
+                             geo.scaling, status=status, workspace=ws_sparse, reuse_plan=False)
         hs = h.index_select(1, idx) + attn.o_proj(a.unsqueeze(0))
         hs = _mlp_block(layer, hs)
 
         for li in range(ck + 1, n_layers):                    # sparse layers
             layer = inner.layers[li]
             a, _ = _attention_block(layer, geo, layer.input_layernorm(hs), idx, S, rope,
-                                    fused_k[li], fused_v[li], False, status, rope_mode)
+                                    fused_k[li], fused_v[li], False, status, rope_mode, ws_sparse, True)
             hs = _mlp_block(layer, hs + a)
 
         logits_sparse = lw.model.lm_head(inner.norm(hs))      # (1, k, vocab)

@@ -68,8 +68,8 @@ def rope_table(inv_freq: torch.Tensor, n_pos: int, scaling: float = 1.0) -> torc
     half = inv.numel()
     table = torch.empty((int(n_pos), half, 2), dtype=torch.float32, device=dev)
     with TIMES.span("rope_table", dev):
-      N.check(N.LIB.cbk_rope_table(_vp(inv), half, int(n_pos), float(scaling), _vp(table), _stream(dev)),
-            "cbk_rope_table")
+        N.check(N.LIB.cbk_rope_table(_vp(inv), half, int(n_pos), float(scaling), _vp(table), _stream(dev)),
+              "cbk_rope_table")
     return table
 
 
@@ -87,9 +87,9 @@ def rope_rows(x: torch.Tensor, positions: torch.Tensor, table: torch.Tensor, hea
     if n_heads * head_dim != xr.shape[1]:
         raise ValueError(f"row width {xr.shape[1]} is not a multiple of head_dim {head_dim}")
     with TIMES.span("rope_rows", dev):
-      N.check(N.LIB.cbk_rope_rows(_vp(xr), _vp(out), xr.shape[0], n_heads, head_dim,
-                                dtype_code(x.dtype), _vp(table), table.shape[0], _vp(pos),
-                                ROPE_MODES[mode], _vp(status), _stream(dev)), "cbk_rope_rows")
+        N.check(N.LIB.cbk_rope_rows(_vp(xr), _vp(out), xr.shape[0], n_heads, head_dim,
+                                  dtype_code(x.dtype), _vp(table), table.shape[0], _vp(pos),
+                                  ROPE_MODES[mode], _vp(status), _stream(dev)), "cbk_rope_rows")
     return out.view(x.shape)
 
 
@@ -173,10 +173,10 @@ def assemble_kv(table: ChunkTable, layer_lo: int, layer_hi: int, n_kv_heads: int
     kb = k_out.data_ptr() + layer_lo * lstride * k_out.element_size()
     vb = v_out.data_ptr() + layer_lo * lstride * v_out.element_size()
     with TIMES.span("assemble_kv", dev):
-      N.check(N.LIB.cbk_assemble_kv(_vp(srcs), _vp(table.starts), table.n_chunks, n_layers, table.S,
-                                  n_kv_heads, head_dim, dtype_code(k_out.dtype), _vp(rope),
-                                  rope.shape[0], _vp(positions), ROPE_MODES[mode], _vp(kb), _vp(vb),
-                                  lstride, _vp(status), _stream(dev)), "cbk_assemble_kv")
+        N.check(N.LIB.cbk_assemble_kv(_vp(srcs), _vp(table.starts), table.n_chunks, n_layers, table.S,
+                                    n_kv_heads, head_dim, dtype_code(k_out.dtype), _vp(rope),
+                                    rope.shape[0], _vp(positions), ROPE_MODES[mode], _vp(kb), _vp(vb),
+                                    lstride, _vp(status), _stream(dev)), "cbk_assemble_kv")
 
 
 def rope_scatter(q_src: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor, idx: torch.Tensor,
@@ -191,11 +191,11 @@ def rope_scatter(q_src: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor, 
     if q_out is None:
         q_out = torch.empty((n_sel, n_q_heads * head_dim), dtype=q_src.dtype, device=dev)
     with TIMES.span("rope_scatter", dev):
-      N.check(N.LIB.cbk_rope_scatter(_vp(q2), q2.stride(0), _vp(k2), k2.stride(0), _vp(v2), v2.stride(0),
-                                   int(bool(gather)), _vp(idx), n_sel, int(S), n_q_heads, n_kv_heads,
-                                   head_dim, dtype_code(q_src.dtype), _vp(rope), rope.shape[0],
-                                   ROPE_MODES[mode], _vp(q_out), _vp(k_cache), _vp(v_cache),
-                                   _vp(status), _stream(dev)), "cbk_rope_scatter")
+        N.check(N.LIB.cbk_rope_scatter(_vp(q2), q2.stride(0), _vp(k2), k2.stride(0), _vp(v2), v2.stride(0),
+                                     int(bool(gather)), _vp(idx), n_sel, int(S), n_q_heads, n_kv_heads,
+                                     head_dim, dtype_code(q_src.dtype), _vp(rope), rope.shape[0],
+                                     ROPE_MODES[mode], _vp(q_out), _vp(k_cache), _vp(v_cache),
+                                     _vp(status), _stream(dev)), "cbk_rope_scatter")
     return q_out
 
 
@@ -207,10 +207,10 @@ def kv_deviation_rows(k_new: torch.Tensor, table: ChunkTable, layer: int) -> tor
     kn = _rows(k_new, "K_new")
     out = torch.empty((table.S,), dtype=torch.float32, device=dev)
     with TIMES.span("kv_deviation", dev):
-      N.check(N.LIB.cbk_kv_deviation(_vp(kn), kn.stride(0), _vp(table.layer_ptr(layer)),
-                                   _vp(table.starts), table.n_chunks, table.S, kn.shape[1],
-                                   dtype_code(k_new.dtype), _vp(out), _stream(dev)),
-            "cbk_kv_deviation")
+        N.check(N.LIB.cbk_kv_deviation(_vp(kn), kn.stride(0), _vp(table.layer_ptr(layer)),
+                                     _vp(table.starts), table.n_chunks, table.S, kn.shape[1],
+                                     dtype_code(k_new.dtype), _vp(out), _stream(dev)),
+              "cbk_kv_deviation")
     return out
 
 
@@ -225,8 +225,8 @@ def topk_select(dev_scores: torch.Tensor, k: int, force_last: bool = False, stat
     d = dev_scores.contiguous()
     idx = torch.empty((int(k),), dtype=torch.int64, device=dev)
     with TIMES.span("topk_select", dev):
-      N.check(N.LIB.cbk_topk_select(_vp(d), d.numel(), int(k), int(bool(force_last)), _vp(idx),
-                                  _vp(status), _stream(dev)), "cbk_topk_select")
+        N.check(N.LIB.cbk_topk_select(_vp(d), d.numel(), int(k), int(bool(force_last)), _vp(idx),
+                                    _vp(status), _stream(dev)), "cbk_topk_select")
     return idx
 
 
@@ -242,24 +242,35 @@ def hkvd_select(k_new: torch.Tensor, table: ChunkTable, layer: int, k: int, forc
         workspace = torch.empty((need // 4,), dtype=torch.float32, device=dev)
     idx = torch.empty((int(k),), dtype=torch.int64, device=dev)
     with TIMES.span("hkvd_select", dev, 2):
-      N.check(N.LIB.cbk_hkvd_select(_vp(kn), kn.stride(0), _vp(table.layer_ptr(layer)),
-                                  _vp(table.starts), table.n_chunks, S, kn.shape[1],
-                                  dtype_code(k_new.dtype), int(k), int(bool(force_last)), _vp(idx),
-                                  _vp(workspace), need, _vp(status), _stream(dev)),
-            "cbk_hkvd_select")
+        N.check(N.LIB.cbk_hkvd_select(_vp(kn), kn.stride(0), _vp(table.layer_ptr(layer)),
+                                    _vp(table.starts), table.n_chunks, S, kn.shape[1],
+                                    dtype_code(k_new.dtype), int(k), int(bool(force_last)), _vp(idx),
+                                    _vp(workspace), need, _vp(status), _stream(dev)),
+              "cbk_hkvd_select")
     return idx, workspace.view(torch.float32)[:S]
 
 
 # ---------------------------------------------------------------------------
 # (e) partial attention
 # ---------------------------------------------------------------------------
+def attn_workspace(n_sel: int, S: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
+                   device) -> torch.Tensor:
+    """Workspace for partial_attn (work plan + split partial results)."""
+    nbytes = int(N.LIB.cbk_partial_attn_workspace_bytes(int(n_sel), int(S), n_q_heads, n_kv_heads, head_dim))
+    if nbytes == 0:
+        N.check(N.CBK_ERR_INVALID, "cbk_partial_attn_workspace_bytes")
+    return torch.empty((nbytes,), dtype=torch.uint8, device=device)
+
+
 def partial_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor,
                  n_q_heads: int, n_kv_heads: int, head_dim: int, scale: float,
-                 out: torch.Tensor | None = None, status=None) -> torch.Tensor:
+                 out: torch.Tensor | None = None, status=None, workspace: torch.Tensor | None = None,
+                 reuse_plan: bool = False) -> torch.Tensor:
     """softmax(scale q k^T, keys <= pos) v for selected rows.
 
     q: [n_sel][Hq*D] (rotated); k_cache/v_cache: [S][Hkv*D]; pos: int64 [n_sel]
-    ascending.  Returns [n_sel][Hq*D]."""
+    ascending.  Returns [n_sel][Hq*D].  ``workspace`` (from attn_workspace) may
+    be shared by calls with the same pos; ``reuse_plan`` skips re-planning."""
     dev = require_cuda(q, k_cache, v_cache, pos)
     n_sel = pos.numel()
     S = k_cache.shape[0]
@@ -268,9 +279,13 @@ def partial_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
             raise ValueError(f"partial_attn: {name} must be contiguous")
     if out is None:
         out = torch.empty((n_sel, n_q_heads * head_dim), dtype=q.dtype, device=dev)
+    if workspace is None:
+        workspace = attn_workspace(n_sel, S, n_q_heads, n_kv_heads, head_dim, dev)
+        reuse_plan = False
     with TIMES.span("partial_attn", dev):
-      N.check(N.LIB.cbk_partial_attn(_vp(q), _vp(k_cache), _vp(v_cache), _vp(pos), n_sel, S,
-                                   n_q_heads, n_kv_heads, head_dim, float(scale),
-                                   dtype_code(q.dtype), _vp(out), _vp(status), _stream(dev)),
-            "cbk_partial_attn")
+        N.check(N.LIB.cbk_partial_attn(_vp(q), _vp(k_cache), _vp(v_cache), _vp(pos), n_sel, S,
+                                       n_q_heads, n_kv_heads, head_dim, float(scale),
+                                       dtype_code(q.dtype), _vp(out), _vp(workspace), workspace.numel(),
+                                       int(bool(reuse_plan)), _vp(status), _stream(dev)),
+                "cbk_partial_attn")
     return out

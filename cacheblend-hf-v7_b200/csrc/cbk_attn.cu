@@ -1,20 +1,33 @@
 // Partial-query attention on 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
-// One CTA computes a 128-row tile of (selected token, q-head) rows that share
-// one KV head: rows r = tok * G + h (G = q heads per KV head), TOK = 128 / G
-// selected tokens.  Keys are visited in 128-key tiles from 0 up to the largest
-// position in the tile; causality is a per-row position compare (no mask
-// tensor).  Accumulators live in TMEM: S = Q K^T (128 fp32 columns) and
-// O = P V (head_dim fp32 columns).
+// Work item = (KV head, pair of 128-row Q tiles, chunk of key tiles).  Rows of a
+// tile are r = tok * G + h (G = q heads per KV head, 128 / G selected tokens per
+// tile), so K/V tiles are shared by the GQA group without expanding them.  Keys
+// are visited in 128-key tiles; causality is a per-row position compare (no
+// mask tensor).  A tile whose key range is longer than one chunk is split over
+// several items; their partial results are merged by attn_combine_kernel.  The
+// chunking is planned on the device (attn_plan_kernel) from the positions, so
+// no host synchronisation is needed, and the plan can be reused by every layer
+// that attends with the same positions.
 //
-// Warp roles (256 threads):
-//   warp 0      TMA producer: Q once, then K/V tiles into a 2-stage ring
-//   warp 1      MMA issuer:   S(j+1) = Q K(j+1)^T is issued before O += P(j) V(j)
-//   warp 2      TMEM allocator
-//   warps 4..7  softmax + epilogue: thread i of warp w owns TMEM lane
-//               32*(w%4)+i, i.e. one full row; row max / exp / sum are
-//               thread-local.  O is rescaled only when the running max grows
-//               by more than 2^8 (the final O / l uses the same stale max).
+// TMEM (512 columns): tile t uses S/P at [256t, 256t+128) and O at
+// [256t+128, 256t+128+D).  S = Q K^T lands in fp32; the softmax warps write P
+// back in place as packed 16-bit pairs and the PV MMA reads P straight from
+// TMEM (A operand in tensor memory), so P never touches shared memory.
+//
+// Warp roles (384 threads):
+//   warp 0        TMA producer: both Q tiles once, then K and V tiles into two
+//                 separate 2-stage rings
+//   warp 1        MMA issuer: per key tile j, for t = 0, 1: O_t += P_t(j) V(j),
+//                 then S_t(j+1) = Q_t K(j+1)^T.  MMAs issued by one thread run
+//                 in order, so S_t(j+1) overwrites P_t(j) only after the PV
+//                 that reads it; while one tile's softmax runs, the tensor core
+//                 works on the other tile.
+//   warp 2        TMEM allocator
+//   warps 4..7    softmax of tile 0; warps 8..11 softmax of tile 1.  Thread i of
+//                 warp w owns TMEM lane 32*(w%4)+i, i.e. one row: max / exp / sum
+//                 are thread-local.  O is rescaled only when the running max
+//                 grows by more than 2^8 (O / l uses the same stale max).
 // Every mbarrier wait is bounded (2 s of wall time); on timeout the kernel
 // sets CBK_STATUS_TIMEOUT, drains its own TMA copies and MMAs, frees TMEM and
 // returns.
@@ -27,38 +40,51 @@
 
 namespace cbk {
 
-constexpr int kBM = 128;       // rows per CTA tile
+constexpr int kBM = 128;       // rows per Q tile
 constexpr int kBN = 128;       // keys per KV tile
-constexpr int kThreads = 256;
-constexpr uint32_t kTmemCols = 256;
+constexpr int kThreads = 384;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kMaxKvTiles = 2049;          // S <= 262144
 
 template <int HD>
 struct AttnSmem {
-  static constexpr int kQBytes = kBM * HD * 2;
-  static constexpr int kKVBytes = kBN * HD * 2;
-  static constexpr int kPBytes = kBM * kBN * 2;
-  static constexpr int kQ = 0;
-  static constexpr int kK0 = kQ + kQBytes;
-  static constexpr int kV0 = kK0 + 2 * kKVBytes;
-  static constexpr int kP = kV0 + 2 * kKVBytes;
-  static constexpr int kBar = kP + kPBytes;            // 16 x 8-byte barriers
-  static constexpr int kMisc = kBar + 16 * 8;          // tmem slot + abort flag
+  static constexpr int kQBytes = kBM * HD * 2;     // one Q tile
+  static constexpr int kKVBytes = kBN * HD * 2;    // one K or V tile
+  static constexpr int kQ = 0;                     // 2 Q tiles
+  static constexpr int kK0 = kQ + 2 * kQBytes;     // 2 K stages
+  static constexpr int kV0 = kK0 + 2 * kKVBytes;   // 2 V stages
+  static constexpr int kBar = kV0 + 2 * kKVBytes;  // 16 x 8-byte barriers
+  static constexpr int kMisc = kBar + 16 * 8;      // tmem slot + abort flag
   static constexpr int kTotal = kMisc + 16;
-  static constexpr int kAlloc = kTotal + 1024;         // slack for 1024-byte alignment
+  // at least 120 KB so that one CTA (holding all 512 TMEM columns) fills an SM
+  static constexpr int kAlloc = (kTotal + 1024) > 122880 ? (kTotal + 1024) : 122880;
 };
 
-enum Bar { B_Q = 0, B_KVFULL0 = 1, B_KVEMPTY0 = 3, B_SFULL = 5, B_SFREE = 6, B_PFULL = 7,
-           B_ODONE = 8, B_DRAIN = 9 };
+enum Bar { B_Q = 0, B_KFULL = 1, B_KEMPTY = 3, B_VFULL = 5, B_VEMPTY = 7, B_SFULL = 9,
+           B_PFULL = 11, B_ODONE = 13, B_DRAIN = 15 };
+
+// Work plan in the caller's workspace (written by attn_plan_kernel).
+struct AttnPlanHeader {
+  int n_items;     // work items (CTAs with work)
+  int chunk;       // key tiles per item (C)
+  int n_slots;     // partial-result slots in use
+  int error;       // nonzero: the plan did not fit the workspace bounds
+};
 
 struct AttnParams {
   const int64_t* pos;
   uint16_t* out;
   int32_t* status;
+  const AttnPlanHeader* plan;
+  const int4* items;      // (kv head, tile pair, chunk, length) longest first
+  const int* tile_base;   // [Hkv][n_tiles]: first partial slot of a split tile, -1 if not split
+  float* part_o;          // [slot][128][HD] unnormalised O
+  float2* part_ml;        // [slot][128] (running max in log2 units, row sum)
   int64_t n_sel;
   int n_q_heads;
   int group;          // G
   int tok_per_tile;   // 128 / G
-  int n_tiles;
+  int n_tiles;        // Q tiles per KV head
   float scale_log2;
 };
 
@@ -72,38 +98,74 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, vol
   }
 }
 
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  return static_cast<uint32_t>(Elem<DT>::from_f(lo)) | (static_cast<uint32_t>(Elem<DT>::from_f(hi)) << 16);
+}
+
+// number of 128-key tiles a Q tile needs (its last token has the largest position)
+__device__ __forceinline__ int tile_key_tiles(const int64_t* pos, int64_t n_sel, int tok_per_tile, int tile) {
+  const int64_t last = min(static_cast<int64_t>(tile + 1) * tok_per_tile, n_sel) - 1;
+  return static_cast<int>(pos[last] / kBN) + 1;
+}
+
 template <int DT, int HD>
 __global__ void __launch_bounds__(kThreads, 1)
 partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const AttnParams prm) {
   using L = AttnSmem<HD>;
+  // one work item per CTA; CTAs beyond the planned items exit at once
+  if (static_cast<int>(blockIdx.x) >= prm.plan->n_items || prm.plan->error) return;
+  const int4 item = prm.items[blockIdx.x];
+
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* sbase = smem_raw + (base - raw_addr);
-  const uint32_t sQ = base + L::kQ, sK0 = base + L::kK0, sV0 = base + L::kV0, sP = base + L::kP;
+  const uint32_t sQ = base + L::kQ, sK0 = base + L::kK0, sV0 = base + L::kV0;
   auto bar = [&](int i) { return base + L::kBar + 8u * i; };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sbase + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sbase + L::kMisc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = prm.n_tiles - 1 - static_cast<int>(blockIdx.x);   // longest tiles first
-  const int kvh = blockIdx.y;
-  const int64_t tok0 = static_cast<int64_t>(tile) * prm.tok_per_tile;
-  const int64_t tok_end = min(tok0 + prm.tok_per_tile, prm.n_sel);
-  const int64_t p_max = prm.pos[tok_end - 1];
-  const int n_kv = static_cast<int>(p_max / kBN) + 1;
+  const int kvh = item.x, pair = item.y, chunk = item.z;
+  const int C = prm.plan->chunk;
+  const int j0 = chunk * C;                 // first key tile of this item
+  // per-tile geometry (tile 1 may be absent for an odd tile count); returns the
+  // number of key tiles of this item for the tile
+  auto geom = [&](int t, int64_t& tok0, int64_t& tok_end, int64_t& p_max) -> int {
+    const int tile = 2 * pair + t;
+    tok0 = static_cast<int64_t>(tile) * prm.tok_per_tile;
+    if (tile >= prm.n_tiles) {
+      tok_end = tok0;
+      p_max = 0;
+      return 0;
+    }
+    tok_end = min(tok0 + prm.tok_per_tile, prm.n_sel);
+    p_max = prm.pos[tok_end - 1];
+    const int n_full = static_cast<int>(p_max / kBN) + 1;
+    return max(0, min(C, n_full - j0));
+  };
+  int64_t a0, a1, a2;
+  const int n_kv0 = geom(0, a0, a1, a2);
+  const int64_t q_tok0 = a0;
+  const int n_kv1 = geom(1, a0, a1, a2);
+  const int64_t q_tok1 = a0;
+  const int n_all = max(n_kv0, n_kv1);
+  const int n_q_tiles = (2 * pair + 1 < prm.n_tiles) ? 2 : 1;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(B_Q), 1);
-    mbar_init(bar(B_KVFULL0), 1);
-    mbar_init(bar(B_KVFULL0 + 1), 1);
-    mbar_init(bar(B_KVEMPTY0), 1);
-    mbar_init(bar(B_KVEMPTY0 + 1), 1);
-    mbar_init(bar(B_SFULL), 1);
-    mbar_init(bar(B_SFREE), 4);
-    mbar_init(bar(B_PFULL), 4);
-    mbar_init(bar(B_ODONE), 1);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B_KFULL + i), 1);
+      mbar_init(bar(B_KEMPTY + i), 1);
+      mbar_init(bar(B_VFULL + i), 1);
+      mbar_init(bar(B_VEMPTY + i), 1);
+      mbar_init(bar(B_SFULL + i), 1);
+      mbar_init(bar(B_PFULL + i), 4);
+      mbar_init(bar(B_ODONE + i), 1);
+    }
     mbar_init(bar(B_DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -116,7 +178,6 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + kBN;
   bool failed = false;
 
   if (warp == 0 && lane == 0) {
@@ -124,73 +185,99 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
-    mbar_expect_tx(bar(B_Q), L::kQBytes);
+    mbar_expect_tx(bar(B_Q), n_q_tiles * L::kQBytes);
+    for (int t = 0; t < n_q_tiles; ++t)
 #pragma unroll
-    for (int h = 0; h < HD / 64; ++h)
-      tma_load_3d(sQ + h * (kBM * 128), &tm_q, bar(B_Q), h * 64, kvh * prm.group,
-                  static_cast<int>(tok0));
-    int last_armed[2] = {-1, -1};
-    for (int j = 0; j < n_kv; ++j) {
+      for (int h = 0; h < HD / 64; ++h)
+        tma_load_3d(sQ + t * L::kQBytes + h * (kBM * 128), &tm_q, bar(B_Q), h * 64,
+                    kvh * prm.group, static_cast<int>(t ? q_tok1 : q_tok0));
+    int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
+    for (int j = 0; j < n_all; ++j) {
       const int st = j & 1;
-      if (j >= 2 && !wait_or_abort(bar(B_KVEMPTY0 + st), ((j >> 1) - 1) & 1, abort_flag)) {
+      if (j >= 2 && !wait_or_abort(bar(B_KEMPTY + st), ((j >> 1) - 1) & 1, abort_flag)) {
         failed = true;
         break;
       }
-      mbar_expect_tx(bar(B_KVFULL0 + st), 2 * L::kKVBytes);
-      const uint32_t dk = sK0 + st * L::kKVBytes, dv = sV0 + st * L::kKVBytes;
+      mbar_expect_tx(bar(B_KFULL + st), L::kKVBytes);
 #pragma unroll
-      for (int h = 0; h < HD / 64; ++h) {
-        tma_load_3d(dk + h * (kBN * 128), &tm_k, bar(B_KVFULL0 + st), h * 64, kvh, j * kBN);
-        tma_load_3d(dv + h * (kBN * 128), &tm_v, bar(B_KVFULL0 + st), h * 64, kvh, j * kBN);
+      for (int h = 0; h < HD / 64; ++h)
+        tma_load_3d(sK0 + st * L::kKVBytes + h * (kBN * 128), &tm_k, bar(B_KFULL + st), h * 64, kvh,
+                    (j0 + j) * kBN);
+      last_k[st] = j;
+      if (j >= 2 && !wait_or_abort(bar(B_VEMPTY + st), ((j >> 1) - 1) & 1, abort_flag)) {
+        failed = true;
+        break;
       }
-      last_armed[st] = j;
+      mbar_expect_tx(bar(B_VFULL + st), L::kKVBytes);
+#pragma unroll
+      for (int h = 0; h < HD / 64; ++h)
+        tma_load_3d(sV0 + st * L::kKVBytes + h * (kBN * 128), &tm_v, bar(B_VFULL + st), h * 64, kvh,
+                    (j0 + j) * kBN);
+      last_v[st] = j;
     }
     // Drain: every armed copy must land before the CTA can retire.
     if (!mbar_wait(bar(B_Q), 0)) failed = true;
-    for (int st = 0; st < 2; ++st)
-      if (last_armed[st] >= 0 && !mbar_wait(bar(B_KVFULL0 + st), (last_armed[st] >> 1) & 1))
-        failed = true;
+    for (int st = 0; st < 2; ++st) {
+      if (last_k[st] >= 0 && !mbar_wait(bar(B_KFULL + st), (last_k[st] >> 1) & 1)) failed = true;
+      if (last_v[st] >= 0 && !mbar_wait(bar(B_VFULL + st), (last_v[st] >> 1) & 1)) failed = true;
+    }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------- MMA issuer
     const uint32_t idesc_s = umma_idesc_f16(DT, kBM, kBN, 0);
     const uint32_t idesc_o = umma_idesc_f16(DT, kBM, HD, 1);
-    auto issue_s = [&](int j) {
-      const int st = j & 1;
-      const uint32_t kb = sK0 + st * L::kKVBytes;
+    auto issue_s = [&](int t, int j) {
+      const uint32_t kb = sK0 + (j & 1) * L::kKVBytes;
+      const uint32_t qb = sQ + t * L::kQBytes;
 #pragma unroll
       for (int kk = 0; kk < HD / 16; ++kk) {
         const uint32_t off = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
         const uint32_t offk = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
-        umma_f16_ss(tS, umma_desc_sw128(sQ + off, 16, 1024), umma_desc_sw128(kb + offk, 16, 1024),
-                    idesc_s, kk > 0 ? 1u : 0u);
+        umma_f16_ss(tmem + 256 * t, umma_desc_sw128(qb + off, 16, 1024),
+                    umma_desc_sw128(kb + offk, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
       }
-      umma_commit(bar(B_SFULL));
+      umma_commit(bar(B_SFULL + t));
+    };
+    auto issue_pv = [&](int t, int j) {
+      const uint32_t vb = sV0 + (j & 1) * L::kKVBytes;
+#pragma unroll
+      for (int kk = 0; kk < kBN / 16; ++kk)
+        umma_f16_ts(tmem + 256 * t + kBN, tmem + 256 * t + kk * 8,
+                    umma_desc_sw128(vb + kk * 16 * 128, kBN * 128, 1024), idesc_o,
+                    (j > 0 || kk > 0) ? 1u : 0u);
     };
     do {
-      if (!wait_or_abort(bar(B_Q), 0, abort_flag) ||
-          !wait_or_abort(bar(B_KVFULL0), 0, abort_flag)) { failed = true; break; }
+      if (!wait_or_abort(bar(B_Q), 0, abort_flag) || !wait_or_abort(bar(B_KFULL), 0, abort_flag)) {
+        failed = true;
+        break;
+      }
       tc_fence_after();
-      issue_s(0);
-      for (int j = 0; j < n_kv; ++j) {
-        if (j + 1 < n_kv) {
-          const int st1 = (j + 1) & 1;
-          if (!wait_or_abort(bar(B_KVFULL0 + st1), ((j + 1) >> 1) & 1, abort_flag) ||
-              !wait_or_abort(bar(B_SFREE), j & 1, abort_flag)) { failed = true; break; }
+      if (n_kv0 > 0) issue_s(0, 0);
+      if (n_kv1 > 0) issue_s(1, 0);
+      umma_commit(bar(B_KEMPTY));
+      for (int j = 0; j < n_all && !failed; ++j) {
+        const bool next_k = (j + 1 < n_kv0) || (j + 1 < n_kv1);
+        if (next_k && !wait_or_abort(bar(B_KFULL + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag)) {
+          failed = true;
+          break;
+        }
+        if (!wait_or_abort(bar(B_VFULL + (j & 1)), (j >> 1) & 1, abort_flag)) {
+          failed = true;
+          break;
+        }
+        for (int t = 0; t < 2; ++t) {
+          const int n_t = t ? n_kv1 : n_kv0;
+          if (j >= n_t) continue;
+          if (!wait_or_abort(bar(B_PFULL + t), j & 1, abort_flag)) {
+            failed = true;
+            break;
+          }
           tc_fence_after();
-          issue_s(j + 1);
+          issue_pv(t, j);
+          if (j + 1 < n_t) issue_s(t, j + 1);
+          else umma_commit(bar(B_ODONE + t));
         }
-        if (!wait_or_abort(bar(B_PFULL), j & 1, abort_flag)) { failed = true; break; }
-        tc_fence_after();
-        const uint32_t vb = sV0 + (j & 1) * L::kKVBytes;
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint32_t offp = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-          umma_f16_ss(tO, umma_desc_sw128(sP + offp, 16, 1024),
-                      umma_desc_sw128(vb + kk * 16 * 128, kBN * 128, 1024), idesc_o,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(bar(B_ODONE));
-        umma_commit(bar(B_KVEMPTY0 + (j & 1)));
+        umma_commit(bar(B_VEMPTY + (j & 1)));
+        if (next_k) umma_commit(bar(B_KEMPTY + ((j + 1) & 1)));
       }
     } while (false);
     // Drain: all MMAs issued by this thread complete before TMEM is released.
@@ -198,39 +285,40 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     if (!mbar_wait(bar(B_DRAIN), 0)) failed = true;
   } else if (warp >= 4) {
     // ----------------------------------------------- softmax + epilogue warps
+    const int t = (warp - 4) >> 2;            // Q tile of this warpgroup
     const int sub = warp & 3;
     const int row = sub * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
-    const int64_t tok = tok0 + row / prm.group;
-    const bool row_valid = tok < tok_end;
-    const int64_t p_row = row_valid ? prm.pos[tok] : p_max;
+    const uint32_t tS = tmem + 256 * t + lane_off, tO = tS + kBN;
+    int64_t t_tok0, t_tok_end, t_pmax;
+    const int n_t = geom(t, t_tok0, t_tok_end, t_pmax);
+    const int64_t tok = t_tok0 + row / prm.group;
+    const bool row_valid = tok < t_tok_end;
+    const int64_t p_row = row_valid ? prm.pos[tok] : t_pmax;
     float m_used = -INFINITY, l_sum = 0.f;
     const float sl2 = prm.scale_log2;
-    uint8_t* prow = sbase + L::kP + row * 128;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!__all_sync(0xffffffffu, wait_or_abort(bar(B_SFULL), j & 1, abort_flag))) {
+    for (int j = 0; j < n_t; ++j) {
+      if (!__all_sync(0xffffffffu, wait_or_abort(bar(B_SFULL + t), j & 1, abort_flag))) {
         failed = true;
         break;
       }
       tc_fence_after();
+      // keys (j0 + j)*kBN + c are visible to this row iff c <= lim
+      const int64_t lim64 = p_row - static_cast<int64_t>(j0 + j) * kBN;
+      const int lim = lim64 >= kBN ? kBN : static_cast<int>(lim64);
+      // the whole S row in registers: four loads in flight, one wait
       uint32_t s[kBN];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c)
-        tmem_ld32(tS + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+      for (int c4 = 0; c4 < kBN / 32; ++c4)
+        tmem_ld32(tS + c4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c4 * 32]));
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_SFREE));
-      // causal limit inside this tile: keys j*kBN + c valid iff <= p_row
-      const int64_t lim64 = p_row - static_cast<int64_t>(j) * kBN;
-      const int lim = lim64 >= kBN ? kBN : static_cast<int>(lim64);   // keys c <= lim are visible
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kBN; ++c)
         if (c <= lim) mx = fmaxf(mx, __uint_as_float(s[c]));
       const float m_tile = mx * sl2;
-      bool rescale = false;
       float alpha = 1.f;
+      bool rescale = false;
       if (j == 0) {
         m_used = m_tile;
       } else if (m_tile > m_used + 8.f) {
@@ -240,67 +328,76 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       float rs = 0.f;
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) {
-        const float p = (c <= lim) ? ex2(__uint_as_float(s[c]) * sl2 - m_used) : 0.f;
-        s[c] = __float_as_uint(p);
-        rs += p;
+      for (int c4 = 0; c4 < kBN / 32; ++c4) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int c = c4 * 32 + 2 * e;
+          const float p0 = (c <= lim) ? ex2(__uint_as_float(s[c]) * sl2 - m_used) : 0.f;
+          const float p1 = (c + 1 <= lim) ? ex2(__uint_as_float(s[c + 1]) * sl2 - m_used) : 0.f;
+          rs += p0 + p1;
+          pk[e] = pack2<DT>(p0, p1);
+        }
+        // P chunk c4 -> columns [16 c4, 16 c4 + 16) (S was read completely above)
+        tmem_st16(tS + c4 * 16, pk);
       }
       l_sum = l_sum * alpha + rs;
-      if (j > 0) {
-        if (!__all_sync(0xffffffffu, wait_or_abort(bar(B_ODONE), (j - 1) & 1, abort_flag))) {
-          failed = true;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + lane_off + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(tO + lane_off + c * 32, o);
-          }
-          tmem_wait_st();
-        }
-      }
-      // P (16-bit) into the K-major, 128-byte-swizzled operand tile
-#pragma unroll
-      for (int ch = 0; ch < kBN / 8; ++ch) {
-        uint4 v;
-        uint16_t* h = reinterpret_cast<uint16_t*>(&v);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) h[e] = Elem<DT>::from_f(__uint_as_float(s[ch * 8 + e]));
-        const int sub_tile = ch >> 3, cc = ch & 7;
-        *reinterpret_cast<uint4*>(prow + sub_tile * (kBM * 128) + ((cc ^ (row & 7)) << 4)) = v;
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_PFULL));
-    }
-    if (!failed) {
-      if (!__all_sync(0xffffffffu, wait_or_abort(bar(B_ODONE), (n_kv - 1) & 1, abort_flag))) {
-        failed = true;
-      } else {
-        tc_fence_after();
-        const float inv_l = 1.f / l_sum;
-        const int hq = kvh * prm.group + row % prm.group;
-        uint16_t* orow = prm.out + (tok * prm.n_q_heads + hq) * static_cast<int64_t>(HD);
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O is stable: the commit behind this tile's S(j) covered PV(j-1)
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
           uint32_t o[32];
-          tmem_ld32(tO + lane_off + c * 32, o);
+          tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
-          if (row_valid) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 v;
-              uint16_t* h = reinterpret_cast<uint16_t*>(&v);
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_PFULL + t));
+    }
+    if (!failed && n_t > 0) {
+      if (!__all_sync(0xffffffffu, wait_or_abort(bar(B_ODONE + t), 0, abort_flag))) {
+        failed = true;
+      } else {
+        tc_fence_after();
+        const int slot0 = prm.tile_base[kvh * prm.n_tiles + 2 * pair + t];
+        if (slot0 >= 0) {
+          // split tile: unnormalised partial O, running max and row sum of this chunk
+          const int64_t slot = slot0 + chunk;
+          float* po = prm.part_o + (slot * kBM + row) * HD;
 #pragma unroll
-              for (int e = 0; e < 8; ++e) h[e] = Elem<DT>::from_f(__uint_as_float(o[q * 8 + e]) * inv_l);
-              st_vec(orow + c * 32 + q * 8, v);
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              *reinterpret_cast<uint4*>(po + c * 32 + q * 4) =
+                  make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+          }
+          prm.part_ml[slot * kBM + row] = make_float2(m_used, l_sum);
+        } else {
+          const float inv_l = 1.f / l_sum;
+          const int hq = kvh * prm.group + row % prm.group;
+          uint16_t* orow = prm.out + (tok * prm.n_q_heads + hq) * static_cast<int64_t>(HD);
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+            if (row_valid) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint4 v;
+                uint16_t* h = reinterpret_cast<uint16_t*>(&v);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) h[e] = Elem<DT>::from_f(__uint_as_float(o[q * 8 + e]) * inv_l);
+                st_vec(orow + c * 32 + q * 8, v);
+              }
             }
           }
         }
@@ -321,7 +418,199 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 }
 
 // ---------------------------------------------------------------------------
-// host side: tensor maps + launch
+// Work plan (one CTA).  Key tiles of a Q-tile pair are split into chunks of at
+// most C tiles, C = max(4, ceil(total / target_items)), where total counts the
+// (pair, key tile) iterations of all KV heads; items are ordered longest first
+// (the block scheduler starts CTAs roughly in index order).  A tile whose key
+// range spans more than one chunk gets consecutive partial slots (tile_base).
+// ---------------------------------------------------------------------------
+constexpr int kPlanThreads = 1024;
+
+// exclusive prefix sum over the block (1024 threads); *total receives the sum
+__device__ int block_excl_scan(int v, int* s_warp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = s_warp[lane];
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    s_warp[lane] = wi - w;           // exclusive warp offsets
+    if (lane == 31) s_warp[32] = wi;  // block total
+  }
+  __syncthreads();
+  const int r = s_warp[warp] + x - v;
+  *total = s_warp[32];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kPlanThreads, 1)
+attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_tile, int n_tiles,
+                 int n_kv_heads, int target_items, int min_chunk, int max_items, int max_slots,
+                 AttnPlanHeader* hdr, int4* items, int* tile_base, int32_t* status) {
+  __shared__ int s_hist[kMaxKvTiles + 1];
+  __shared__ int s_warp[33];
+  __shared__ unsigned long long s_total;
+  __shared__ int s_max;
+  __shared__ int s_error;
+  const int tid = threadIdx.x;
+  const int n_pairs = (n_tiles + 1) / 2;
+  if (tid == 0) {
+    s_total = 0;
+    s_max = 0;
+    s_error = 0;
+  }
+  for (int i = tid; i <= kMaxKvTiles; i += kPlanThreads) s_hist[i] = 0;
+  __syncthreads();
+  auto pair_tiles = [&](int p) {   // the later tile of a pair has the larger key range
+    return tile_key_tiles(pos, n_sel, tok_per_tile, min(2 * p + 1, n_tiles - 1));
+  };
+  // 1. key-tile iterations of all pairs
+  unsigned long long local = 0;
+  int local_max = 0;
+  for (int p = tid; p < n_pairs; p += kPlanThreads) {
+    const int n = pair_tiles(p);
+    local += n;
+    local_max = max(local_max, n);
+  }
+  atomicAdd(&s_total, local);
+  atomicMax(&s_max, local_max);
+  __syncthreads();
+  const unsigned long long total = s_total * static_cast<unsigned long long>(n_kv_heads);
+  int C = static_cast<int>((total + target_items - 1) / target_items);
+  C = max(C, min_chunk);
+  if (tid == 0 && s_max > kMaxKvTiles) s_error = 1;
+  // 2. item lengths -> histogram (identical for every KV head)
+  for (int p = tid; p < n_pairs; p += kPlanThreads) {
+    const int n = min(pair_tiles(p), kMaxKvTiles);
+    const int full = n / C, rem = n % C;
+    if (full) atomicAdd(&s_hist[min(C, kMaxKvTiles)], full * n_kv_heads);
+    if (rem) atomicAdd(&s_hist[rem], n_kv_heads);
+  }
+  __syncthreads();
+  // 3. offsets in descending length order: thread i owns the kPerThread lengths
+  //    kMaxKvTiles - kPerThread*i - r (r = 0 ..), down to length 0
+  {
+    constexpr int kPerThread = (kMaxKvTiles + 1 + kPlanThreads - 1) / kPlanThreads;
+    int cnt[kPerThread];
+    int mine = 0;
+#pragma unroll
+    for (int r = 0; r < kPerThread; ++r) {
+      const int len = kMaxKvTiles - kPerThread * tid - r;
+      cnt[r] = len >= 0 ? s_hist[len] : 0;
+      mine += cnt[r];
+    }
+    int tot;
+    int off = block_excl_scan(mine, s_warp, &tot);
+#pragma unroll
+    for (int r = 0; r < kPerThread; ++r) {
+      const int len = kMaxKvTiles - kPerThread * tid - r;
+      if (len >= 0) s_hist[len] = off;
+      off += cnt[r];
+    }
+    if (tid == 0) {
+      if (tot > max_items) s_error = 1;
+      hdr->n_items = tot;
+    }
+  }
+  __syncthreads();
+  // 4. emit items (order inside one length class is arbitrary)
+  for (int p = tid; p < n_pairs; p += kPlanThreads) {
+    const int n = min(pair_tiles(p), kMaxKvTiles);
+    const int nc = (n + C - 1) / C;
+    for (int h = 0; h < n_kv_heads; ++h)
+      for (int c = 0; c < nc; ++c) {
+        const int len = min(C, n - c * C);
+        const int at = atomicAdd(&s_hist[min(len, kMaxKvTiles)], 1);
+        if (at < max_items) items[at] = make_int4(h, p, c, len);
+      }
+  }
+  // 5. partial slots of split tiles, in (head, tile) order
+  int carry = 0;
+  const int n_all = n_kv_heads * n_tiles;
+  for (int b0 = 0; b0 < n_all; b0 += kPlanThreads) {
+    const int i = b0 + tid;
+    int cnt = 0;
+    if (i < n_all) {
+      const int nc = (tile_key_tiles(pos, n_sel, tok_per_tile, i % n_tiles) + C - 1) / C;
+      cnt = nc > 1 ? nc : 0;
+    }
+    int tot;
+    const int off = block_excl_scan(cnt, s_warp, &tot);
+    if (i < n_all) tile_base[i] = cnt ? carry + off : -1;
+    carry += tot;
+  }
+  if (tid == 0) {
+    if (carry > max_slots) s_error = 1;
+    hdr->chunk = C;
+    hdr->n_slots = carry;
+    hdr->error = s_error;
+    if (s_error) report(status, CBK_STATUS_COUNT);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Merge the partial results of split tiles: one thread per row,
+// O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
+// ---------------------------------------------------------------------------
+template <int DT, int HD>
+__global__ void __launch_bounds__(kBM)
+attn_combine_kernel(const AttnParams prm) {
+  const int tile = blockIdx.x, kvh = blockIdx.y, row = threadIdx.x;
+  if (prm.plan->error) return;
+  const int slot0 = prm.tile_base[kvh * prm.n_tiles + tile];
+  if (slot0 < 0) return;
+  const int64_t tok = static_cast<int64_t>(tile) * prm.tok_per_tile + row / prm.group;
+  if (tok >= prm.n_sel) return;
+  const int C = prm.plan->chunk;
+  const int nc = (tile_key_tiles(prm.pos, prm.n_sel, prm.tok_per_tile, tile) + C - 1) / C;
+  float M = -INFINITY;
+  for (int c = 0; c < nc; ++c) M = fmaxf(M, prm.part_ml[(static_cast<int64_t>(slot0) + c) * kBM + row].x);
+  float acc[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) acc[d] = 0.f;
+  float Lsum = 0.f;
+  for (int c = 0; c < nc; ++c) {
+    const int64_t slot = slot0 + c;
+    const float2 ml = prm.part_ml[slot * kBM + row];
+    const float w = ex2(ml.x - M);       // a chunk without visible keys has m = -inf -> 0
+    Lsum += ml.y * w;
+    const float4* po = reinterpret_cast<const float4*>(prm.part_o + (slot * kBM + row) * HD);
+#pragma unroll
+    for (int q = 0; q < HD / 4; ++q) {
+      const float4 v = po[q];
+      acc[4 * q] += v.x * w;
+      acc[4 * q + 1] += v.y * w;
+      acc[4 * q + 2] += v.z * w;
+      acc[4 * q + 3] += v.w * w;
+    }
+  }
+  const float inv = 1.f / Lsum;
+  const int hq = kvh * prm.group + row % prm.group;
+  uint16_t* orow = prm.out + (tok * prm.n_q_heads + hq) * static_cast<int64_t>(HD);
+#pragma unroll
+  for (int q = 0; q < HD / 8; ++q) {
+    uint4 v;
+    uint16_t* h = reinterpret_cast<uint16_t*>(&v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = Elem<DT>::from_f(acc[8 * q + e] * inv);
+    st_vec(orow + q * 8, v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side: tensor maps, workspace layout, launch
 // ---------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -356,43 +645,95 @@ static int make_map(CUtensorMap* m, const void* ptr, int dtype, uint64_t d0, uin
 
 int ensure_smem_attr(const void* func, int bytes);   // cbk_api.cu
 
+static int sm_count() {
+  static int cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+// Workspace layout of one partial-attention call (all offsets 256-byte aligned).
+struct AttnLayout {
+  int tok_per_tile, n_tiles, n_pairs, target, min_chunk, max_items, max_slots;
+  size_t off_items, off_tile_base, off_ml, off_o, bytes;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int head_dim) {
+  AttnLayout a;
+  const int G = n_q_heads / n_kv_heads;
+  a.tok_per_tile = kBM / G;
+  a.n_tiles = static_cast<int>((n_sel + a.tok_per_tile - 1) / a.tok_per_tile);
+  a.n_pairs = (a.n_tiles + 1) / 2;
+  a.target = 2 * sm_count();
+  a.min_chunk = 4;
+  // items <= total / C + pairs <= target + pairs (C >= total / target)
+  a.max_items = a.target + n_kv_heads * a.n_pairs;
+  // split tiles span more than C key tiles each, so their slots number < 4 * total / C <= 4 * target
+  a.max_slots = 4 * a.target + 2;
+  a.off_items = align256(sizeof(AttnPlanHeader));
+  a.off_tile_base = a.off_items + align256(static_cast<size_t>(a.max_items) * sizeof(int4));
+  a.off_ml = a.off_tile_base + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int));
+  a.off_o = a.off_ml + align256(static_cast<size_t>(a.max_slots) * kBM * sizeof(float2));
+  a.bytes = a.off_o + static_cast<size_t>(a.max_slots) * kBM * head_dim * sizeof(float);
+  return a;
+}
+
 template <int DT, int HD>
 static int launch_attn(const void* q, const void* k, const void* v, const int64_t* pos,
                        int64_t n_sel, int64_t S, int n_q_heads, int n_kv_heads, float scale,
-                       void* out, int32_t* status, cudaStream_t st) {
+                       void* out, void* workspace, int reuse_plan, int32_t* status, cudaStream_t st) {
   const int G = n_q_heads / n_kv_heads;
+  const AttnLayout lay = attn_layout(n_sel, n_q_heads, n_kv_heads, HD);
   CUtensorMap mq, mk, mv;
   if (int rc = make_map(&mq, q, DT, HD, n_q_heads, n_sel, G, kBM / G)) return rc;
   if (int rc = make_map(&mk, k, DT, HD, n_kv_heads, S, 1, kBN)) return rc;
   if (int rc = make_map(&mv, v, DT, HD, n_kv_heads, S, 1, kBN)) return rc;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
   AttnParams prm;
   prm.pos = pos;
   prm.out = static_cast<uint16_t*>(out);
   prm.status = status;
+  prm.plan = reinterpret_cast<const AttnPlanHeader*>(ws);
+  prm.items = reinterpret_cast<const int4*>(ws + lay.off_items);
+  prm.tile_base = reinterpret_cast<const int*>(ws + lay.off_tile_base);
+  prm.part_ml = reinterpret_cast<float2*>(ws + lay.off_ml);
+  prm.part_o = reinterpret_cast<float*>(ws + lay.off_o);
   prm.n_sel = n_sel;
   prm.n_q_heads = n_q_heads;
   prm.group = G;
-  prm.tok_per_tile = kBM / G;
-  prm.n_tiles = static_cast<int>((n_sel + prm.tok_per_tile - 1) / prm.tok_per_tile);
+  prm.tok_per_tile = lay.tok_per_tile;
+  prm.n_tiles = lay.n_tiles;
   prm.scale_log2 = scale * 1.4426950408889634f;
+  if (!reuse_plan) {
+    attn_plan_kernel<<<1, kPlanThreads, 0, st>>>(
+        pos, n_sel, lay.tok_per_tile, lay.n_tiles, n_kv_heads, lay.target, lay.min_chunk,
+        lay.max_items, lay.max_slots, reinterpret_cast<AttnPlanHeader*>(ws),
+        reinterpret_cast<int4*>(ws + lay.off_items), reinterpret_cast<int*>(ws + lay.off_tile_base),
+        status);
+    if (int rc = check_launch("attn_plan_kernel")) return rc;
+  }
   auto kern = partial_attn_kernel<DT, HD>;
   const int smem = AttnSmem<HD>::kAlloc;
   if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem)) return rc;
-  dim3 grid(static_cast<unsigned>(prm.n_tiles), static_cast<unsigned>(n_kv_heads));
-  kern<<<grid, kThreads, smem, st>>>(mq, mk, mv, prm);
-  return check_launch("partial_attn_kernel");
+  kern<<<static_cast<unsigned>(lay.max_items), kThreads, smem, st>>>(mq, mk, mv, prm);
+  if (int rc = check_launch("partial_attn_kernel")) return rc;
+  attn_combine_kernel<DT, HD><<<dim3(static_cast<unsigned>(lay.n_tiles), static_cast<unsigned>(n_kv_heads)),
+                                kBM, 0, st>>>(prm);
+  return check_launch("attn_combine_kernel");
 }
 
 }  // namespace cbk
 
 using namespace cbk;
 
-extern "C" int cbk_partial_attn(const void* q, const void* k, const void* v, const int64_t* pos,
-                                int64_t n_sel, int64_t S, int n_q_heads, int n_kv_heads,
-                                int head_dim, float scale, int dtype, void* out, int32_t* status,
-                                void* stream) {
-  if (dtype != CBK_BF16 && dtype != CBK_F16)
-    return set_error(CBK_ERR_UNSUPPORTED, "cbk_partial_attn: dtype %d not supported", dtype);
+static int check_attn_geometry(int n_q_heads, int n_kv_heads, int head_dim, int64_t n_sel, int64_t S) {
   if (head_dim != 64 && head_dim != 128)
     return set_error(CBK_ERR_UNSUPPORTED, "cbk_partial_attn: head_dim %d (64 or 128 only)", head_dim);
   if (n_kv_heads <= 0 || n_q_heads <= 0 || n_q_heads % n_kv_heads != 0)
@@ -400,22 +741,41 @@ extern "C" int cbk_partial_attn(const void* q, const void* k, const void* v, con
   const int G = n_q_heads / n_kv_heads;
   if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16)
     return set_error(CBK_ERR_UNSUPPORTED, "cbk_partial_attn: GQA group %d not in {1,2,4,8,16}", G);
-  if (!q || !k || !v || !pos || !out)
+  if (S <= 0 || n_sel < 0 || S > static_cast<int64_t>(kMaxKvTiles - 1) * kBN || n_sel > S)
+    return set_error(CBK_ERR_INVALID, "cbk_partial_attn: need 0 <= n_sel <= S <= %d (n_sel %lld, S %lld)",
+                     (kMaxKvTiles - 1) * kBN, (long long)n_sel, (long long)S);
+  return CBK_OK;
+}
+
+extern "C" size_t cbk_partial_attn_workspace_bytes(int64_t n_sel, int64_t S, int n_q_heads,
+                                                   int n_kv_heads, int head_dim) {
+  if (check_attn_geometry(n_q_heads, n_kv_heads, head_dim, n_sel, S) != CBK_OK) return 0;
+  return attn_layout(n_sel < 1 ? 1 : n_sel, n_q_heads, n_kv_heads, head_dim).bytes;
+}
+
+extern "C" int cbk_partial_attn(const void* q, const void* k, const void* v, const int64_t* pos,
+                                int64_t n_sel, int64_t S, int n_q_heads, int n_kv_heads,
+                                int head_dim, float scale, int dtype, void* out, void* workspace,
+                                size_t workspace_bytes, int reuse_plan, int32_t* status,
+                                void* stream) {
+  if (dtype != CBK_BF16 && dtype != CBK_F16)
+    return set_error(CBK_ERR_UNSUPPORTED, "cbk_partial_attn: dtype %d not supported", dtype);
+  if (int rc = check_attn_geometry(n_q_heads, n_kv_heads, head_dim, n_sel, S)) return rc;
+  if (!q || !k || !v || !pos || !out || !workspace)
     return set_error(CBK_ERR_INVALID, "cbk_partial_attn: null pointer argument");
-  if (S <= 0 || n_sel < 0 || S > (int64_t(1) << 31) || n_sel > (int64_t(1) << 31))
-    return set_error(CBK_ERR_INVALID, "cbk_partial_attn: bad sizes");
-  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
-       reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out)) & 15u)
-    return set_error(CBK_ERR_INVALID, "cbk_partial_attn: q/k/v/out must be 16-byte aligned");
-  if ((n_sel + (128 / G) - 1) / (128 / G) > 2147483647LL)
-    return set_error(CBK_ERR_INVALID, "cbk_partial_attn: too many tiles");
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(workspace)) & 15u)
+    return set_error(CBK_ERR_INVALID, "cbk_partial_attn: q/k/v/out/workspace must be 16-byte aligned");
   if (n_sel == 0) return CBK_OK;
+  const size_t need = attn_layout(n_sel, n_q_heads, n_kv_heads, head_dim).bytes;
+  if (workspace_bytes < need)
+    return set_error(CBK_ERR_WORKSPACE, "cbk_partial_attn: workspace %zu < %zu bytes", workspace_bytes, need);
   auto st = static_cast<cudaStream_t>(stream);
   if (dtype == CBK_BF16)
     return head_dim == 128
-               ? launch_attn<CBK_BF16, 128>(q, k, v, pos, n_sel, S, n_q_heads, n_kv_heads, scale, out, status, st)
-               : launch_attn<CBK_BF16, 64>(q, k, v, pos, n_sel, S, n_q_heads, n_kv_heads, scale, out, status, st);
+               ? launch_attn<CBK_BF16, 128>(q, k, v, pos, n_sel, S, n_q_heads, n_kv_heads, scale, out, workspace, reuse_plan, status, st)
+               : launch_attn<CBK_BF16, 64>(q, k, v, pos, n_sel, S, n_q_heads, n_kv_heads, scale, out, workspace, reuse_plan, status, st);
   return head_dim == 128
-             ? launch_attn<CBK_F16, 128>(q, k, v, pos, n_sel, S, n_q_heads, n_kv_heads, scale, out, status, st)
-             : launch_attn<CBK_F16, 64>(q, k, v, pos, n_sel, S, n_q_heads, n_kv_heads, scale, out, status, st);
+             ? launch_attn<CBK_F16, 128>(q, k, v, pos, n_sel, S, n_q_heads, n_kv_heads, scale, out, workspace, reuse_plan, status, st)
+             : launch_attn<CBK_F16, 64>(q, k, v, pos, n_sel, S, n_q_heads, n_kv_heads, scale, out, workspace, reuse_plan, status, st);
 }

@@ -165,11 +165,21 @@ int cbk_hkvd_select_noalloc(const void* k_new, int64_t new_row_stride, const cbk
  *   out[j][h] = softmax_t<=pos[j]( scale * q[j][h] . k[t][h/G] ) . v[t][h/G]
  * for j < n_sel, h < n_q_heads, G = n_q_heads / n_kv_heads, keys t in [0, pos[j]].
  * q: [n_sel][n_q_heads][head_dim]; k/v: [S][n_kv_heads][head_dim]; pos ascending
- * (int64), each in [0, S).  head_dim 64 or 128; G in {1,2,4,8,16}.
- * fp32 accumulation in TMEM, fp32 online softmax, 16-bit P and output. */
+ * (int64), distinct, each in [0, S).  head_dim 64 or 128; G in {1,2,4,8,16};
+ * S <= 262144.  fp32 accumulation in TMEM, fp32 online softmax, 16-bit P and
+ * output.  The key range of long query tiles is split across CTAs; a plan
+ * (computed on the device from pos) and the split partial results live in the
+ * caller's `workspace` (>= cbk_partial_attn_workspace_bytes(...) bytes, which
+ * depends on the current device's SM count).  With reuse_plan != 0 the plan
+ * already in `workspace` is reused: the caller guarantees the same pos, n_sel
+ * and head geometry as the call that built it (e.g. every sparse layer of one
+ * blended prefill).  Three launches: plan (unless reused), attention, combine. */
+size_t cbk_partial_attn_workspace_bytes(int64_t n_sel, int64_t S, int n_q_heads, int n_kv_heads,
+                                        int head_dim);
 int cbk_partial_attn(const void* q, const void* k, const void* v, const int64_t* pos,
                      int64_t n_sel, int64_t S, int n_q_heads, int n_kv_heads, int head_dim,
-                     float scale, int dtype, void* out, int32_t* status, void* stream);
+                     float scale, int dtype, void* out, void* workspace, size_t workspace_bytes,
+                     int reuse_plan, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -42,10 +42,13 @@ def test_abi_version_and_pure_helpers():
 @pytest.mark.parametrize("call,code", [
     ("cbk_topk_select(None, 10, 0, 0, None, None, None)", -1),
     ("cbk_topk_select(1024, 10, 11, 0, 2048, None, None)", -1),
-    ("cbk_partial_attn(16, 16, 16, 16, 4, 8, 4, 2, 96, 0.1, 0, 16, None, None)", -2),
-    ("cbk_partial_attn(16, 16, 16, 16, 4, 8, 12, 4, 128, 0.1, 0, 16, None, None)", -2),
-    ("cbk_partial_attn(16, 16, 16, 16, 4, 8, 4, 2, 128, 0.1, 7, 16, None, None)", -2),
-    ("cbk_partial_attn(16, 16, 16, 16, 4, 8, 5, 2, 128, 0.1, 0, 16, None, None)", -1),
+    ("cbk_partial_attn(16, 16, 16, 16, 4, 8, 4, 2, 96, 0.1, 0, 16, 16, 1 << 30, 0, None, None)", -2),
+    ("cbk_partial_attn(16, 16, 16, 16, 4, 8, 12, 4, 128, 0.1, 0, 16, 16, 1 << 30, 0, None, None)", -2),
+    ("cbk_partial_attn(16, 16, 16, 16, 4, 8, 4, 2, 128, 0.1, 7, 16, 16, 1 << 30, 0, None, None)", -2),
+    ("cbk_partial_attn(16, 16, 16, 16, 4, 8, 5, 2, 128, 0.1, 0, 16, 16, 1 << 30, 0, None, None)", -1),
+    ("cbk_partial_attn(16, 16, 16, 16, 9, 8, 4, 2, 128, 0.1, 0, 16, 16, 1 << 30, 0, None, None)", -1),
+    ("cbk_partial_attn(16, 16, 16, 16, 4, 8, 4, 2, 128, 0.1, 0, 16, None, 1 << 30, 0, None, None)", -1),
+    ("cbk_partial_attn(16, 16, 16, 16, 4, 8, 4, 2, 128, 0.1, 0, 16, 16, 64, 0, None, None)", -4),
     ("cbk_assemble_kv(None, None, 1, 1, 8, 2, 64, 0, None, 8, None, 0, None, None, 0, None, None)", -1),
     ("cbk_assemble_kv(16, 16, 1, 1, 8, 2, 40, 0, 16, 8, None, 0, 16, 16, 1024, None, None)", -2),
     ("cbk_rope_scatter(16, 8, 16, 8, 16, 8, 0, 16, 1, 8, 3, 2, 64, 0, 16, 8, 0, 16, 16, 16, None, None)", -1),

@@ -288,6 +288,7 @@ ATTN_CASES = [
     ("short", 100, 15, 4, 1, 128, "bf16"),
     ("one_row", 2000, 1, 8, 2, 128, "bf16"),
     ("f16_128", 1500, 225, 32, 8, 128, "f16"),
+    ("long_split", 20000, 2000, 32, 8, 128, "bf16"),
 ]
 
 
@@ -336,3 +337,22 @@ def test_partial_attention_repeatable(ops):
     a = ops.partial_attn(q, k, v, pos, Hq, Hkv, D, D ** -0.5)
     b = ops.partial_attn(q, k, v, pos, Hq, Hkv, D, D ** -0.5)
     assert torch.equal(a, b)
+
+
+def test_partial_attention_plan_reuse(ops):
+    """One plan (built from pos) serves every layer with the same selection: a
+    second layer's inputs with reuse_plan give the same bits as a fresh plan."""
+    g = torch.Generator().manual_seed(5)
+    S, n, Hq, Hkv, D = 6208, 931, 32, 8, 128
+    pos = torch.cat([torch.sort(torch.randperm(S - 1, generator=g)[:n - 1]).values,
+                     torch.tensor([S - 1])]).to(DEV)
+    layers = [tuple(rand16(sh, "bf16", g).to(DEV) for sh in ((n, Hq * D), (S, Hkv * D), (S, Hkv * D)))
+              for _ in range(2)]
+    ws = ops.attn_workspace(n, S, Hq, Hkv, D, DEV)
+    st = status_word()
+    a0 = ops.partial_attn(*layers[0], pos, Hq, Hkv, D, D ** -0.5, workspace=ws, reuse_plan=False, status=st)
+    a1 = ops.partial_attn(*layers[1], pos, Hq, Hkv, D, D ** -0.5, workspace=ws, reuse_plan=True, status=st)
+    b1 = ops.partial_attn(*layers[1], pos, Hq, Hkv, D, D ** -0.5)
+    assert_status_clean(st)
+    assert torch.equal(a1, b1)
+    assert not torch.equal(a0, a1)
