@@ -204,6 +204,7 @@ def run_ours(args):
     clk = clocks.stop()
     ms = max_over_ranks(t0.elapsed_time(t1))
     kern = TIMES.summary()
+    launch_counts = dict(TIMES.launches)
 
     # --- end to end through the public API (host ids in, first token out) -----
     pinned = [torch.tensor([t for c in chunks for t in c.token_ids], dtype=torch.int64).pin_memory()
@@ -229,11 +230,19 @@ def run_ours(args):
     D, Hq, Hkv, L = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.num_hidden_layers
     kv_dim = Hkv * D
     hbm_peak, tf_burst, tf_sust, peak_src = load_peaks()
-    n_attn, attn_ms = kern.get("partial_attn", (0, 0.0))
-    flops_step = attn_flops(idx_l, S, Hq, D, CHECK_LAYER, L)
-    per_launch_flops = flops_step / L
+    # attention: sparse layers (selected rows) and dense layers before the check layer
+    sel_sum = sum(int(p) + 1 for p in idx_l)
+    n_sp, ms_sp = kern.get("partial_attn", (0, 0.0))
+    n_de, ms_de = kern.get("partial_attn_dense", (0, 0.0))
+    fl_sp = 4 * Hq * D * sel_sum                       # per sparse-layer call
+    fl_de = 4 * Hq * D * (S * (S + 1) // 2)            # per dense-layer call
+    n_attn = n_sp + n_de
+    attn_ms = ms_sp + ms_de
+    per_launch_flops = (n_sp * fl_sp + n_de * fl_de) / max(n_attn, 1)
     attn_avg_ms = attn_ms / max(n_attn, 1)
     achieved_tf = per_launch_flops / (attn_avg_ms * 1e-3) / 1e12 if n_attn else None
+    tf_sp = fl_sp / (ms_sp / n_sp * 1e-3) / 1e12 if n_sp else None
+    tf_de = fl_de / (ms_de / n_de * 1e-3) / 1e12 if n_de else None
     n_asm, asm_ms = kern.get("assemble_kv", (0, 0.0))
     asm_bytes = (L - CHECK_LAYER) * 2 * 2 * S * kv_dim * 2        # read chunk K/V + write fused K/V
     n_hk, hk_ms = kern.get("hkvd_select", (0, 0.0))
@@ -249,7 +258,7 @@ def run_ours(args):
         except Exception:
             traffic = None
 
-    launches = sum(n for n, _ in kern.values())
+    launches = sum(launch_counts.values())
     res = {
         "metric": METRIC,
         "value": round(world * S * args.steps / (ms * 1e-3), 1),
@@ -276,19 +285,23 @@ def run_ours(args):
                      "peak": tf_sust, "unit": "TFLOP/s",
                      "frac": round(achieved_tf / tf_sust, 4) if achieved_tf else None,
                      "peak_kind": f"{peak_src} bf16 sustained (kernel timed inside a long step)",
-                     "flops_per_launch": per_launch_flops, "launches": n_attn,
+                     "flops_per_launch": per_launch_flops, "calls": n_attn,
                      "avg_launch_ms": round(attn_avg_ms, 5), "traffic": traffic},
         "kernels": {
-            "assemble_kv": {"launches": n_asm, "avg_ms": round(asm_ms / max(n_asm, 1), 4),
+            "assemble_kv": {"calls": n_asm, "avg_ms": round(asm_ms / max(n_asm, 1), 4),
                             "bytes": asm_bytes,
                             "GB/s": round(asm_bytes / (asm_ms / max(n_asm, 1) * 1e-3) / 1e9, 1) if n_asm else None,
                             "frac_hbm": round(asm_bytes / (asm_ms / max(n_asm, 1) * 1e-3) / 1e9 / hbm_peak, 3) if n_asm else None},
-            "hkvd_select": {"launches": n_hk, "avg_ms": round(hk_ms / max(n_hk / 2, 1), 4), "bytes": hk_bytes,
-                            "GB/s": round(hk_bytes / (hk_ms / max(n_hk / 2, 1) * 1e-3) / 1e9, 1) if n_hk else None},
-            "rope_scatter": {"launches": n_sc, "avg_ms": round(sc_ms / max(n_sc, 1), 4),
+            "hkvd_select": {"calls": n_hk, "avg_ms": round(hk_ms / max(n_hk, 1), 4), "bytes": hk_bytes,
+                            "GB/s": round(hk_bytes / (hk_ms / max(n_hk, 1) * 1e-3) / 1e9, 1) if n_hk else None},
+            "rope_scatter": {"calls": n_sc, "avg_ms": round(sc_ms / max(n_sc, 1), 4),
                              "bytes_sparse_layer": sc_bytes_sparse},
-            "partial_attn": {"launches": n_attn, "avg_ms": round(attn_avg_ms, 4),
-                             "TFLOP/s": round(achieved_tf, 1) if achieved_tf else None},
+            "partial_attn_sparse": {"calls": n_sp, "avg_ms": round(ms_sp / max(n_sp, 1), 4),
+                                    "flops_per_call": fl_sp,
+                                    "TFLOP/s": round(tf_sp, 1) if tf_sp else None},
+            "partial_attn_dense": {"calls": n_de, "avg_ms": round(ms_de / max(n_de, 1), 4),
+                                   "flops_per_call": fl_de,
+                                   "TFLOP/s": round(tf_de, 1) if tf_de else None},
             "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_src,
         },
         "gpu_launches": launches,
@@ -529,10 +542,14 @@ def run_attn_layers(args):
     from cacheblend import ops
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    S, k, Hq, Hkv, D, L = 6208, 931, 32, 8, 128, args.attn_layers
+    S, k, Hq, Hkv, D, L = 6208, min(args.attn_k, 6208), 32, 8, 128, args.attn_layers
     g = torch.Generator(device=device).manual_seed(0)
     gc = torch.Generator().manual_seed(0)
-    pos = torch.cat([torch.sort(torch.randperm(S - 1, generator=gc)[:k - 1]).values, torch.tensor([S - 1])]).to(device)
+    if k == S:
+        pos = torch.arange(S, device=device)
+    else:
+        pos = torch.cat([torch.sort(torch.randperm(S - 1, generator=gc)[:k - 1]).values,
+                         torch.tensor([S - 1])]).to(device)
     kc = torch.randn((L, S, Hkv * D), generator=g, device=device).to(torch.bfloat16)
     vc = torch.randn((L, S, Hkv * D), generator=g, device=device).to(torch.bfloat16)
     q = torch.randn((L, k, Hq * D), generator=g, device=device).to(torch.bfloat16)
@@ -573,6 +590,7 @@ def main():
     ap.add_argument("--workload", default="mistral7b-7k-blend",
                     choices=["mistral7b-7k-blend", "kv-microbench", "attn-layers"])
     ap.add_argument("--attn-layers", type=int, default=31)
+    ap.add_argument("--attn-k", type=int, default=931, help="selected rows (6208 = dense causal)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -37,7 +37,7 @@ class KernelTimes:
 
     def summary(self):
         torch.cuda.synchronize()
-        return {n: (self.launches[n], sum(a.elapsed_time(b) for a, b in ev)) for n, ev in self.spans.items()}
+        return {n: (len(ev), sum(a.elapsed_time(b) for a, b in ev)) for n, ev in self.spans.items()}
 
 
 TIMES = KernelTimes()

@@ -122,7 +122,8 @@ class _Geometry:
         self.scaling = float(attn0.scaling)
 
 
-def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_mode, ws, reuse):
+def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_mode, ws, reuse,
+                     tag=""):
     """q/k/v projections -> (b)+(d) RoPE + scatter into the fused cache ->
     (e) partial attention -> o_proj.  Returns the attention output rows."""
     attn = layer.self_attn
@@ -132,7 +133,7 @@ def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_
     q_rot = ops.rope_scatter(q[0], k_pre[0], v[0], pos, gather, S, geo.n_q, geo.n_kv, geo.head_dim,
                              rope, kc, vc, mode=rope_mode, status=status)
     a = ops.partial_attn(q_rot, kc, vc, pos, geo.n_q, geo.n_kv, geo.head_dim, geo.scaling,
-                         status=status, workspace=ws, reuse_plan=reuse)
+                         status=status, workspace=ws, reuse_plan=reuse, timer_tag=tag)
     return attn.o_proj(a.unsqueeze(0)), k_pre
 
 
@@ -218,7 +219,8 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
         for li in range(ck):                                  # dense layers (one shared plan)
             layer = inner.layers[li]
             a, _ = _attention_block(layer, geo, layer.input_layernorm(h), pos_all, S, rope,
-                                    fused_k[li], fused_v[li], False, status, rope_mode, ws_dense, li > 0)
+                                    fused_k[li], fused_v[li], False, status, rope_mode, ws_dense, li > 0,
+                                    tag="_dense")
             h = _mlp_block(layer, h + a)
 
         # check layer: full projections, HKVD, then sparse from here on

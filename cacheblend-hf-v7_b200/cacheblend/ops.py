@@ -265,7 +265,7 @@ def attn_workspace(n_sel: int, S: int, n_q_heads: int, n_kv_heads: int, head_dim
 def partial_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor,
                  n_q_heads: int, n_kv_heads: int, head_dim: int, scale: float,
                  out: torch.Tensor | None = None, status=None, workspace: torch.Tensor | None = None,
-                 reuse_plan: bool = False) -> torch.Tensor:
+                 reuse_plan: bool = False, timer_tag: str = "") -> torch.Tensor:
     """softmax(scale q k^T, keys <= pos) v for selected rows.
 
     q: [n_sel][Hq*D] (rotated); k_cache/v_cache: [S][Hkv*D]; pos: int64 [n_sel]
@@ -282,7 +282,7 @@ def partial_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
     if workspace is None:
         workspace = attn_workspace(n_sel, S, n_q_heads, n_kv_heads, head_dim, dev)
         reuse_plan = False
-    with TIMES.span("partial_attn", dev):
+    with TIMES.span("partial_attn" + timer_tag, dev, 2 if reuse_plan else 3):   # plan, attention, combine
         N.check(N.LIB.cbk_partial_attn(_vp(q), _vp(k_cache), _vp(v_cache), _vp(pos), n_sel, S,
                                        n_q_heads, n_kv_heads, head_dim, float(scale),
                                        dtype_code(q.dtype), _vp(out), _vp(workspace), workspace.numel(),

@@ -78,7 +78,7 @@ struct AttnParams {
   const AttnPlanHeader* plan;
   const int4* items;      // (kv head, tile pair, chunk, length) longest first
   const int* tile_base;   // [Hkv][n_tiles]: first partial slot of a split tile, -1 if not split
-  float* part_o;          // [slot][128][HD] unnormalised O
+  __half* part_o;         // [slot][128][HD] O / l of the chunk (fp16, bounded by |V|)
   float2* part_ml;        // [slot][128] (running max in log2 units, row sum)
   int64_t n_sel;
   int n_q_heads;
@@ -98,9 +98,16 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, vol
   }
 }
 
+// two fp32 -> one packed 16-bit pair (lo in the low half), one conversion instruction
 template <int DT>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  return static_cast<uint32_t>(Elem<DT>::from_f(lo)) | (static_cast<uint32_t>(Elem<DT>::from_f(hi)) << 16);
+  if constexpr (DT == CBK_BF16) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  } else {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
 }
 
 // number of 128-key tiles a Q tile needs (its last token has the largest position)
@@ -312,10 +319,17 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       for (int c4 = 0; c4 < kBN / 32; ++c4)
         tmem_ld32(tS + c4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c4 * 32]));
       tmem_wait_ld();
+      // whole tile visible to every row of the warp: no masking work
+      const bool full = __all_sync(0xffffffffu, lim >= kBN - 1);
       float mx = -INFINITY;
+      if (full) {
 #pragma unroll
-      for (int c = 0; c < kBN; ++c)
-        if (c <= lim) mx = fmaxf(mx, __uint_as_float(s[c]));
+        for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < kBN; ++c)
+          if (c <= lim) mx = fmaxf(mx, __uint_as_float(s[c]));
+      }
       const float m_tile = mx * sl2;
       float alpha = 1.f;
       bool rescale = false;
@@ -330,13 +344,24 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 #pragma unroll
       for (int c4 = 0; c4 < kBN / 32; ++c4) {
         uint32_t pk[16];
+        if (full) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int c = c4 * 32 + 2 * e;
-          const float p0 = (c <= lim) ? ex2(__uint_as_float(s[c]) * sl2 - m_used) : 0.f;
-          const float p1 = (c + 1 <= lim) ? ex2(__uint_as_float(s[c + 1]) * sl2 - m_used) : 0.f;
-          rs += p0 + p1;
-          pk[e] = pack2<DT>(p0, p1);
+          for (int e = 0; e < 16; ++e) {
+            const int c = c4 * 32 + 2 * e;
+            const float p0 = ex2(__uint_as_float(s[c]) * sl2 - m_used);
+            const float p1 = ex2(__uint_as_float(s[c + 1]) * sl2 - m_used);
+            rs += p0 + p1;
+            pk[e] = pack2<DT>(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int c = c4 * 32 + 2 * e;
+            const float p0 = (c <= lim) ? ex2(__uint_as_float(s[c]) * sl2 - m_used) : 0.f;
+            const float p1 = (c + 1 <= lim) ? ex2(__uint_as_float(s[c + 1]) * sl2 - m_used) : 0.f;
+            rs += p0 + p1;
+            pk[e] = pack2<DT>(p0, p1);
+          }
         }
         // P chunk c4 -> columns [16 c4, 16 c4 + 16) (S was read completely above)
         tmem_st16(tS + c4 * 16, pk);
@@ -366,18 +391,25 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tc_fence_after();
         const int slot0 = prm.tile_base[kvh * prm.n_tiles + 2 * pair + t];
         if (slot0 >= 0) {
-          // split tile: unnormalised partial O, running max and row sum of this chunk
+          // split tile: this chunk's O / l (fp16), running max and row sum
           const int64_t slot = slot0 + chunk;
-          float* po = prm.part_o + (slot * kBM + row) * HD;
+          __half* po = prm.part_o + (slot * kBM + row) * HD;
+          const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;   // no visible key: O = 0
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
             uint32_t o[32];
             tmem_ld32(tO + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              *reinterpret_cast<uint4*>(po + c * 32 + q * 4) =
-                  make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+            for (int q = 0; q < 4; ++q) {
+              uint4 v;
+              uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                w[e] = pack2<CBK_F16>(__uint_as_float(o[q * 8 + 2 * e]) * inv_l,
+                                      __uint_as_float(o[q * 8 + 2 * e + 1]) * inv_l);
+              st_vec(po + c * 32 + q * 8, v);
+            }
           }
           prm.part_ml[slot * kBM + row] = make_float2(m_used, l_sum);
         } else {
@@ -561,51 +593,57 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
 }
 
 // ---------------------------------------------------------------------------
-// Merge the partial results of split tiles: one thread per row,
-// O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
+// Merge the partial results of split tiles.  One warp per row (a row of a slot
+// is HD contiguous fp16, so every load is coalesced):
+//   O = sum_c w_c Ohat_c / sum_c w_c,  w_c = l_c 2^(m_c - M),  Ohat_c = O_c / l_c.
 // ---------------------------------------------------------------------------
+constexpr int kCombineThreads = 256;
+
 template <int DT, int HD>
-__global__ void __launch_bounds__(kBM)
+__global__ void __launch_bounds__(kCombineThreads)
 attn_combine_kernel(const AttnParams prm) {
-  const int tile = blockIdx.x, kvh = blockIdx.y, row = threadIdx.x;
+  constexpr int kPerLane = HD / 32;   // 4 (HD 128) or 2 (HD 64) elements per lane
+  const int tile = blockIdx.x, kvh = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (prm.plan->error) return;
   const int slot0 = prm.tile_base[kvh * prm.n_tiles + tile];
   if (slot0 < 0) return;
-  const int64_t tok = static_cast<int64_t>(tile) * prm.tok_per_tile + row / prm.group;
-  if (tok >= prm.n_sel) return;
   const int C = prm.plan->chunk;
   const int nc = (tile_key_tiles(prm.pos, prm.n_sel, prm.tok_per_tile, tile) + C - 1) / C;
-  float M = -INFINITY;
-  for (int c = 0; c < nc; ++c) M = fmaxf(M, prm.part_ml[(static_cast<int64_t>(slot0) + c) * kBM + row].x);
-  float acc[HD];
+  for (int row = warp; row < kBM; row += kCombineThreads / 32) {
+    const int64_t tok = static_cast<int64_t>(tile) * prm.tok_per_tile + row / prm.group;
+    if (tok >= prm.n_sel) break;   // rows are token-major: the rest are padding too
+    float M = -INFINITY;
+    for (int c = 0; c < nc; ++c) M = fmaxf(M, prm.part_ml[(static_cast<int64_t>(slot0) + c) * kBM + row].x);
+    float acc[kPerLane];
 #pragma unroll
-  for (int d = 0; d < HD; ++d) acc[d] = 0.f;
-  float Lsum = 0.f;
-  for (int c = 0; c < nc; ++c) {
-    const int64_t slot = slot0 + c;
-    const float2 ml = prm.part_ml[slot * kBM + row];
-    const float w = ex2(ml.x - M);       // a chunk without visible keys has m = -inf -> 0
-    Lsum += ml.y * w;
-    const float4* po = reinterpret_cast<const float4*>(prm.part_o + (slot * kBM + row) * HD);
-#pragma unroll
-    for (int q = 0; q < HD / 4; ++q) {
-      const float4 v = po[q];
-      acc[4 * q] += v.x * w;
-      acc[4 * q + 1] += v.y * w;
-      acc[4 * q + 2] += v.z * w;
-      acc[4 * q + 3] += v.w * w;
+    for (int e = 0; e < kPerLane; ++e) acc[e] = 0.f;
+    float wsum = 0.f;
+    for (int c = 0; c < nc; ++c) {
+      const int64_t slot = slot0 + c;
+      const float2 ml = prm.part_ml[slot * kBM + row];
+      const float w = ml.y * ex2(ml.x - M);   // a chunk without visible keys has l = 0
+      wsum += w;
+      const __half* po = prm.part_o + (slot * kBM + row) * HD + lane * kPerLane;
+      if constexpr (kPerLane == 4) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(po);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+        acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * b.x; acc[3] += w * b.y;
+      } else {
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(po));
+        acc[0] += w * a.x; acc[1] += w * a.y;
+      }
     }
-  }
-  const float inv = 1.f / Lsum;
-  const int hq = kvh * prm.group + row % prm.group;
-  uint16_t* orow = prm.out + (tok * prm.n_q_heads + hq) * static_cast<int64_t>(HD);
-#pragma unroll
-  for (int q = 0; q < HD / 8; ++q) {
-    uint4 v;
-    uint16_t* h = reinterpret_cast<uint16_t*>(&v);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) h[e] = Elem<DT>::from_f(acc[8 * q + e] * inv);
-    st_vec(orow + q * 8, v);
+    const float inv = 1.f / wsum;
+    const int hq = kvh * prm.group + row % prm.group;
+    uint16_t* orow = prm.out + (tok * prm.n_q_heads + hq) * static_cast<int64_t>(HD) + lane * kPerLane;
+    if constexpr (kPerLane == 4) {
+      *reinterpret_cast<uint2*>(orow) = make_uint2(pack2<DT>(acc[0] * inv, acc[1] * inv),
+                                                   pack2<DT>(acc[2] * inv, acc[3] * inv));
+    } else {
+      *reinterpret_cast<uint32_t*>(orow) = pack2<DT>(acc[0] * inv, acc[1] * inv);
+    }
   }
 }
 
@@ -681,7 +719,7 @@ static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int 
   a.off_tile_base = a.off_items + align256(static_cast<size_t>(a.max_items) * sizeof(int4));
   a.off_ml = a.off_tile_base + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int));
   a.off_o = a.off_ml + align256(static_cast<size_t>(a.max_slots) * kBM * sizeof(float2));
-  a.bytes = a.off_o + static_cast<size_t>(a.max_slots) * kBM * head_dim * sizeof(float);
+  a.bytes = a.off_o + static_cast<size_t>(a.max_slots) * kBM * head_dim * sizeof(__half);
   return a;
 }
 
@@ -704,7 +742,7 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   prm.items = reinterpret_cast<const int4*>(ws + lay.off_items);
   prm.tile_base = reinterpret_cast<const int*>(ws + lay.off_tile_base);
   prm.part_ml = reinterpret_cast<float2*>(ws + lay.off_ml);
-  prm.part_o = reinterpret_cast<float*>(ws + lay.off_o);
+  prm.part_o = reinterpret_cast<__half*>(ws + lay.off_o);
   prm.n_sel = n_sel;
   prm.n_q_heads = n_q_heads;
   prm.group = G;
@@ -725,7 +763,7 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   kern<<<static_cast<unsigned>(lay.max_items), kThreads, smem, st>>>(mq, mk, mv, prm);
   if (int rc = check_launch("partial_attn_kernel")) return rc;
   attn_combine_kernel<DT, HD><<<dim3(static_cast<unsigned>(lay.n_tiles), static_cast<unsigned>(n_kv_heads)),
-                                kBM, 0, st>>>(prm);
+                                kCombineThreads, 0, st>>>(prm);
   return check_launch("attn_combine_kernel");
 }
 
