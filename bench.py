@@ -276,6 +276,8 @@ def run_ours(args):
         "config": {"workload": "mistral7b-7k-blend", "model": "Mistral-7B architecture, random init",
                    "chunks": f"{N_CHUNKS}x{CHUNK_LEN}+{QUERY_LEN}", "S": S, "recompute_ratio": RATIO,
                    "k_selected": k_sel, "check_layer": CHECK_LAYER, "global_batch": world,
+                   "selection": {"min_pos": int(min(idx_l)), "median_pos": int(sorted(idx_l)[len(idx_l) // 2]),
+                                 "frac_in_last_1088": round(sum(p >= S - 1088 for p in idx_l) / len(idx_l), 3)},
                    "requests_per_rank": args.requests, "parallelism": f"by-request x{world}",
                    "l2": "inputs larger than L2 (14.5 GB weights, 0.81 GB fused KV per step)"},
         "e2e": {"value": round(world * S / (e2e_step * 1e-3), 1), "unit": "tokens/s",
@@ -547,6 +549,8 @@ def run_attn_layers(args):
     gc = torch.Generator().manual_seed(0)
     if k == S:
         pos = torch.arange(S, device=device)
+    elif args.attn_dist == "tail":      # the last k positions (a selection clustered at the end)
+        pos = torch.arange(S - k, S, device=device)
     else:
         pos = torch.cat([torch.sort(torch.randperm(S - 1, generator=gc)[:k - 1]).values,
                          torch.tensor([S - 1])]).to(device)
@@ -571,7 +575,8 @@ def run_attn_layers(args):
         "metric": "partial attention TFLOP/s (Mistral-7B sparse layer)", "value": round(ach, 1),
         "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "dtype": "bf16",
-        "data": "synthetic", "config": {"workload": "attn-layers", "S": S, "k": k, "layers": L},
+        "data": "synthetic", "config": {"workload": "attn-layers", "S": S, "k": k, "layers": L,
+                                        "selection": args.attn_dist},
         "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": tf_burst, "unit": "TFLOP/s",
                      "frac": round(ach / tf_burst, 4), "peak_kind": f"{src} bf16 burst (kernel timed alone)",
                      "flops_per_launch": flops, "avg_launch_ms": round(t / n, 5)},
@@ -591,6 +596,7 @@ def main():
                     choices=["mistral7b-7k-blend", "kv-microbench", "attn-layers"])
     ap.add_argument("--attn-layers", type=int, default=31)
     ap.add_argument("--attn-k", type=int, default=931, help="selected rows (6208 = dense causal)")
+    ap.add_argument("--attn-dist", default="uniform", choices=["uniform", "tail"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
