@@ -10,14 +10,20 @@
 // no host synchronisation is needed, and the plan can be reused by every layer
 // that attends with the same positions.
 //
+// The attention kernel is persistent: one CTA per SM keeps its TMEM and
+// barriers and pulls items (longest first) from a queue in the workspace.  The
+// producer publishes each item to the other warps through a two-slot ring in
+// shared memory and loads the next item's Q as soon as the current item's last
+// S = Q K^T has been issued, so set-up costs overlap the previous item.
+//
 // TMEM (512 columns): tile t uses S/P at [256t, 256t+128) and O at
-// [256t+128, 256t+128+D).  S = Q K^T lands in fp32; the softmax warps write P
-// back in place as packed 16-bit pairs and the PV MMA reads P straight from
-// TMEM (A operand in tensor memory), so P never touches shared memory.
+// [256t+128, 256t+128+D).  S lands in fp32; the softmax warps write P back in
+// place as packed 16-bit pairs and the PV MMA reads P straight from TMEM (A
+// operand in tensor memory), so P never touches shared memory.
 //
 // Warp roles (384 threads):
-//   warp 0        TMA producer: both Q tiles once, then K and V tiles into two
-//                 separate 2-stage rings
+//   warp 0        producer: fetches items, loads both Q tiles, then K and V tiles
+//                 into two separate 2-stage rings (TMA)
 //   warp 1        MMA issuer: per key tile j, for t = 0, 1: O_t += P_t(j) V(j),
 //                 then S_t(j+1) = Q_t K(j+1)^T.  MMAs issued by one thread run
 //                 in order, so S_t(j+1) overwrites P_t(j) only after the PV
@@ -28,9 +34,10 @@
 //                 warp w owns TMEM lane 32*(w%4)+i, i.e. one row: max / exp / sum
 //                 are thread-local.  O is rescaled only when the running max
 //                 grows by more than 2^8 (O / l uses the same stale max).
-// Every mbarrier wait is bounded (2 s of wall time); on timeout the kernel
-// sets CBK_STATUS_TIMEOUT, drains its own TMA copies and MMAs, frees TMEM and
-// returns.
+// Barrier phases are counted across items.  Every mbarrier wait is bounded
+// (2 s of wall time); on timeout the kernel sets CBK_STATUS_TIMEOUT, drains its
+// own TMA copies and MMAs, frees TMEM and returns.
+#include <algorithm>
 #include <mutex>
 
 #include <cuda.h>
@@ -53,22 +60,26 @@ struct AttnSmem {
   static constexpr int kQ = 0;                     // 2 Q tiles
   static constexpr int kK0 = kQ + 2 * kQBytes;     // 2 K stages
   static constexpr int kV0 = kK0 + 2 * kKVBytes;   // 2 V stages
-  static constexpr int kBar = kV0 + 2 * kKVBytes;  // 16 x 8-byte barriers
-  static constexpr int kMisc = kBar + 16 * 8;      // tmem slot + abort flag
+  static constexpr int kBar = kV0 + 2 * kKVBytes;  // 32 x 8-byte barriers
+  static constexpr int kItems = kBar + 32 * 8;     // 2-slot item ring (int4)
+  static constexpr int kMisc = kItems + 2 * 16;    // tmem slot + abort flag
   static constexpr int kTotal = kMisc + 16;
   // at least 120 KB so that one CTA (holding all 512 TMEM columns) fills an SM
   static constexpr int kAlloc = (kTotal + 1024) > 122880 ? (kTotal + 1024) : 122880;
 };
 
-enum Bar { B_Q = 0, B_KFULL = 1, B_KEMPTY = 3, B_VFULL = 5, B_VEMPTY = 7, B_SFULL = 9,
-           B_PFULL = 11, B_ODONE = 13, B_DRAIN = 15 };
+enum Bar { B_QFULL = 0, B_QEMPTY = 1, B_KFULL = 2, B_KEMPTY = 4, B_VFULL = 6, B_VEMPTY = 8,
+           B_SFULL = 10, B_PFULL = 12, B_ODONE = 14, B_OFREE = 16, B_IFULL = 18, B_IEMPTY = 20,
+           B_DRAIN = 22 };
 
 // Work plan in the caller's workspace (written by attn_plan_kernel).
 struct AttnPlanHeader {
-  int n_items;     // work items (CTAs with work)
+  int n_items;     // work items
   int chunk;       // key tiles per item (C)
   int n_slots;     // partial-result slots in use
   int error;       // nonzero: the plan did not fit the workspace bounds
+  int next_item;   // queue head: zeroed by the plan and after every attention call
+  int n_split;     // Q tiles (over all KV heads) whose key range is split
 };
 
 struct AttnParams {
@@ -76,8 +87,10 @@ struct AttnParams {
   uint16_t* out;
   int32_t* status;
   const AttnPlanHeader* plan;
+  int* queue;             // &plan->next_item
   const int4* items;      // (kv head, tile pair, chunk, length) longest first
   const int* tile_base;   // [Hkv][n_tiles]: first partial slot of a split tile, -1 if not split
+  const int* split_list;  // [n_split]: kvh * n_tiles + tile of every split tile
   __half* part_o;         // [slot][128][HD] O / l of the chunk (fp16, bounded by |V|)
   float2* part_ml;        // [slot][128] (running max in log2 units, row sum)
   int64_t n_sel;
@@ -116,14 +129,49 @@ __device__ __forceinline__ int tile_key_tiles(const int64_t* pos, int64_t n_sel,
   return static_cast<int>(pos[last] / kBN) + 1;
 }
 
+// geometry of one work item: Q-tile pair, chunk of key tiles
+struct ItemGeom {
+  int kvh, pair, chunk, j0;
+  int n_kv[2];          // key tiles of this item for tile 0 / 1 (0: tile absent or done)
+  int n_all;            // max of the two
+  int n_q_tiles;        // 1 when the pair's second tile does not exist
+  int64_t tok0[2], tok_end[2], p_max[2];
+};
+
+__device__ __forceinline__ ItemGeom item_geom(const int4 item, int C, const AttnParams& prm) {
+  ItemGeom g;
+  g.kvh = item.x;
+  g.pair = item.y;
+  g.chunk = item.z;
+  g.j0 = item.z * C;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int tile = 2 * g.pair + t;
+    g.tok0[t] = static_cast<int64_t>(tile) * prm.tok_per_tile;
+    if (tile >= prm.n_tiles) {
+      g.tok_end[t] = g.tok0[t];
+      g.p_max[t] = 0;
+      g.n_kv[t] = 0;
+    } else {
+      g.tok_end[t] = min(g.tok0[t] + prm.tok_per_tile, prm.n_sel);
+      g.p_max[t] = prm.pos[g.tok_end[t] - 1];
+      const int n_full = static_cast<int>(g.p_max[t] / kBN) + 1;
+      g.n_kv[t] = max(0, min(C, n_full - g.j0));
+    }
+  }
+  g.n_all = max(g.n_kv[0], g.n_kv[1]);
+  g.n_q_tiles = (2 * g.pair + 1 < prm.n_tiles) ? 2 : 1;
+  return g;
+}
+
 template <int DT, int HD>
 __global__ void __launch_bounds__(kThreads, 1)
 partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const AttnParams prm) {
   using L = AttnSmem<HD>;
-  // one work item per CTA; CTAs beyond the planned items exit at once
-  if (static_cast<int>(blockIdx.x) >= prm.plan->n_items || prm.plan->error) return;
-  const int4 item = prm.items[blockIdx.x];
+  if (prm.plan->error || prm.plan->n_items == 0) return;
+  const int n_items = prm.plan->n_items;
+  const int C = prm.plan->chunk;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -131,38 +179,15 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   uint8_t* sbase = smem_raw + (base - raw_addr);
   const uint32_t sQ = base + L::kQ, sK0 = base + L::kK0, sV0 = base + L::kV0;
   auto bar = [&](int i) { return base + L::kBar + 8u * i; };
+  volatile int4* s_item = reinterpret_cast<volatile int4*>(sbase + L::kItems);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sbase + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sbase + L::kMisc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kvh = item.x, pair = item.y, chunk = item.z;
-  const int C = prm.plan->chunk;
-  const int j0 = chunk * C;                 // first key tile of this item
-  // per-tile geometry (tile 1 may be absent for an odd tile count); returns the
-  // number of key tiles of this item for the tile
-  auto geom = [&](int t, int64_t& tok0, int64_t& tok_end, int64_t& p_max) -> int {
-    const int tile = 2 * pair + t;
-    tok0 = static_cast<int64_t>(tile) * prm.tok_per_tile;
-    if (tile >= prm.n_tiles) {
-      tok_end = tok0;
-      p_max = 0;
-      return 0;
-    }
-    tok_end = min(tok0 + prm.tok_per_tile, prm.n_sel);
-    p_max = prm.pos[tok_end - 1];
-    const int n_full = static_cast<int>(p_max / kBN) + 1;
-    return max(0, min(C, n_full - j0));
-  };
-  int64_t a0, a1, a2;
-  const int n_kv0 = geom(0, a0, a1, a2);
-  const int64_t q_tok0 = a0;
-  const int n_kv1 = geom(1, a0, a1, a2);
-  const int64_t q_tok1 = a0;
-  const int n_all = max(n_kv0, n_kv1);
-  const int n_q_tiles = (2 * pair + 1 < prm.n_tiles) ? 2 : 1;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(B_Q), 1);
+    mbar_init(bar(B_QFULL), 1);
+    mbar_init(bar(B_QEMPTY), 1);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(B_KFULL + i), 1);
@@ -170,8 +195,11 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_init(bar(B_VFULL + i), 1);
       mbar_init(bar(B_VEMPTY + i), 1);
       mbar_init(bar(B_SFULL + i), 1);
-      mbar_init(bar(B_PFULL + i), 4);
+      mbar_init(bar(B_PFULL + i), 4);     // one arrive per softmax warp of the tile
       mbar_init(bar(B_ODONE + i), 1);
+      mbar_init(bar(B_OFREE + i), 4);
+      mbar_init(bar(B_IFULL + i), 1);
+      mbar_init(bar(B_IEMPTY + i), 9);    // MMA thread + 8 softmax warps
     }
     mbar_init(bar(B_DRAIN), 1);
     *abort_flag = 0;
@@ -187,43 +215,74 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   const uint32_t tmem = *tmem_slot;
   bool failed = false;
 
+  // consumers: item n of this CTA from ring slot n & 1
+  auto take_item = [&](int n, int4& item) -> bool {
+    if (!wait_or_abort(bar(B_IFULL + (n & 1)), (n >> 1) & 1, abort_flag)) return false;
+    const volatile int4& v = s_item[n & 1];
+    item = make_int4(v.x, v.y, v.z, v.w);
+    return true;
+  };
+
   if (warp == 0 && lane == 0) {
-    // ----------------------------------------------------------- TMA producer
+    // ------------------------------------------------ item queue + TMA producer
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
-    mbar_expect_tx(bar(B_Q), n_q_tiles * L::kQBytes);
-    for (int t = 0; t < n_q_tiles; ++t)
-#pragma unroll
-      for (int h = 0; h < HD / 64; ++h)
-        tma_load_3d(sQ + t * L::kQBytes + h * (kBM * 128), &tm_q, bar(B_Q), h * 64,
-                    kvh * prm.group, static_cast<int>(t ? q_tok1 : q_tok0));
+    int g = 0;                               // K/V tiles loaded by this CTA
     int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
-    for (int j = 0; j < n_all; ++j) {
-      const int st = j & 1;
-      if (j >= 2 && !wait_or_abort(bar(B_KEMPTY + st), ((j >> 1) - 1) & 1, abort_flag)) {
+    int n_q = 0;                             // Q loads issued
+    for (int n = 0; !failed; ++n) {
+      if (n >= 2 && !wait_or_abort(bar(B_IEMPTY + (n & 1)), ((n >> 1) - 1) & 1, abort_flag)) {
         failed = true;
         break;
       }
-      mbar_expect_tx(bar(B_KFULL + st), L::kKVBytes);
-#pragma unroll
-      for (int h = 0; h < HD / 64; ++h)
-        tma_load_3d(sK0 + st * L::kKVBytes + h * (kBN * 128), &tm_k, bar(B_KFULL + st), h * 64, kvh,
-                    (j0 + j) * kBN);
-      last_k[st] = j;
-      if (j >= 2 && !wait_or_abort(bar(B_VEMPTY + st), ((j >> 1) - 1) & 1, abort_flag)) {
+      const int idx = atomicAdd(prm.queue, 1);
+      const int4 item = idx < n_items ? prm.items[idx] : make_int4(-1, 0, 0, 0);
+      s_item[n & 1].x = item.x;
+      s_item[n & 1].y = item.y;
+      s_item[n & 1].z = item.z;
+      s_item[n & 1].w = item.w;
+      mbar_arrive(bar(B_IFULL + (n & 1)));   // release: the slot is visible to the waiters
+      if (item.x < 0) break;
+      const ItemGeom ig = item_geom(item, C, prm);
+      // Q of this item once the previous item's last S = Q K^T has been issued
+      if (n_q > 0 && !wait_or_abort(bar(B_QEMPTY), (n_q - 1) & 1, abort_flag)) {
         failed = true;
         break;
       }
-      mbar_expect_tx(bar(B_VFULL + st), L::kKVBytes);
+      mbar_expect_tx(bar(B_QFULL), ig.n_q_tiles * L::kQBytes);
+      for (int t = 0; t < ig.n_q_tiles; ++t)
 #pragma unroll
-      for (int h = 0; h < HD / 64; ++h)
-        tma_load_3d(sV0 + st * L::kKVBytes + h * (kBN * 128), &tm_v, bar(B_VFULL + st), h * 64, kvh,
-                    (j0 + j) * kBN);
-      last_v[st] = j;
+        for (int h = 0; h < HD / 64; ++h)
+          tma_load_3d(sQ + t * L::kQBytes + h * (kBM * 128), &tm_q, bar(B_QFULL), h * 64,
+                      ig.kvh * prm.group, static_cast<int>(ig.tok0[t]));
+      ++n_q;
+      for (int j = 0; j < ig.n_all; ++j, ++g) {
+        const int st = g & 1;
+        if (g >= 2 && !wait_or_abort(bar(B_KEMPTY + st), ((g >> 1) - 1) & 1, abort_flag)) {
+          failed = true;
+          break;
+        }
+        mbar_expect_tx(bar(B_KFULL + st), L::kKVBytes);
+#pragma unroll
+        for (int h = 0; h < HD / 64; ++h)
+          tma_load_3d(sK0 + st * L::kKVBytes + h * (kBN * 128), &tm_k, bar(B_KFULL + st), h * 64, ig.kvh,
+                      (ig.j0 + j) * kBN);
+        last_k[st] = g;
+        if (g >= 2 && !wait_or_abort(bar(B_VEMPTY + st), ((g >> 1) - 1) & 1, abort_flag)) {
+          failed = true;
+          break;
+        }
+        mbar_expect_tx(bar(B_VFULL + st), L::kKVBytes);
+#pragma unroll
+        for (int h = 0; h < HD / 64; ++h)
+          tma_load_3d(sV0 + st * L::kKVBytes + h * (kBN * 128), &tm_v, bar(B_VFULL + st), h * 64, ig.kvh,
+                      (ig.j0 + j) * kBN);
+        last_v[st] = g;
+      }
     }
     // Drain: every armed copy must land before the CTA can retire.
-    if (!mbar_wait(bar(B_Q), 0)) failed = true;
+    if (n_q > 0 && !mbar_wait(bar(B_QFULL), (n_q - 1) & 1)) failed = true;
     for (int st = 0; st < 2; ++st) {
       if (last_k[st] >= 0 && !mbar_wait(bar(B_KFULL + st), (last_k[st] >> 1) & 1)) failed = true;
       if (last_v[st] >= 0 && !mbar_wait(bar(B_VFULL + st), (last_v[st] >> 1) & 1)) failed = true;
@@ -232,8 +291,8 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     // ------------------------------------------------------------- MMA issuer
     const uint32_t idesc_s = umma_idesc_f16(DT, kBM, kBN, 0);
     const uint32_t idesc_o = umma_idesc_f16(DT, kBM, HD, 1);
-    auto issue_s = [&](int t, int j) {
-      const uint32_t kb = sK0 + (j & 1) * L::kKVBytes;
+    auto issue_s = [&](int t, int g) {
+      const uint32_t kb = sK0 + (g & 1) * L::kKVBytes;
       const uint32_t qb = sQ + t * L::kQBytes;
 #pragma unroll
       for (int kk = 0; kk < HD / 16; ++kk) {
@@ -244,49 +303,79 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       umma_commit(bar(B_SFULL + t));
     };
-    auto issue_pv = [&](int t, int j) {
-      const uint32_t vb = sV0 + (j & 1) * L::kKVBytes;
+    auto issue_pv = [&](int t, int g, bool acc) {
+      const uint32_t vb = sV0 + (g & 1) * L::kKVBytes;
 #pragma unroll
       for (int kk = 0; kk < kBN / 16; ++kk)
         umma_f16_ts(tmem + 256 * t + kBN, tmem + 256 * t + kk * 8,
                     umma_desc_sw128(vb + kk * 16 * 128, kBN * 128, 1024), idesc_o,
-                    (j > 0 || kk > 0) ? 1u : 0u);
+                    (acc || kk > 0) ? 1u : 0u);
     };
-    do {
-      if (!wait_or_abort(bar(B_Q), 0, abort_flag) || !wait_or_abort(bar(B_KFULL), 0, abort_flag)) {
+    int g = 0;                 // K/V tiles consumed
+    int pc[2] = {0, 0};        // P tiles consumed per Q-tile slot
+    int oc[2] = {0, 0};        // O results handed to the epilogue per Q-tile slot
+    for (int n = 0; !failed; ++n) {
+      int4 item;
+      if (!take_item(n, item)) {
+        failed = true;
+        break;
+      }
+      mbar_arrive(bar(B_IEMPTY + (n & 1)));
+      if (item.x < 0) break;
+      const ItemGeom ig = item_geom(item, C, prm);
+      if (!wait_or_abort(bar(B_QFULL), n & 1, abort_flag) ||
+          !wait_or_abort(bar(B_KFULL + (g & 1)), (g >> 1) & 1, abort_flag)) {
         failed = true;
         break;
       }
       tc_fence_after();
-      if (n_kv0 > 0) issue_s(0, 0);
-      if (n_kv1 > 0) issue_s(1, 0);
-      umma_commit(bar(B_KEMPTY));
-      for (int j = 0; j < n_all && !failed; ++j) {
-        const bool next_k = (j + 1 < n_kv0) || (j + 1 < n_kv1);
-        if (next_k && !wait_or_abort(bar(B_KFULL + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag)) {
+      // S(0): the previous item's PVs that read P from these columns were issued
+      // earlier by this thread, so they complete first
+      if (ig.n_kv[0] > 0) issue_s(0, g);
+      if (ig.n_kv[1] > 0) issue_s(1, g);
+      umma_commit(bar(B_KEMPTY + (g & 1)));
+      if (ig.n_all == 1) umma_commit(bar(B_QEMPTY));
+      for (int j = 0; j < ig.n_all && !failed; ++j) {
+        const int gj = g + j;
+        const bool next_k = j + 1 < ig.n_all;
+        if (next_k && !wait_or_abort(bar(B_KFULL + ((gj + 1) & 1)), ((gj + 1) >> 1) & 1, abort_flag)) {
           failed = true;
           break;
         }
-        if (!wait_or_abort(bar(B_VFULL + (j & 1)), (j >> 1) & 1, abort_flag)) {
+        if (!wait_or_abort(bar(B_VFULL + (gj & 1)), (gj >> 1) & 1, abort_flag)) {
           failed = true;
           break;
         }
+#pragma unroll
         for (int t = 0; t < 2; ++t) {
-          const int n_t = t ? n_kv1 : n_kv0;
+          const int n_t = ig.n_kv[t];
           if (j >= n_t) continue;
-          if (!wait_or_abort(bar(B_PFULL + t), j & 1, abort_flag)) {
+          if (!wait_or_abort(bar(B_PFULL + t), pc[t] & 1, abort_flag)) {
+            failed = true;
+            break;
+          }
+          ++pc[t];
+          // the first PV of an item overwrites O: the previous epilogue must have read it
+          if (j == 0 && oc[t] > 0 && !wait_or_abort(bar(B_OFREE + t), (oc[t] - 1) & 1, abort_flag)) {
             failed = true;
             break;
           }
           tc_fence_after();
-          issue_pv(t, j);
-          if (j + 1 < n_t) issue_s(t, j + 1);
-          else umma_commit(bar(B_ODONE + t));
+          issue_pv(t, gj, j > 0);
+          if (j + 1 < n_t) {
+            issue_s(t, gj + 1);
+          } else {
+            umma_commit(bar(B_ODONE + t));
+            ++oc[t];
+          }
         }
-        umma_commit(bar(B_VEMPTY + (j & 1)));
-        if (next_k) umma_commit(bar(B_KEMPTY + ((j + 1) & 1)));
+        if (failed) break;
+        umma_commit(bar(B_VEMPTY + (gj & 1)));
+        if (next_k) umma_commit(bar(B_KEMPTY + ((gj + 1) & 1)));
+        if (j + 2 == ig.n_all) umma_commit(bar(B_QEMPTY));   // last S of the item issued
       }
-    } while (false);
+      g += ig.n_all;
+    }
     // Drain: all MMAs issued by this thread complete before TMEM is released.
     umma_commit(bar(B_DRAIN));
     if (!mbar_wait(bar(B_DRAIN), 0)) failed = true;
@@ -297,143 +386,161 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const int row = sub * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const uint32_t tS = tmem + 256 * t + lane_off, tO = tS + kBN;
-    int64_t t_tok0, t_tok_end, t_pmax;
-    const int n_t = geom(t, t_tok0, t_tok_end, t_pmax);
-    const int64_t tok = t_tok0 + row / prm.group;
-    const bool row_valid = tok < t_tok_end;
-    const int64_t p_row = row_valid ? prm.pos[tok] : t_pmax;
-    float m_used = -INFINITY, l_sum = 0.f;
     const float sl2 = prm.scale_log2;
-    for (int j = 0; j < n_t; ++j) {
-      if (!__all_sync(0xffffffffu, wait_or_abort(bar(B_SFULL + t), j & 1, abort_flag))) {
+    int sc = 0;     // S tiles consumed
+    int oc = 0;     // O results consumed
+    for (int n = 0; !failed; ++n) {
+      int4 item;
+      if (!__all_sync(0xffffffffu, take_item(n, item))) {
         failed = true;
         break;
       }
-      tc_fence_after();
-      // keys (j0 + j)*kBN + c are visible to this row iff c <= lim
-      const int64_t lim64 = p_row - static_cast<int64_t>(j0 + j) * kBN;
-      const int lim = lim64 >= kBN ? kBN : static_cast<int>(lim64);
-      // the whole S row in registers: four loads in flight, one wait
-      uint32_t s[kBN];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_IEMPTY + (n & 1)));
+      if (item.x < 0) break;
+      const ItemGeom ig = item_geom(item, C, prm);
+      // (t is warp-uniform; selects keep the geometry in registers)
+      const int n_t = t ? ig.n_kv[1] : ig.n_kv[0];
+      if (n_t == 0) continue;
+      const int64_t tok = (t ? ig.tok0[1] : ig.tok0[0]) + row / prm.group;
+      const bool row_valid = tok < (t ? ig.tok_end[1] : ig.tok_end[0]);
+      const int64_t p_row = row_valid ? prm.pos[tok] : (t ? ig.p_max[1] : ig.p_max[0]);
+      float m_used = -INFINITY, l_sum = 0.f;
+      for (int j = 0; j < n_t; ++j, ++sc) {
+        if (!__all_sync(0xffffffffu, wait_or_abort(bar(B_SFULL + t), sc & 1, abort_flag))) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        // keys (j0 + j)*kBN + c are visible to this row iff c <= lim
+        const int64_t lim64 = p_row - static_cast<int64_t>(ig.j0 + j) * kBN;
+        const int lim = lim64 >= kBN ? kBN : static_cast<int>(lim64);
+        // the whole S row in registers: four loads in flight, one wait
+        uint32_t s[kBN];
 #pragma unroll
-      for (int c4 = 0; c4 < kBN / 32; ++c4)
-        tmem_ld32(tS + c4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c4 * 32]));
-      tmem_wait_ld();
-      // whole tile visible to every row of the warp: no masking work
-      const bool full = __all_sync(0xffffffffu, lim >= kBN - 1);
-      float mx = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < kBN; ++c)
-          if (c <= lim) mx = fmaxf(mx, __uint_as_float(s[c]));
-      }
-      const float m_tile = mx * sl2;
-      float alpha = 1.f;
-      bool rescale = false;
-      if (j == 0) {
-        m_used = m_tile;
-      } else if (m_tile > m_used + 8.f) {
-        alpha = ex2(m_used - m_tile);
-        m_used = m_tile;
-        rescale = true;
-      }
-      float rs = 0.f;
-#pragma unroll
-      for (int c4 = 0; c4 < kBN / 32; ++c4) {
-        uint32_t pk[16];
+        for (int c4 = 0; c4 < kBN / 32; ++c4)
+          tmem_ld32(tS + c4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c4 * 32]));
+        tmem_wait_ld();
+        // whole tile visible to every row of the warp: no masking work
+        const bool full = __all_sync(0xffffffffu, lim >= kBN - 1);
+        float mx = -INFINITY;
         if (full) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int c = c4 * 32 + 2 * e;
-            const float p0 = ex2(__uint_as_float(s[c]) * sl2 - m_used);
-            const float p1 = ex2(__uint_as_float(s[c + 1]) * sl2 - m_used);
-            rs += p0 + p1;
-            pk[e] = pack2<DT>(p0, p1);
-          }
+          for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
         } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int c = c4 * 32 + 2 * e;
-            const float p0 = (c <= lim) ? ex2(__uint_as_float(s[c]) * sl2 - m_used) : 0.f;
-            const float p1 = (c + 1 <= lim) ? ex2(__uint_as_float(s[c + 1]) * sl2 - m_used) : 0.f;
-            rs += p0 + p1;
-            pk[e] = pack2<DT>(p0, p1);
+          for (int c = 0; c < kBN; ++c)
+            if (c <= lim) mx = fmaxf(mx, __uint_as_float(s[c]));
+        }
+        const float m_tile = mx * sl2;
+        float alpha = 1.f;
+        bool rescale = false;
+        if (j == 0) {
+          m_used = m_tile;
+        } else if (m_tile > m_used + 8.f) {
+          alpha = ex2(m_used - m_tile);
+          m_used = m_tile;
+          rescale = true;
+        }
+        float rs = 0.f;
+#pragma unroll
+        for (int c4 = 0; c4 < kBN / 32; ++c4) {
+          uint32_t pk[16];
+          if (full) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int c = c4 * 32 + 2 * e;
+              const float p0 = ex2(__uint_as_float(s[c]) * sl2 - m_used);
+              const float p1 = ex2(__uint_as_float(s[c + 1]) * sl2 - m_used);
+              rs += p0 + p1;
+              pk[e] = pack2<DT>(p0, p1);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int c = c4 * 32 + 2 * e;
+              const float p0 = (c <= lim) ? ex2(__uint_as_float(s[c]) * sl2 - m_used) : 0.f;
+              const float p1 = (c + 1 <= lim) ? ex2(__uint_as_float(s[c + 1]) * sl2 - m_used) : 0.f;
+              rs += p0 + p1;
+              pk[e] = pack2<DT>(p0, p1);
+            }
+          }
+          // P chunk c4 -> columns [16 c4, 16 c4 + 16) (S was read completely above)
+          tmem_st16(tS + c4 * 16, pk);
+        }
+        l_sum = l_sum * alpha + rs;
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O is stable: the commit behind this tile's S(j) covered PV(j-1)
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + c * 32, o);
           }
         }
-        // P chunk c4 -> columns [16 c4, 16 c4 + 16) (S was read completely above)
-        tmem_st16(tS + c4 * 16, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_PFULL + t));
       }
-      l_sum = l_sum * alpha + rs;
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O is stable: the commit behind this tile's S(j) covered PV(j-1)
+      if (failed) break;
+      if (!__all_sync(0xffffffffu, wait_or_abort(bar(B_ODONE + t), oc & 1, abort_flag))) {
+        failed = true;
+        break;
+      }
+      ++oc;
+      tc_fence_after();
+      const int slot0 = prm.tile_base[ig.kvh * prm.n_tiles + 2 * ig.pair + t];
+      if (slot0 >= 0) {
+        // split tile: this chunk's O / l (fp16), running max and row sum
+        const int64_t slot = slot0 + ig.chunk;
+        __half* po = prm.part_o + (slot * kBM + row) * HD;
+        const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;   // no visible key: O = 0
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(tO + c * 32, o);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_PFULL + t));
-    }
-    if (!failed && n_t > 0) {
-      if (!__all_sync(0xffffffffu, wait_or_abort(bar(B_ODONE + t), 0, abort_flag))) {
-        failed = true;
-      } else {
-        tc_fence_after();
-        const int slot0 = prm.tile_base[kvh * prm.n_tiles + 2 * pair + t];
-        if (slot0 >= 0) {
-          // split tile: this chunk's O / l (fp16), running max and row sum
-          const int64_t slot = slot0 + chunk;
-          __half* po = prm.part_o + (slot * kBM + row) * HD;
-          const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;   // no visible key: O = 0
+          for (int q = 0; q < 4; ++q) {
+            uint4 v;
+            uint32_t* w = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + c * 32, o);
-            tmem_wait_ld();
+            for (int e = 0; e < 4; ++e)
+              w[e] = pack2<CBK_F16>(__uint_as_float(o[q * 8 + 2 * e]) * inv_l,
+                                    __uint_as_float(o[q * 8 + 2 * e + 1]) * inv_l);
+            st_vec(po + c * 32 + q * 8, v);
+          }
+        }
+        prm.part_ml[slot * kBM + row] = make_float2(m_used, l_sum);
+      } else {
+        const float inv_l = 1.f / l_sum;
+        const int hq = ig.kvh * prm.group + row % prm.group;
+        uint16_t* orow = prm.out + (tok * prm.n_q_heads + hq) * static_cast<int64_t>(HD);
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+          if (row_valid) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               uint4 v;
-              uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+              uint16_t* h = reinterpret_cast<uint16_t*>(&v);
 #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                w[e] = pack2<CBK_F16>(__uint_as_float(o[q * 8 + 2 * e]) * inv_l,
-                                      __uint_as_float(o[q * 8 + 2 * e + 1]) * inv_l);
-              st_vec(po + c * 32 + q * 8, v);
-            }
-          }
-          prm.part_ml[slot * kBM + row] = make_float2(m_used, l_sum);
-        } else {
-          const float inv_l = 1.f / l_sum;
-          const int hq = kvh * prm.group + row % prm.group;
-          uint16_t* orow = prm.out + (tok * prm.n_q_heads + hq) * static_cast<int64_t>(HD);
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + c * 32, o);
-            tmem_wait_ld();
-            if (row_valid) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 v;
-                uint16_t* h = reinterpret_cast<uint16_t*>(&v);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) h[e] = Elem<DT>::from_f(__uint_as_float(o[q * 8 + e]) * inv_l);
-                st_vec(orow + c * 32 + q * 8, v);
-              }
+              for (int e = 0; e < 8; ++e) h[e] = Elem<DT>::from_f(__uint_as_float(o[q * 8 + e]) * inv_l);
+              st_vec(orow + c * 32 + q * 8, v);
             }
           }
         }
       }
+      // O has been read: the next item's first PV may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(B_OFREE + t));
     }
   }
 
@@ -490,7 +597,7 @@ __device__ int block_excl_scan(int v, int* s_warp, int* total) {
 __global__ void __launch_bounds__(kPlanThreads, 1)
 attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_tile, int n_tiles,
                  int n_kv_heads, int target_items, int min_chunk, int max_items, int max_slots,
-                 AttnPlanHeader* hdr, int4* items, int* tile_base, int32_t* status) {
+                 AttnPlanHeader* hdr, int4* items, int* tile_base, int* split_list, int32_t* status) {
   __shared__ int s_hist[kMaxKvTiles + 1];
   __shared__ int s_warp[33];
   __shared__ unsigned long long s_total;
@@ -568,8 +675,9 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
         if (at < max_items) items[at] = make_int4(h, p, c, len);
       }
   }
-  // 5. partial slots of split tiles, in (head, tile) order
-  int carry = 0;
+  // 5. partial slots of split tiles, in (head, tile) order, and the list of
+  //    split tiles that the combine kernel walks
+  int carry = 0, n_split = 0;
   const int n_all = n_kv_heads * n_tiles;
   for (int b0 = 0; b0 < n_all; b0 += kPlanThreads) {
     const int i = b0 + tid;
@@ -578,61 +686,81 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
       const int nc = (tile_key_tiles(pos, n_sel, tok_per_tile, i % n_tiles) + C - 1) / C;
       cnt = nc > 1 ? nc : 0;
     }
-    int tot;
+    int tot, tot_split;
     const int off = block_excl_scan(cnt, s_warp, &tot);
-    if (i < n_all) tile_base[i] = cnt ? carry + off : -1;
+    const int rank = block_excl_scan(cnt ? 1 : 0, s_warp, &tot_split);
+    if (i < n_all) {
+      tile_base[i] = cnt ? carry + off : -1;
+      if (cnt) split_list[n_split + rank] = i;
+    }
     carry += tot;
+    n_split += tot_split;
   }
   if (tid == 0) {
     if (carry > max_slots) s_error = 1;
+    hdr->n_split = n_split;
     hdr->chunk = C;
     hdr->n_slots = carry;
     hdr->error = s_error;
+    hdr->next_item = 0;
     if (s_error) report(status, CBK_STATUS_COUNT);
   }
 }
 
 // ---------------------------------------------------------------------------
-// Merge the partial results of split tiles.  One warp per row (a row of a slot
-// is HD contiguous fp16, so every load is coalesced):
+// Merge the partial results of split tiles.  Work unit = (split tile, group of
+// kCombineRows rows), one warp per row; the units are spread over a fixed grid
+// from the plan's list of split tiles, so no CTA is spent on unsplit tiles.  A
+// row of a slot is HD contiguous fp16, so every load is coalesced.  One pass
+// with a running maximum:
 //   O = sum_c w_c Ohat_c / sum_c w_c,  w_c = l_c 2^(m_c - M),  Ohat_c = O_c / l_c.
 // ---------------------------------------------------------------------------
 constexpr int kCombineThreads = 256;
+constexpr int kCombineRows = kCombineThreads / 32;
+constexpr int kCombineUnitsPerTile = kBM / kCombineRows;
 
 template <int DT, int HD>
 __global__ void __launch_bounds__(kCombineThreads)
 attn_combine_kernel(const AttnParams prm) {
   constexpr int kPerLane = HD / 32;   // 4 (HD 128) or 2 (HD 64) elements per lane
-  const int tile = blockIdx.x, kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // every attention CTA has finished: rewind the item queue for the next call
+  if (blockIdx.x == 0 && threadIdx.x == 0) *prm.queue = 0;
   if (prm.plan->error) return;
-  const int slot0 = prm.tile_base[kvh * prm.n_tiles + tile];
-  if (slot0 < 0) return;
   const int C = prm.plan->chunk;
-  const int nc = (tile_key_tiles(prm.pos, prm.n_sel, prm.tok_per_tile, tile) + C - 1) / C;
-  for (int row = warp; row < kBM; row += kCombineThreads / 32) {
+  const int n_units = prm.plan->n_split * kCombineUnitsPerTile;
+  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    const int ti = prm.split_list[u / kCombineUnitsPerTile];
+    const int kvh = ti / prm.n_tiles, tile = ti % prm.n_tiles;
+    const int row = (u % kCombineUnitsPerTile) * kCombineRows + warp;
     const int64_t tok = static_cast<int64_t>(tile) * prm.tok_per_tile + row / prm.group;
-    if (tok >= prm.n_sel) break;   // rows are token-major: the rest are padding too
-    float M = -INFINITY;
-    for (int c = 0; c < nc; ++c) M = fmaxf(M, prm.part_ml[(static_cast<int64_t>(slot0) + c) * kBM + row].x);
+    if (tok >= prm.n_sel) continue;   // padding row of the last tile
+    const int slot0 = prm.tile_base[ti];
+    const int nc = (tile_key_tiles(prm.pos, prm.n_sel, prm.tok_per_tile, tile) + C - 1) / C;
     float acc[kPerLane];
 #pragma unroll
     for (int e = 0; e < kPerLane; ++e) acc[e] = 0.f;
-    float wsum = 0.f;
+    float M = -INFINITY, wsum = 0.f;
     for (int c = 0; c < nc; ++c) {
       const int64_t slot = slot0 + c;
       const float2 ml = prm.part_ml[slot * kBM + row];
-      const float w = ml.y * ex2(ml.x - M);   // a chunk without visible keys has l = 0
-      wsum += w;
-      const __half* po = prm.part_o + (slot * kBM + row) * HD + lane * kPerLane;
-      if constexpr (kPerLane == 4) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(po);
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-        acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * b.x; acc[3] += w * b.y;
-      } else {
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(po));
-        acc[0] += w * a.x; acc[1] += w * a.y;
+      if (ml.y > 0.f) {                     // a chunk without visible keys has l = 0
+        const float Mn = fmaxf(M, ml.x);
+        const float r = ex2(M - Mn);        // 0 on the first visible chunk
+        const float w = ml.y * ex2(ml.x - Mn);
+        wsum = wsum * r + w;
+        const __half* po = prm.part_o + (slot * kBM + row) * HD + lane * kPerLane;
+        if constexpr (kPerLane == 4) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(po);
+          const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+          const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+          acc[0] = acc[0] * r + w * a.x; acc[1] = acc[1] * r + w * a.y;
+          acc[2] = acc[2] * r + w * b.x; acc[3] = acc[3] * r + w * b.y;
+        } else {
+          const float2 a = __half22float2(*reinterpret_cast<const __half2*>(po));
+          acc[0] = acc[0] * r + w * a.x; acc[1] = acc[1] * r + w * a.y;
+        }
+        M = Mn;
       }
     }
     const float inv = 1.f / wsum;
@@ -698,7 +826,7 @@ static int sm_count() {
 // Workspace layout of one partial-attention call (all offsets 256-byte aligned).
 struct AttnLayout {
   int tok_per_tile, n_tiles, n_pairs, target, min_chunk, max_items, max_slots;
-  size_t off_items, off_tile_base, off_ml, off_o, bytes;
+  size_t off_items, off_tile_base, off_split, off_ml, off_o, bytes;
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -717,7 +845,8 @@ static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int 
   a.max_slots = 4 * a.target + 2;
   a.off_items = align256(sizeof(AttnPlanHeader));
   a.off_tile_base = a.off_items + align256(static_cast<size_t>(a.max_items) * sizeof(int4));
-  a.off_ml = a.off_tile_base + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int));
+  a.off_split = a.off_tile_base + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int));
+  a.off_ml = a.off_split + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int));
   a.off_o = a.off_ml + align256(static_cast<size_t>(a.max_slots) * kBM * sizeof(float2));
   a.bytes = a.off_o + static_cast<size_t>(a.max_slots) * kBM * head_dim * sizeof(__half);
   return a;
@@ -739,8 +868,10 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   prm.out = static_cast<uint16_t*>(out);
   prm.status = status;
   prm.plan = reinterpret_cast<const AttnPlanHeader*>(ws);
+  prm.queue = &reinterpret_cast<AttnPlanHeader*>(ws)->next_item;
   prm.items = reinterpret_cast<const int4*>(ws + lay.off_items);
   prm.tile_base = reinterpret_cast<const int*>(ws + lay.off_tile_base);
+  prm.split_list = reinterpret_cast<const int*>(ws + lay.off_split);
   prm.part_ml = reinterpret_cast<float2*>(ws + lay.off_ml);
   prm.part_o = reinterpret_cast<__half*>(ws + lay.off_o);
   prm.n_sel = n_sel;
@@ -754,16 +885,16 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
         pos, n_sel, lay.tok_per_tile, lay.n_tiles, n_kv_heads, lay.target, lay.min_chunk,
         lay.max_items, lay.max_slots, reinterpret_cast<AttnPlanHeader*>(ws),
         reinterpret_cast<int4*>(ws + lay.off_items), reinterpret_cast<int*>(ws + lay.off_tile_base),
-        status);
+        reinterpret_cast<int*>(ws + lay.off_split), status);
     if (int rc = check_launch("attn_plan_kernel")) return rc;
   }
   auto kern = partial_attn_kernel<DT, HD>;
   const int smem = AttnSmem<HD>::kAlloc;
   if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem)) return rc;
-  kern<<<static_cast<unsigned>(lay.max_items), kThreads, smem, st>>>(mq, mk, mv, prm);
+  const int grid = std::min(lay.max_items, sm_count());   // persistent: one CTA per SM
+  kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(mq, mk, mv, prm);
   if (int rc = check_launch("partial_attn_kernel")) return rc;
-  attn_combine_kernel<DT, HD><<<dim3(static_cast<unsigned>(lay.n_tiles), static_cast<unsigned>(n_kv_heads)),
-                                kCombineThreads, 0, st>>>(prm);
+  attn_combine_kernel<DT, HD><<<static_cast<unsigned>(2 * sm_count()), kCombineThreads, 0, st>>>(prm);
   return check_launch("attn_combine_kernel");
 }
 
