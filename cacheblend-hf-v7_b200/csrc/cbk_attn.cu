@@ -123,6 +123,29 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
+// max of three (one instruction on sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float m;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+  return m;
+}
+
+// (d0, d1) = (a0, a1) * (b, b) + (c, c) as one packed fp32 pair instruction
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\tmov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+
+// (d0, d1) += (a0, a1) as one packed fp32 pair instruction
+__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1) {
+  asm("{\n\t.reg .b64 ra, rd;\n\t"
+      "mov.b64 rd, {%0, %1};\n\tmov.b64 ra, {%2, %3};\n\t"
+      "add.f32x2 rd, rd, ra;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(d0), "+f"(d1) : "f"(a0), "f"(a1));
+}
+
 // number of 128-key tiles a Q tile needs (its last token has the largest position)
 __device__ __forceinline__ int tile_key_tiles(const int64_t* pos, int64_t n_sel, int tok_per_tile, int tile) {
   const int64_t last = min(static_cast<int64_t>(tile + 1) * tok_per_tile, n_sel) - 1;
@@ -425,8 +448,16 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const bool full = __all_sync(0xffffffffu, lim >= kBN - 1);
         float mx = -INFINITY;
         if (full) {
+          // four independent chains of three-input max: 64 instructions, short dependency chains
+          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-          for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+          for (int c = 0; c < kBN; c += 8) {
+            m0 = max3f(m0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+            m1 = max3f(m1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
+            m2 = max3f(m2, __uint_as_float(s[c + 4]), __uint_as_float(s[c + 5]));
+            m3 = max3f(m3, __uint_as_float(s[c + 6]), __uint_as_float(s[c + 7]));
+          }
+          mx = max3f(m0, m1, fmaxf(m2, m3));
         } else {
 #pragma unroll
           for (int c = 0; c < kBN; ++c)
@@ -443,6 +474,8 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           rescale = true;
         }
         float rs = 0.f;
+        float ra0 = 0.f, ra1 = 0.f, rb0 = 0.f, rb1 = 0.f;   // packed partial row sums
+        const float neg_m = -m_used;
 #pragma unroll
         for (int c4 = 0; c4 < kBN / 32; ++c4) {
           uint32_t pk[16];
@@ -450,9 +483,11 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const int c = c4 * 32 + 2 * e;
-              const float p0 = ex2(__uint_as_float(s[c]) * sl2 - m_used);
-              const float p1 = ex2(__uint_as_float(s[c + 1]) * sl2 - m_used);
-              rs += p0 + p1;
+              float x0, x1;
+              fma2(x0, x1, __uint_as_float(s[c]), __uint_as_float(s[c + 1]), sl2, neg_m);
+              const float p0 = ex2(x0), p1 = ex2(x1);
+              if (e & 1) add2(rb0, rb1, p0, p1);
+              else add2(ra0, ra1, p0, p1);
               pk[e] = pack2<DT>(p0, p1);
             }
           } else {
@@ -468,6 +503,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           // P chunk c4 -> columns [16 c4, 16 c4 + 16) (S was read completely above)
           tmem_st16(tS + c4 * 16, pk);
         }
+        rs += (ra0 + ra1) + (rb0 + rb1);
         l_sum = l_sum * alpha + rs;
         if (__any_sync(0xffffffffu, rescale)) {
           // O is stable: the commit behind this tile's S(j) covered PV(j-1)
