@@ -44,6 +44,9 @@ SIGNATURES = {
     "cbk_partial_attn_workspace_bytes": (_sz, [_i64, _i64, _i32, _i32, _i32]),
     "cbk_partial_attn": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _f32, _i32, _vp,
                                 _vp, _sz, _i32, _vp, _vp]),
+    "cbk_add_rmsnorm": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _f32, _i64, _i32, _i32,
+                               _vp, _i64, _vp, _vp]),
+    "cbk_silu_mul": (_i32, [_vp, _i64, _vp, _i64, _i64, _i32, _i32, _vp, _i64, _vp]),
 }
 
 

@@ -14,7 +14,10 @@ data-parallel stages on the sm_100a kernels:
   (e)     ``partial_attn_kernel``  selected queries against the full fused KV
           on tcgen05 tensor cores (causal by position, GQA without expansion).
 
-Projections, norms and MLPs stay in the HF modules (cuBLAS through torch).
+Projections stay in the HF modules (cuBLAS through torch).  RMSNorm with the
+residual add folded in, and SiLU(gate) * up, run as one-pass libcbk kernels
+with the HF modules' 16-bit roundings (``add_rmsnorm``, ``silu_mul``); the
+check layer's residual gather rides in the same norm launch.
 The returned cache holds views of the fused buffers (no staging copy).
 ``fuse_full_recompute`` / ``fuse_full_reuse`` / ``fuse_prefix_cache`` keep the
 reference's behaviour (they are the ratio==0 / ratio>=1 / single-chunk
@@ -122,6 +125,32 @@ class _Geometry:
         self.scaling = float(attn0.scaling)
 
 
+_RMSNORMS = ("MistralRMSNorm", "LlamaRMSNorm")
+_MLPS = ("MistralMLP", "LlamaMLP")
+_SILUS = ("SiLUActivation", "SiLU")
+
+
+def _norm(mod, x, delta=None, rows=None, sum_out=None, status=None):
+    """mod(x[rows] + delta), also writing the sum to sum_out: the decoder
+    layer's residual add plus its RMSNorm (MistralDecoderLayer.forward)."""
+    if type(mod).__name__ in _RMSNORMS and mod.weight.dtype == x.dtype:
+        return ops.add_rmsnorm(x, mod.weight, mod.variance_epsilon, delta=delta, rows=rows,
+                               sum_out=sum_out, status=status)
+    s = x if rows is None else x.index_select(x.dim() - 2, rows)
+    if delta is not None:
+        s = s + delta
+    if sum_out is not None:
+        sum_out.copy_(s)
+    return mod(s)
+
+
+def _mlp(layer, hn):
+    mlp = layer.mlp
+    if type(mlp).__name__ in _MLPS and type(mlp.act_fn).__name__ in _SILUS:
+        return mlp.down_proj(ops.silu_mul(mlp.gate_proj(hn), mlp.up_proj(hn)))
+    return mlp(hn)
+
+
 def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_mode, ws, reuse,
                      tag=""):
     """q/k/v projections -> (b)+(d) RoPE + scatter into the fused cache ->
@@ -135,10 +164,6 @@ def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_
     a = ops.partial_attn(q_rot, kc, vc, pos, geo.n_q, geo.n_kv, geo.head_dim, geo.scaling,
                          status=status, workspace=ws, reuse_plan=reuse, timer_tag=tag)
     return attn.o_proj(a.unsqueeze(0)), k_pre
-
-
-def _mlp_block(layer, h):
-    return h + layer.mlp(layer.post_attention_layernorm(h))
 
 
 def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
@@ -213,20 +238,23 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
                 raise ValueError(f"input_ids has {ids.shape[1]} tokens, chunks have {S}")
         lw._pre_rope_k = {}
         pos_all = torch.arange(S, device=device, dtype=torch.int64)
-        h = inner.embed_tokens(ids)
+        h = inner.embed_tokens(ids)     # residual stream; updated in place by the fused norms
+        m = None                        # pending MLP output, added by the next norm
 
         ws_dense = ops.attn_workspace(S, S, geo.n_q, geo.n_kv, geo.head_dim, device) if ck else None
         for li in range(ck):                                  # dense layers (one shared plan)
             layer = inner.layers[li]
-            a, _ = _attention_block(layer, geo, layer.input_layernorm(h), pos_all, S, rope,
+            hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None,
+                       status=status)
+            a, _ = _attention_block(layer, geo, hn, pos_all, S, rope,
                                     fused_k[li], fused_v[li], False, status, rope_mode, ws_dense, li > 0,
                                     tag="_dense")
-            h = _mlp_block(layer, h + a)
+            m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=a, sum_out=h, status=status))
 
         # check layer: full projections, HKVD, then sparse from here on
         layer = inner.layers[ck]
         attn = layer.self_attn
-        hn = layer.input_layernorm(h)
+        hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None, status=status)
         q = attn.q_proj(hn)
         k_pre = attn.k_proj(hn)
         v = attn.v_proj(hn)
@@ -237,16 +265,19 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
         ws_sparse = ops.attn_workspace(k_sel, S, geo.n_q, geo.n_kv, geo.head_dim, device)
         a = ops.partial_attn(q_rot, fused_k[ck], fused_v[ck], idx, geo.n_q, geo.n_kv, geo.head_dim,
                              geo.scaling, status=status, workspace=ws_sparse, reuse_plan=False)
-        hs = h.index_select(1, idx) + attn.o_proj(a.unsqueeze(0))
-        hs = _mlp_block(layer, hs)
+        # selected residual rows gathered inside the norm launch
+        o = attn.o_proj(a.unsqueeze(0))
+        hs = torch.empty_like(o)
+        m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=o, rows=idx, sum_out=hs, status=status))
 
         for li in range(ck + 1, n_layers):                    # sparse layers
             layer = inner.layers[li]
-            a, _ = _attention_block(layer, geo, layer.input_layernorm(hs), idx, S, rope,
+            hn = _norm(layer.input_layernorm, hs, delta=m, sum_out=hs, status=status)
+            a, _ = _attention_block(layer, geo, hn, idx, S, rope,
                                     fused_k[li], fused_v[li], False, status, rope_mode, ws_sparse, True)
-            hs = _mlp_block(layer, hs + a)
+            m = _mlp(layer, _norm(layer.post_attention_layernorm, hs, delta=a, sum_out=hs, status=status))
 
-        logits_sparse = lw.model.lm_head(inner.norm(hs))      # (1, k, vocab)
+        logits_sparse = lw.model.lm_head(_norm(inner.norm, hs, delta=m, status=status))   # (1, k, vocab)
         logits = torch.zeros((1, S, logits_sparse.shape[-1]), dtype=logits_sparse.dtype, device=device)
         logits[0].index_copy_(0, idx, logits_sparse[0])
 

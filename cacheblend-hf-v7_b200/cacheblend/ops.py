@@ -289,3 +289,68 @@ def partial_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, 
                                        int(bool(reuse_plan)), _vp(status), _stream(dev)),
                 "cbk_partial_attn")
     return out
+
+
+# ---------------------------------------------------------------------------
+# decoder-layer row kernels (RMSNorm with residual add, SiLU * up)
+# ---------------------------------------------------------------------------
+def add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, delta: torch.Tensor | None = None,
+                rows: torch.Tensor | None = None, sum_out: torch.Tensor | None = None,
+                out: torch.Tensor | None = None, status=None) -> torch.Tensor:
+    """HF RMSNorm of ``s`` = x (rows gathered by ``rows`` when given) plus ``delta``
+    (16-bit residual add), in one pass.  ``s`` is written to ``sum_out`` when
+    given (it may be ``x`` itself when ``rows`` is None).  x: [..., cols]; the
+    result has delta's / the gathered row count and x's last dimension."""
+    dev = require_cuda(x, weight, delta, rows, sum_out, out)
+    x2 = _rows(x, "x")
+    cols = x2.shape[1]
+    if weight.dtype != x.dtype or weight.numel() != cols:
+        raise ValueError(f"add_rmsnorm: weight must be {x.dtype}[{cols}], got {weight.dtype}{list(weight.shape)}")
+    w = weight.contiguous()
+    if rows is not None:
+        if rows.dtype != torch.int64:
+            raise ValueError("add_rmsnorm: rows must be int64")
+        rows = rows.contiguous()
+        n = rows.numel()
+    else:
+        n = x2.shape[0]
+    d2 = None
+    if delta is not None:
+        if delta.dtype != x.dtype or delta.shape[-1] != cols or delta.numel() != n * cols:
+            raise ValueError(f"add_rmsnorm: delta must be {x.dtype} with {n} rows of {cols}")
+        d2 = _rows(delta, "delta")
+    lead = (delta.shape[:-1] if delta is not None else
+            (x.shape[:-1] if rows is None else (1, n) if x.dim() == 3 else (n,)))
+    if out is None:
+        out = torch.empty((*lead, cols), dtype=x.dtype, device=dev)
+    o2 = out.view(-1, cols)
+    s2 = None
+    if sum_out is not None:
+        if sum_out.dtype != x.dtype or sum_out.numel() != n * cols:
+            raise ValueError(f"add_rmsnorm: sum_out must be {x.dtype} with {n} rows of {cols}")
+        if rows is not None and sum_out.data_ptr() == x2.data_ptr():
+            raise ValueError("add_rmsnorm: sum_out may alias x only without a row gather")
+        s2 = sum_out.view(-1, cols)
+    with TIMES.span("add_rmsnorm", dev):
+        N.check(N.LIB.cbk_add_rmsnorm(_vp(x2), x2.stride(0), x2.shape[0], _vp(rows), _vp(d2),
+                                      d2.stride(0) if d2 is not None else 0, _vp(s2),
+                                      s2.stride(0) if s2 is not None else 0, _vp(w), float(eps), n, cols,
+                                      dtype_code(x.dtype), _vp(o2), o2.stride(0), _vp(status), _stream(dev)),
+                "cbk_add_rmsnorm")
+    return out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """round16(silu(gate)) * up with the 16-bit roundings of torch's SiLU and mul."""
+    dev = require_cuda(gate, up, out)
+    if gate.shape != up.shape or gate.dtype != up.dtype:
+        raise ValueError(f"silu_mul: gate {gate.dtype}{list(gate.shape)} vs up {up.dtype}{list(up.shape)}")
+    g2, u2 = _rows(gate, "gate"), _rows(up, "up")
+    if out is None:
+        out = torch.empty(gate.shape, dtype=gate.dtype, device=dev)
+    o2 = out.view(-1, gate.shape[-1])
+    with TIMES.span("silu_mul", dev):
+        N.check(N.LIB.cbk_silu_mul(_vp(g2), g2.stride(0), _vp(u2), u2.stride(0), g2.shape[0], g2.shape[1],
+                                   dtype_code(gate.dtype), _vp(o2), o2.stride(0), _stream(dev)),
+                "cbk_silu_mul")
+    return out

@@ -744,59 +744,95 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
 }
 
 // ---------------------------------------------------------------------------
-// Merge the partial results of split tiles.  Work unit = (split tile, group of
-// kCombineRows rows), one warp per row; the units are spread over a fixed grid
-// from the plan's list of split tiles, so no CTA is spent on unsplit tiles.  A
-// row of a slot is HD contiguous fp16, so every load is coalesced.  One pass
-// with a running maximum:
+// Merge the partial results of split tiles.  One warp per row of a split tile
+// (rows come from the plan's list of split tiles, so no work is spent on
+// unsplit tiles).  Lane c first holds chunk c's (m, l), so the row maximum and
+// the weight sum are warp reductions; then the O rows of the chunks (HD
+// contiguous fp16 each, coalesced) are read four at a time with the loads
+// issued back to back:
 //   O = sum_c w_c Ohat_c / sum_c w_c,  w_c = l_c 2^(m_c - M),  Ohat_c = O_c / l_c.
 // ---------------------------------------------------------------------------
 constexpr int kCombineThreads = 256;
 constexpr int kCombineRows = kCombineThreads / 32;
-constexpr int kCombineUnitsPerTile = kBM / kCombineRows;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
 
 template <int DT, int HD>
 __global__ void __launch_bounds__(kCombineThreads)
 attn_combine_kernel(const AttnParams prm) {
   constexpr int kPerLane = HD / 32;   // 4 (HD 128) or 2 (HD 64) elements per lane
+  constexpr int kInFlight = 4;        // O rows loaded per batch
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // every attention CTA has finished: rewind the item queue for the next call
   if (blockIdx.x == 0 && threadIdx.x == 0) *prm.queue = 0;
   if (prm.plan->error) return;
   const int C = prm.plan->chunk;
-  const int n_units = prm.plan->n_split * kCombineUnitsPerTile;
-  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-    const int ti = prm.split_list[u / kCombineUnitsPerTile];
+  const int n_rows = prm.plan->n_split * kBM;
+  for (int u = blockIdx.x * kCombineRows + warp; u < n_rows; u += gridDim.x * kCombineRows) {
+    const int ti = prm.split_list[u / kBM];
+    const int row = u % kBM;
     const int kvh = ti / prm.n_tiles, tile = ti % prm.n_tiles;
-    const int row = (u % kCombineUnitsPerTile) * kCombineRows + warp;
     const int64_t tok = static_cast<int64_t>(tile) * prm.tok_per_tile + row / prm.group;
     if (tok >= prm.n_sel) continue;   // padding row of the last tile
-    const int slot0 = prm.tile_base[ti];
+    const int64_t slot0 = prm.tile_base[ti];
     const int nc = (tile_key_tiles(prm.pos, prm.n_sel, prm.tok_per_tile, tile) + C - 1) / C;
+    // row maximum over the chunks with visible keys (a chunk without any has l = 0)
+    float M = -INFINITY;
+    for (int c0 = 0; c0 < nc; c0 += 32) {
+      float m = -INFINITY;
+      if (c0 + lane < nc) {
+        const float2 ml = prm.part_ml[(slot0 + c0 + lane) * kBM + row];
+        if (ml.y > 0.f) m = ml.x;
+      }
+      M = fmaxf(M, warp_max(m));
+    }
     float acc[kPerLane];
 #pragma unroll
     for (int e = 0; e < kPerLane; ++e) acc[e] = 0.f;
-    float M = -INFINITY, wsum = 0.f;
-    for (int c = 0; c < nc; ++c) {
-      const int64_t slot = slot0 + c;
-      const float2 ml = prm.part_ml[slot * kBM + row];
-      if (ml.y > 0.f) {                     // a chunk without visible keys has l = 0
-        const float Mn = fmaxf(M, ml.x);
-        const float r = ex2(M - Mn);        // 0 on the first visible chunk
-        const float w = ml.y * ex2(ml.x - Mn);
-        wsum = wsum * r + w;
-        const __half* po = prm.part_o + (slot * kBM + row) * HD + lane * kPerLane;
-        if constexpr (kPerLane == 4) {
-          const uint2 raw = *reinterpret_cast<const uint2*>(po);
-          const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-          const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-          acc[0] = acc[0] * r + w * a.x; acc[1] = acc[1] * r + w * a.y;
-          acc[2] = acc[2] * r + w * b.x; acc[3] = acc[3] * r + w * b.y;
-        } else {
-          const float2 a = __half22float2(*reinterpret_cast<const __half2*>(po));
-          acc[0] = acc[0] * r + w * a.x; acc[1] = acc[1] * r + w * a.y;
+    float wsum = 0.f;
+    for (int c0 = 0; c0 < nc; c0 += 32) {
+      const int cn = min(32, nc - c0);
+      float w = 0.f;
+      if (lane < cn) {
+        const float2 ml = prm.part_ml[(slot0 + c0 + lane) * kBM + row];
+        if (ml.y > 0.f) w = ml.y * ex2(ml.x - M);
+      }
+      wsum += warp_sum(w);
+      for (int c = 0; c < cn; c += kInFlight) {
+        float wc[kInFlight];
+        uint32_t raw[kInFlight][kPerLane / 2];
+#pragma unroll
+        for (int q = 0; q < kInFlight; ++q) {
+          const int cc = min(c + q, cn - 1);     // in range; weight 0 past the end
+          const float wq = __shfl_sync(0xffffffffu, w, cc);
+          wc[q] = (c + q < cn) ? wq : 0.f;
+          const __half* po = prm.part_o + ((slot0 + c0 + cc) * kBM + row) * HD + lane * kPerLane;
+          if constexpr (kPerLane == 4) {
+            const uint2 r = *reinterpret_cast<const uint2*>(po);
+            raw[q][0] = r.x;
+            raw[q][1] = r.y;
+          } else {
+            raw[q][0] = *reinterpret_cast<const uint32_t*>(po);
+          }
         }
-        M = Mn;
+#pragma unroll
+        for (int q = 0; q < kInFlight; ++q)
+#pragma unroll
+          for (int e = 0; e < kPerLane / 2; ++e) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&raw[q][e]));
+            acc[2 * e] = fmaf(wc[q], f.x, acc[2 * e]);
+            acc[2 * e + 1] = fmaf(wc[q], f.y, acc[2 * e + 1]);
+          }
       }
     }
     const float inv = 1.f / wsum;
@@ -930,7 +966,11 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   const int grid = std::min(lay.max_items, sm_count());   // persistent: one CTA per SM
   kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(mq, mk, mv, prm);
   if (int rc = check_launch("partial_attn_kernel")) return rc;
-  attn_combine_kernel<DT, HD><<<static_cast<unsigned>(2 * sm_count()), kCombineThreads, 0, st>>>(prm);
+  // one warp per row of a split tile; at most every tile is split
+  const int64_t max_rows = static_cast<int64_t>(n_kv_heads) * lay.n_tiles * kBM;
+  const int comb_grid = static_cast<int>(std::min<int64_t>((max_rows + kCombineRows - 1) / kCombineRows,
+                                                           16 * sm_count()));
+  attn_combine_kernel<DT, HD><<<static_cast<unsigned>(comb_grid), kCombineThreads, 0, st>>>(prm);
   return check_launch("attn_combine_kernel");
 }
 

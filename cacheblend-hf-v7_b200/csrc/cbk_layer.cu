@@ -1,0 +1,207 @@
+// Row-wise kernels of the decoder layer around the recompute path, each one
+// HBM pass that reproduces the rounding of the HF modules it replaces
+// (transformers MistralRMSNorm / LlamaRMSNorm, MistralMLP / LlamaMLP act * up,
+// and the decoder layer's residual adds):
+//
+//   add_rmsnorm   s   = x[src(r)] (+ delta[r])             16-bit add, rounded
+//                 out = w * round16(s * rsqrt(mean(s^2) + eps))   rounded
+//                 (the sum s is written back when a residual is wanted; src(r)
+//                 = rows[r] gathers residual rows by index)
+//   silu_mul      out = round16(round16(g / (1 + exp(-g))) * u)
+//
+// Squares of 16-bit values are exact in fp32; the row sum runs in a fixed
+// order (per thread, then warp butterfly, then warps in order), so a row's
+// result does not depend on the launch.  Only that order differs from torch's
+// reduction, which moves the mean by at most an fp32 ulp or so.
+#include <algorithm>
+
+#include "cbk_common.cuh"
+
+namespace cbk {
+
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxVec = 4;       // 16-byte vectors per thread: cols <= 256 * 8 * 4 = 8192
+
+template <int DT>
+__global__ void __launch_bounds__(kNormThreads)
+add_rmsnorm_kernel(const uint16_t* x, int64_t x_stride, int64_t x_rows, const int64_t* __restrict__ rows,
+                   const uint16_t* delta, int64_t delta_stride, uint16_t* sum_out,
+                   int64_t sum_stride, const uint16_t* __restrict__ weight, float eps, int cols,
+                   uint16_t* __restrict__ out, int64_t out_stride, int64_t n_rows, int32_t* status) {
+  using E = Elem<DT>;
+  __shared__ float s_warp[kNormThreads / 32];
+  const int64_t r = blockIdx.x;
+  if (r >= n_rows) return;
+  int64_t src = r;
+  if (rows) {
+    src = rows[r];
+    if (src < 0 || src >= x_rows) {
+      report(status, CBK_STATUS_BAD_INDEX);
+      return;
+    }
+  }
+  const int n_vec = cols / 8;
+  const uint16_t* xr = x + src * x_stride;
+  uint4 v[kNormMaxVec];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int c = (i * kNormThreads + threadIdx.x);
+    if (c < n_vec) {
+      uint4 a = ld_vec(xr + c * 8);
+      if (delta) {
+        const uint4 b = ld_vec(delta + r * delta_stride + c * 8);
+        const uint16_t* ha = reinterpret_cast<const uint16_t*>(&a);
+        const uint16_t* hb = reinterpret_cast<const uint16_t*>(&b);
+        uint4 s;
+        uint16_t* hs = reinterpret_cast<uint16_t*>(&s);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) hs[e] = E::from_f(E::to_f(ha[e]) + E::to_f(hb[e]));
+        a = s;
+      }
+      if (sum_out) st_vec(sum_out + r * sum_stride + c * 8, a);
+      const uint16_t* h = reinterpret_cast<const uint16_t*>(&a);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float f = E::to_f(h[e]);
+        ss = fmaf(f, f, ss);
+      }
+      v[i] = a;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) s_warp[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) tot += s_warp[w];
+  const float rstd = rsqrtf(tot * (1.f / static_cast<float>(cols)) + eps);
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int c = (i * kNormThreads + threadIdx.x);
+    if (c < n_vec) {
+      const uint4 wv = ld_vec(weight + c * 8);
+      const uint16_t* h = reinterpret_cast<const uint16_t*>(&v[i]);
+      const uint16_t* hw = reinterpret_cast<const uint16_t*>(&wv);
+      uint4 o;
+      uint16_t* ho = reinterpret_cast<uint16_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float y = round16<DT>(E::to_f(h[e]) * rstd);
+        ho[e] = E::from_f(E::to_f(hw[e]) * y);
+      }
+      st_vec(out + r * out_stride + c * 8, o);
+    }
+  }
+}
+
+template <int DT>
+__global__ void silu_mul_kernel(const uint16_t* __restrict__ g, int64_t g_stride, const uint16_t* __restrict__ u,
+                                int64_t u_stride, int cols, int64_t n_rows, uint16_t* __restrict__ out,
+                                int64_t out_stride) {
+  using E = Elem<DT>;
+  const int n_vec = cols / 8;
+  const int64_t total = n_rows * n_vec;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / n_vec;
+    const int c = static_cast<int>(i - r * n_vec) * 8;
+    const uint4 a = ld_stream(g + r * g_stride + c);
+    const uint4 b = ld_stream(u + r * u_stride + c);
+    const uint16_t* ha = reinterpret_cast<const uint16_t*>(&a);
+    const uint16_t* hb = reinterpret_cast<const uint16_t*>(&b);
+    uint4 o;
+    uint16_t* ho = reinterpret_cast<uint16_t*>(&o);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float xg = E::to_f(ha[e]);
+      const float act = round16<DT>(xg / (1.0f + expf(-xg)));
+      ho[e] = E::from_f(act * E::to_f(hb[e]));
+    }
+    st_vec(out + r * out_stride + c, o);
+  }
+}
+
+int sm_count_layer() {
+  static int cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+}  // namespace cbk
+
+using namespace cbk;
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+extern "C" int cbk_add_rmsnorm(const void* x, int64_t x_stride, int64_t x_rows, const int64_t* rows,
+                               const void* delta, int64_t delta_stride, void* sum_out, int64_t sum_stride,
+                               const void* weight, float eps, int64_t n_rows, int cols, int dtype, void* out,
+                               int64_t out_stride, int32_t* status, void* stream) {
+  if (dtype != CBK_BF16 && dtype != CBK_F16)
+    return set_error(CBK_ERR_UNSUPPORTED, "cbk_add_rmsnorm: dtype %d not supported", dtype);
+  if (n_rows < 0 || cols <= 0 || cols % 8 != 0 || cols > kNormThreads * 8 * kNormMaxVec)
+    return set_error(CBK_ERR_INVALID, "cbk_add_rmsnorm: need cols %% 8 == 0 and 0 < cols <= %d (cols %d)",
+                     kNormThreads * 8 * kNormMaxVec, cols);
+  if (!x || !weight || !out)
+    return set_error(CBK_ERR_INVALID, "cbk_add_rmsnorm: null pointer argument");
+  if (x_stride < cols || out_stride < cols || (delta && delta_stride < cols) || (sum_out && sum_stride < cols))
+    return set_error(CBK_ERR_INVALID, "cbk_add_rmsnorm: a row stride is shorter than the row");
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(out) || (delta && !aligned16(delta)) ||
+      (sum_out && !aligned16(sum_out)) || (x_stride | out_stride | (delta ? delta_stride : 0) |
+                                           (sum_out ? sum_stride : 0)) % 8 != 0)
+    return set_error(CBK_ERR_INVALID, "cbk_add_rmsnorm: pointers must be 16-byte aligned, strides multiples of 8");
+  if (!rows && n_rows > x_rows)
+    return set_error(CBK_ERR_INVALID, "cbk_add_rmsnorm: %lld rows requested from %lld", (long long)n_rows,
+                     (long long)x_rows);
+  if (n_rows == 0) return CBK_OK;
+  if (n_rows > 0x7fffffffLL) return set_error(CBK_ERR_INVALID, "cbk_add_rmsnorm: too many rows");
+  auto st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(n_rows);
+  auto xs = static_cast<const uint16_t*>(x);
+  auto ds = static_cast<const uint16_t*>(delta);
+  auto ss = static_cast<uint16_t*>(sum_out);
+  auto ws = static_cast<const uint16_t*>(weight);
+  auto os = static_cast<uint16_t*>(out);
+  if (dtype == CBK_BF16)
+    add_rmsnorm_kernel<CBK_BF16><<<grid, kNormThreads, 0, st>>>(xs, x_stride, x_rows, rows, ds, delta_stride, ss, sum_stride,
+                                                                ws, eps, cols, os, out_stride, n_rows, status);
+  else
+    add_rmsnorm_kernel<CBK_F16><<<grid, kNormThreads, 0, st>>>(xs, x_stride, x_rows, rows, ds, delta_stride, ss, sum_stride,
+                                                               ws, eps, cols, os, out_stride, n_rows, status);
+  return check_launch("add_rmsnorm_kernel");
+}
+
+extern "C" int cbk_silu_mul(const void* gate, int64_t gate_stride, const void* up, int64_t up_stride,
+                            int64_t n_rows, int cols, int dtype, void* out, int64_t out_stride, void* stream) {
+  if (dtype != CBK_BF16 && dtype != CBK_F16)
+    return set_error(CBK_ERR_UNSUPPORTED, "cbk_silu_mul: dtype %d not supported", dtype);
+  if (n_rows < 0 || cols <= 0 || cols % 8 != 0)
+    return set_error(CBK_ERR_INVALID, "cbk_silu_mul: need cols %% 8 == 0 (cols %d)", cols);
+  if (!gate || !up || !out) return set_error(CBK_ERR_INVALID, "cbk_silu_mul: null pointer argument");
+  if (gate_stride < cols || up_stride < cols || out_stride < cols)
+    return set_error(CBK_ERR_INVALID, "cbk_silu_mul: a row stride is shorter than the row");
+  if (!aligned16(gate) || !aligned16(up) || !aligned16(out) || (gate_stride | up_stride | out_stride) % 8 != 0)
+    return set_error(CBK_ERR_INVALID, "cbk_silu_mul: pointers must be 16-byte aligned, strides multiples of 8");
+  if (n_rows == 0) return CBK_OK;
+  auto st = static_cast<cudaStream_t>(stream);
+  const int64_t total = n_rows * (cols / 8);
+  const int threads = 256;
+  const int64_t want = (total + threads - 1) / threads;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(want, 8LL * sm_count_layer()));
+  auto g = static_cast<const uint16_t*>(gate);
+  auto u = static_cast<const uint16_t*>(up);
+  auto o = static_cast<uint16_t*>(out);
+  if (dtype == CBK_BF16)
+    silu_mul_kernel<CBK_BF16><<<grid, threads, 0, st>>>(g, gate_stride, u, up_stride, cols, n_rows, o, out_stride);
+  else
+    silu_mul_kernel<CBK_F16><<<grid, threads, 0, st>>>(g, gate_stride, u, up_stride, cols, n_rows, o, out_stride);
+  return check_launch("silu_mul_kernel");
+}

@@ -181,6 +181,30 @@ int cbk_partial_attn(const void* q, const void* k, const void* v, const int64_t*
                      float scale, int dtype, void* out, void* workspace, size_t workspace_bytes,
                      int reuse_plan, int32_t* status, void* stream);
 
+/* Decoder-layer row kernels around the recompute path.  They replace the HF
+ * modules that fuse_selective runs between its projections (transformers
+ * MistralRMSNorm/LlamaRMSNorm.forward, MistralMLP/LlamaMLP act_fn(gate) * up,
+ * and the residual adds of MistralDecoderLayer.forward) with the same 16-bit
+ * roundings, one HBM pass each.
+ *
+ * cbk_add_rmsnorm: for r < n_rows, with s = x[src] (src = rows ? rows[r] : r,
+ * 0 <= src < x_rows) plus delta[r] when delta is not NULL (sum rounded to 16
+ * bits, like torch's bf16 add):
+ *   out[r] = weight * round16(s * rsqrt(mean(s^2) + eps))   (rounded to 16 bits)
+ * and sum_out[r] = s when sum_out is not NULL (sum_out may equal x only when
+ * rows is NULL).  cols % 8 == 0, cols <= 8192; 16-byte aligned pointers, row
+ * strides (elements) multiples of 8.  An out-of-range rows[r] sets
+ * CBK_STATUS_BAD_INDEX and leaves row r untouched.
+ *
+ * cbk_silu_mul: out[r][c] = round16(round16(g / (1 + exp(-g))) * up[r][c]),
+ * g = gate[r][c] (torch's silu in fp32, then the 16-bit product). */
+int cbk_add_rmsnorm(const void* x, int64_t x_stride, int64_t x_rows, const int64_t* rows,
+                    const void* delta, int64_t delta_stride, void* sum_out, int64_t sum_stride,
+                    const void* weight, float eps, int64_t n_rows, int cols, int dtype, void* out,
+                    int64_t out_stride, int32_t* status, void* stream);
+int cbk_silu_mul(const void* gate, int64_t gate_stride, const void* up, int64_t up_stride,
+                 int64_t n_rows, int cols, int dtype, void* out, int64_t out_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,20 @@ def test_abi_version_and_pure_helpers():
     ("cbk_kv_deviation(16, 12, 16, 16, 1, 8, 12, 0, 16, None)", -1),
     ("cbk_hkvd_select(16, 8, 16, 16, 1, 8, 8, 0, 2, 1, 16, 16, 4, None, None)", -4),
     ("cbk_rope_rows(16, 16, 4, 2, 64, 1, 16, 8, 16, 5, None, None)", -1),
+    # add_rmsnorm(x, xs, x_rows, rows, delta, ds, sum, ss, w, eps, n_rows, cols, dtype, out, os, status, stream)
+    ("cbk_add_rmsnorm(16, 64, 4, None, None, 0, None, 0, 16, 1e-5, 4, 64, 3, 16, 64, None, None)", -2),
+    ("cbk_add_rmsnorm(16, 64, 4, None, None, 0, None, 0, 16, 1e-5, 4, 60, 0, 16, 64, None, None)", -1),
+    ("cbk_add_rmsnorm(16, 9000, 4, None, None, 0, None, 0, 16, 1e-5, 4, 8200, 0, 16, 9000, None, None)", -1),
+    ("cbk_add_rmsnorm(None, 64, 4, None, None, 0, None, 0, 16, 1e-5, 4, 64, 0, 16, 64, None, None)", -1),
+    ("cbk_add_rmsnorm(16, 32, 4, None, None, 0, None, 0, 16, 1e-5, 4, 64, 0, 16, 64, None, None)", -1),
+    ("cbk_add_rmsnorm(18, 64, 4, None, None, 0, None, 0, 16, 1e-5, 4, 64, 0, 16, 64, None, None)", -1),
+    ("cbk_add_rmsnorm(16, 64, 4, None, None, 0, None, 0, 16, 1e-5, 5, 64, 0, 16, 64, None, None)", -1),
+    ("cbk_add_rmsnorm(16, 64, 4, None, None, 0, None, 0, 16, 1e-5, 0, 64, 0, 16, 64, None, None)", 0),
+    ("cbk_silu_mul(16, 64, 16, 64, 4, 64, 2, 16, 64, None)", -2),
+    ("cbk_silu_mul(16, 64, 16, 64, 4, 12, 0, 16, 64, None)", -1),
+    ("cbk_silu_mul(16, 64, None, 64, 4, 64, 0, 16, 64, None)", -1),
+    ("cbk_silu_mul(16, 64, 16, 60, 4, 64, 0, 16, 64, None)", -1),
+    ("cbk_silu_mul(16, 64, 16, 64, 0, 64, 0, 16, 64, None)", 0),
 ])
 def test_validation_errors_before_any_launch(call, code):
     from cacheblend import _native as N
