@@ -309,7 +309,7 @@ def run_ours(args):
         "gpu_launches": launches,
         "clocks": clk,
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:       # host-core baseline: rank 0 at N=1 only
         res["cpu_baseline"] = cpu_baseline(model, lw, store, reqs[0], budget_s=args.cpu_budget)
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -392,6 +392,22 @@ def run_reference(args):
     import numpy as np
     if int(os.environ.get("RANK", "0")) != 0:
         return
+    # torchrun sets OMP_NUM_THREADS=1 for every rank; the reference arm runs on
+    # rank 0 alone and may use every host core
+    try:
+        from threadpoolctl import threadpool_limits
+        limiter = threadpool_limits(limits=os.cpu_count() or 1)
+    except Exception:
+        limiter = None
+    try:
+        _run_reference(args)
+    finally:
+        if limiter is not None:
+            limiter.restore_original_limits()
+
+
+def _run_reference(args):
+    import numpy as np
     from oracle import model as om
     rng = np.random.default_rng(0)
     c = MISTRAL_7B
