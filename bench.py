@@ -552,6 +552,204 @@ def run_kv_microbench(args):
         "kernels": out, "hbm_peak_gbs": hbm, "hbm_peak_kind": src, "clocks": clk}), flush=True)
 
 
+LLAMA3_70B = dict(layers=80, n_q=64, n_kv=8, head_dim=128, theta=5e5)
+SH_CHUNKS, SH_CHUNK_LEN, SH_QUERY_LEN, SH_RATIO = 64, 2048, 256, 0.15
+
+
+def run_kv_sharded(args):
+    """Llama-3-70B-shaped 128K blended prefill hot path, KV heads sharded over
+    the ranks (rank r keeps KV heads [r*8/N, (r+1)*8/N) and their q heads).
+    Per step: (a)+(b) assemble of every cached layer, the dense layer before the
+    check layer (fresh rows for all tokens), (c) HKVD: partial deviation over
+    this rank's heads, NCCL all-gather of the S fp32 partials, the same top-K
+    on every rank, then per sparse layer (b)+(d) RoPE + scatter of the fresh
+    rows and (e) partial attention.  Projections / MLP would need tensor-parallel
+    all-reduces and are not on this path: the fresh Q/K/V rows are seeded
+    synthetic inputs (one set reused by every layer).  Total work is one request
+    whatever N is: strong scaling."""
+    import torch
+    import torch.distributed as dist
+    from cacheblend import ops
+    from cacheblend._timing import TIMES
+    from cacheblend.sharding import head_shard, sharded_hkvd_select
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    c = LLAMA3_70B
+    L, Hq, Hkv, D = args.sh_layers, c["n_q"], c["n_kv"], c["head_dim"]
+    ck = CHECK_LAYER
+    lo, hi = head_shard(Hkv, world, rank)
+    hkv = hi - lo
+    hq = hkv * (Hq // Hkv)
+    kvd = hkv * D
+    lens = [SH_CHUNK_LEN] * SH_CHUNKS + [SH_QUERY_LEN]
+    S = sum(lens)
+    k_sel = max(1, min(S, int(S * SH_RATIO)))
+    bf = torch.bfloat16
+
+    def randn(shape, seed):
+        g = torch.Generator(device=device).manual_seed(seed)
+        return torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(bf)
+
+    # per-layer chunk K/V of this rank's heads (chunks are row ranges of one buffer)
+    ck_k = [randn((S, kvd), 10_000 * rank + 2 * l) for l in range(L)]
+    ck_v = [randn((S, kvd), 10_000 * rank + 2 * l + 1) for l in range(L)]
+    starts = [0]
+    for n in lens:
+        starts.append(starts[-1] + n)
+    entries = [{"K": [ck_k[l][a:b].unsqueeze(0) for l in range(L)],
+                "V": [ck_v[l][a:b].unsqueeze(0) for l in range(L)]} for a, b in zip(starts, starts[1:])]
+    table = ops.ChunkTable(entries, range(ck, L), device)
+    inv_freq = 1.0 / (c["theta"] ** (torch.arange(0, D, 2, dtype=torch.float32, device=device) / D))
+    rope = ops.rope_table(inv_freq, S)
+    fused_k = torch.empty((L, S, kvd), dtype=bf, device=device)
+    fused_v = torch.empty_like(fused_k)
+    # recomputed check-layer K = cached + N(0, 0.05) on a random 20% of tokens
+    # (the token mask is common to all ranks: the same tokens are recomputed)
+    gm = torch.Generator(device=device).manual_seed(77)
+    mask = (torch.rand((S, 1), generator=gm, device=device) < 0.2).float()
+    k_fresh = (ck_k[ck].float() + randn((S, kvd), 10_000 * rank + 9_999).float() * 0.05 * mask).to(bf)
+    del mask
+    q_all, k_all, v_all = randn((S, hq * D), 5 + rank), randn((S, kvd), 6 + rank), randn((S, kvd), 7 + rank)
+    q_rows, k_rows, v_rows = q_all[:k_sel], k_all[:k_sel], v_all[:k_sel]
+    pos_all = torch.arange(S, device=device, dtype=torch.int64)
+    scale = D ** -0.5
+    ws_dense = ops.attn_workspace(S, S, hq, hkv, D, device)
+    ws_sparse = ops.attn_workspace(k_sel, S, hq, hkv, D, device)
+    q_dense = torch.empty((S, hq * D), dtype=bf, device=device)
+    q_sparse = torch.empty((k_sel, hq * D), dtype=bf, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(k_check):
+        ops.assemble_kv(table, ck, L, hkv, D, rope, fused_k, fused_v, status=status)
+        for li in range(ck):
+            ops.rope_scatter(q_all, k_all, v_all, pos_all, False, S, hq, hkv, D, rope, fused_k[li],
+                             fused_v[li], q_out=q_dense, status=status)
+            ops.partial_attn(q_dense, fused_k[li], fused_v[li], pos_all, hq, hkv, D, scale, status=status,
+                             workspace=ws_dense, reuse_plan=li > 0, timer_tag="_dense")
+        idx = sharded_hkvd_select(k_check, table, ck, k_sel)
+        for li in range(ck, L):
+            if li == ck:      # check layer: fresh rows gathered from the full-row projections
+                ops.rope_scatter(q_all, k_check, v_all, idx, True, S, hq, hkv, D, rope, fused_k[li],
+                                 fused_v[li], q_out=q_sparse, status=status)
+            else:
+                ops.rope_scatter(q_rows, k_rows, v_rows, idx, False, S, hq, hkv, D, rope, fused_k[li],
+                                 fused_v[li], q_out=q_sparse, status=status)
+            ops.partial_attn(q_sparse, fused_k[li], fused_v[li], idx, hq, hkv, D, scale, status=status,
+                             workspace=ws_sparse, reuse_plan=li > ck)
+        return idx
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        idx = step(k_fresh)
+    torch.cuda.synchronize()
+    # every rank must hold the identical selection
+    same = True
+    if world > 1:
+        allidx = torch.empty((world, k_sel), dtype=torch.int64, device=device)
+        dist.all_gather_into_tensor(allidx, idx)
+        same = bool((allidx == allidx[0:1]).all().item())
+
+    clocks = Clocks(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    TIMES.reset()
+    TIMES.active = True
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        idx = step(k_fresh)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    TIMES.active = False
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+    kern = TIMES.summary()
+    launches = sum(TIMES.launches.values())
+
+    # end to end: the check-layer K from pinned host memory, the selection back to the host
+    k_host = k_fresh.cpu().pin_memory()
+    k_dev = torch.empty_like(k_fresh)
+    barrier()
+    torch.cuda.synchronize()
+    e2e = []
+    for _ in range(args.steps):
+        a = time.perf_counter()
+        k_dev.copy_(k_host, non_blocking=True)
+        idx_host = step(k_dev).cpu()
+        e2e.append((time.perf_counter() - a) * 1e3)
+    barrier()
+    e2e_ms = max_over_ranks(sum(e2e) / len(e2e))
+    st = int(status.item())
+
+    idx_l = idx_host.tolist()
+    sel = sum(int(p) + 1 for p in idx_l)
+    fl_sp = 4 * hq * D * sel
+    fl_de = 4 * hq * D * (S * (S + 1) // 2)
+    n_sp, ms_sp = kern.get("partial_attn", (0, 0.0))
+    n_de, ms_de = kern.get("partial_attn_dense", (0, 0.0))
+    n_asm, asm_ms = kern.get("assemble_kv", (0, 0.0))
+    asm_bytes = (L - ck) * 2 * 2 * S * kvd * 2
+    hbm_peak, tf_burst, tf_sust, peak_src = load_peaks()
+    tf_sp = fl_sp / (ms_sp / n_sp * 1e-3) / 1e12 if n_sp else None
+    res = {
+        "metric": "KV-head-sharded blended-prefill hot path tokens/s (Llama-3-70B shape, 128K ctx)",
+        "value": round(S / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) chunk K/V and fresh rows; recomputed K = cached + N(0,0.05) on 20%)",
+        "config": {"workload": "llama70b-128k-sharded", "layers": L, "S": S, "k_selected": k_sel,
+                   "chunks": f"{SH_CHUNKS}x{SH_CHUNK_LEN}+{SH_QUERY_LEN}", "q_heads_per_rank": hq,
+                   "kv_heads_per_rank": hkv, "head_dim": D, "check_layer": ck,
+                   "parallelism": f"kv-heads/{world}", "exchange": "NCCL all_gather of S fp32 partials",
+                   "selection_identical_on_all_ranks": same, "status": st,
+                   "l2": "inputs larger than L2 (per-layer K/V buffers)"},
+        "e2e": {"value": round(S / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": S * kvd * 2, "d2h_bytes_per_step": k_sel * 8},
+        "roofline": {"kernel": "partial_attn_kernel", "bound": "tensor",
+                     "achieved": round(tf_sp, 1) if tf_sp else None, "peak": tf_sust, "unit": "TFLOP/s",
+                     "frac": round(tf_sp / tf_sust, 4) if tf_sp else None,
+                     "peak_kind": f"{peak_src} bf16 sustained", "flops_per_launch": fl_sp, "calls": n_sp,
+                     "avg_launch_ms": round(ms_sp / max(n_sp, 1), 4)},
+        "kernels": {
+            "assemble_kv": {"calls": n_asm, "avg_ms": round(asm_ms / max(n_asm, 1), 3), "bytes": asm_bytes,
+                            "GB/s": round(asm_bytes / (asm_ms / n_asm * 1e-3) / 1e9, 1) if n_asm else None},
+            "partial_attn_dense": {"calls": n_de, "avg_ms": round(ms_de / max(n_de, 1), 3),
+                                   "TFLOP/s": round(fl_de / (ms_de / n_de * 1e-3) / 1e12, 1) if n_de else None},
+            "hkvd_partial_plus_exchange": {k: round(v[1] / max(v[0], 1), 4) for k, v in kern.items()
+                                           if k in ("kv_deviation", "topk_select")},
+        },
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
 def run_attn_layers(args):
     """Partial attention alone at the Mistral-7B sparse-layer shape: S = 6208 keys,
     k = 931 selected rows (uniform random, last position included), 32 q / 8 KV heads,
@@ -609,10 +807,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=30.0)
     ap.add_argument("--workload", default="mistral7b-7k-blend",
-                    choices=["mistral7b-7k-blend", "kv-microbench", "attn-layers"])
+                    choices=["mistral7b-7k-blend", "kv-microbench", "attn-layers", "llama70b-128k-sharded"])
     ap.add_argument("--attn-layers", type=int, default=31)
     ap.add_argument("--attn-k", type=int, default=931, help="selected rows (6208 = dense causal)")
     ap.add_argument("--attn-dist", default="uniform", choices=["uniform", "tail"])
+    ap.add_argument("--sh-layers", type=int, default=80, help="layers of the sharded 128K workload")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -622,6 +821,8 @@ def main():
         run_kv_microbench(args)
     elif args.workload == "attn-layers":
         run_attn_layers(args)
+    elif args.workload == "llama70b-128k-sharded":
+        run_kv_sharded(args)
     else:
         run_ours(args)
 

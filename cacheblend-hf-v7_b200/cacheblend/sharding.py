@@ -37,7 +37,10 @@ def combine_partials(parts) -> torch.Tensor:
 
 def exchange_deviation(partial: torch.Tensor, group=None) -> torch.Tensor:
     """All-gather per-rank deviation partials (S,) fp32 and sum them in rank
-    order; every rank returns the same tensor."""
+    order; every rank returns the same tensor.  Without a process group (one
+    GPU) the partial is the total."""
+    if not (dist.is_available() and dist.is_initialized()):
+        return partial
     world = dist.get_world_size(group)
     if world == 1:
         return partial
