@@ -251,7 +251,7 @@ def run_ours(args):
     k_sel = len(idx_l)
     sc_bytes_sparse = k_sel * (cfg.hidden_size + 2 * kv_dim) * 2 * 2
     traffic = None
-    prof = os.path.join(ROOT, "profiles", "partial_attn_traffic.json")
+    prof = os.path.join(ROOT, "profiles", "partial_attn_kernel_mistral7b_7k_blend_traffic.json")
     if os.path.exists(prof):
         try:
             traffic = json.load(open(prof)).get("bytes_per_launch")
