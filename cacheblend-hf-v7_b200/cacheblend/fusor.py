@@ -251,16 +251,20 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
                                     tag="_dense")
             m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=a, sum_out=h, status=status))
 
-        # check layer: full projections, HKVD, then sparse from here on
+        # check layer: full-row K, HKVD, then sparse from here on
         layer = inner.layers[ck]
         attn = layer.self_attn
         hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None, status=status)
-        q = attn.q_proj(hn)
-        k_pre = attn.k_proj(hn)
-        v = attn.v_proj(hn)
+        k_pre = attn.k_proj(hn)             # every row: HKVD compares each token's fresh K
         idx, deviations = ops.hkvd_select(k_pre[0], table, ck, k_sel, force_last=True, status=status)
+        # Q and V only for the selected rows (the reference projects all S rows,
+        # fusor.py:333-335, and keeps these)
+        hn_sel = hn.index_select(1, idx)
+        q = attn.q_proj(hn_sel)
+        v = attn.v_proj(hn_sel)
+        k_rows = k_pre.index_select(1, idx)
         cur.wait_event(assembled)
-        q_rot = ops.rope_scatter(q[0], k_pre[0], v[0], idx, True, S, geo.n_q, geo.n_kv, geo.head_dim,
+        q_rot = ops.rope_scatter(q[0], k_rows[0], v[0], idx, False, S, geo.n_q, geo.n_kv, geo.head_dim,
                                  rope, fused_k[ck], fused_v[ck], mode=rope_mode, status=status)
         ws_sparse = ops.attn_workspace(k_sel, S, geo.n_q, geo.n_kv, geo.head_dim, device)
         a = ops.partial_attn(q_rot, fused_k[ck], fused_v[ck], idx, geo.n_q, geo.n_kv, geo.head_dim,

@@ -90,7 +90,7 @@ struct AttnParams {
   int* queue;             // &plan->next_item
   const int4* items;      // (kv head, tile pair, chunk, length) longest first
   const int* tile_base;   // [Hkv][n_tiles]: first partial slot of a split tile, -1 if not split
-  const int* split_list;  // [n_split]: kvh * n_tiles + tile of every split tile
+  const int4* split_desc; // [n_split]: (kvh * n_tiles + tile, first slot, chunks, 0) per split tile
   __half* part_o;         // [slot][128][HD] O / l of the chunk (fp16, bounded by |V|)
   float2* part_ml;        // [slot][128] (running max in log2 units, row sum)
   int64_t n_sel;
@@ -145,6 +145,62 @@ __device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1) {
       "add.f32x2 rd, rd, ra;\n\tmov.b64 {%0, %1}, rd;\n\t}"
       : "+f"(d0), "+f"(d1) : "f"(a0), "f"(a1));
 }
+
+// packed fp32 pairs (two floats in one 64-bit register pair) for the f32x2 instructions
+__device__ __forceinline__ uint64_t pk_f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk_f2(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x for a pair on the FMA pipe, to take load off the exponential unit.
+// Split x = j + f with j = rint(x) (adding 1.5 * 2^23 leaves rint(x) in the low
+// mantissa bits) and f in [-0.5, 0.5]; 2^f by a degree-3 polynomial, the
+// minimax fit for relative error on [-0.5, 0.5] found with the Remez exchange
+// algorithm (max relative error 7.5e-5, below the 16-bit rounding of P); 2^j is
+// added into the exponent field.  x is clamped at -126 (j >= -126 keeps the
+// exponent field from borrowing into the sign); below that the result is a
+// denormal ~1e-38 instead of 0.
+__device__ __forceinline__ void exp2_fma_pair(float x0, float x1, float& y0, float& y1) {
+  constexpr float kMagic = 12582912.f;   // 1.5 * 2^23
+  const uint64_t X = pk_f2(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t M = pk_f2(kMagic, kMagic);
+  const uint64_t T = add_f2(X, M);
+  const uint64_t F = sub_f2(X, sub_f2(T, M));
+  uint64_t P = fma_f2(F, pk_f2(0.0551716685295105f, 0.0551716685295105f),
+                      pk_f2(0.2426111251115799f, 0.2426111251115799f));
+  P = fma_f2(P, F, pk_f2(0.6932609677314758f, 0.6932609677314758f));
+  P = fma_f2(P, F, pk_f2(0.9999280571937561f, 0.9999280571937561f));
+  float p0, p1, t0, t1;
+  upk_f2(P, p0, p1);
+  upk_f2(T, t0, t1);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
+// Pairs e (of the 16 per 32 columns) whose exponentials go to the FMA pipe on
+// fully visible key tiles; the others use ex2.approx.
+#ifndef CBK_ATTN_EMU_MASK
+#define CBK_ATTN_EMU_MASK 0x8888
+#endif
 
 // number of 128-key tiles a Q tile needs (its last token has the largest position)
 __device__ __forceinline__ int tile_key_tiles(const int64_t* pos, int64_t n_sel, int tok_per_tile, int tile) {
@@ -483,9 +539,14 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const int c = c4 * 32 + 2 * e;
-              float x0, x1;
+              float x0, x1, p0, p1;
               fma2(x0, x1, __uint_as_float(s[c]), __uint_as_float(s[c + 1]), sl2, neg_m);
-              const float p0 = ex2(x0), p1 = ex2(x1);
+              if ((CBK_ATTN_EMU_MASK >> e) & 1) {
+                exp2_fma_pair(x0, x1, p0, p1);
+              } else {
+                p0 = ex2(x0);
+                p1 = ex2(x1);
+              }
               if (e & 1) add2(rb0, rb1, p0, p1);
               else add2(ra0, ra1, p0, p1);
               pk[e] = pack2<DT>(p0, p1);
@@ -633,7 +694,7 @@ __device__ int block_excl_scan(int v, int* s_warp, int* total) {
 __global__ void __launch_bounds__(kPlanThreads, 1)
 attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_tile, int n_tiles,
                  int n_kv_heads, int target_items, int min_chunk, int max_items, int max_slots,
-                 AttnPlanHeader* hdr, int4* items, int* tile_base, int* split_list, int32_t* status) {
+                 AttnPlanHeader* hdr, int4* items, int* tile_base, int4* split_desc, int32_t* status) {
   __shared__ int s_hist[kMaxKvTiles + 1];
   __shared__ int s_warp[33];
   __shared__ unsigned long long s_total;
@@ -727,7 +788,7 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
     const int rank = block_excl_scan(cnt ? 1 : 0, s_warp, &tot_split);
     if (i < n_all) {
       tile_base[i] = cnt ? carry + off : -1;
-      if (cnt) split_list[n_split + rank] = i;
+      if (cnt) split_desc[n_split + rank] = make_int4(i, carry + off, cnt, 0);
     }
     carry += tot;
     n_split += tot_split;
@@ -744,12 +805,12 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
 }
 
 // ---------------------------------------------------------------------------
-// Merge the partial results of split tiles.  One warp per row of a split tile
-// (rows come from the plan's list of split tiles, so no work is spent on
-// unsplit tiles).  Lane c first holds chunk c's (m, l), so the row maximum and
-// the weight sum are warp reductions; then the O rows of the chunks (HD
-// contiguous fp16 each, coalesced) are read four at a time with the loads
-// issued back to back:
+// Merge the partial results of split tiles.  One warp per row of a split tile;
+// the plan's descriptor of the tile (tile, first slot, chunk count) is the only
+// load the rest depends on, so no work is spent on unsplit tiles.  Lane c holds
+// chunk c's (m, l): the row maximum and the weight sum are warp reductions.
+// With up to 8 chunks, their (m, l) and O rows (HD contiguous fp16 each,
+// coalesced) are all loaded at once; longer rows go four O rows at a time:
 //   O = sum_c w_c Ohat_c / sum_c w_c,  w_c = l_c 2^(m_c - M),  Ohat_c = O_c / l_c.
 // ---------------------------------------------------------------------------
 constexpr int kCombineThreads = 256;
@@ -771,68 +832,92 @@ template <int DT, int HD>
 __global__ void __launch_bounds__(kCombineThreads)
 attn_combine_kernel(const AttnParams prm) {
   constexpr int kPerLane = HD / 32;   // 4 (HD 128) or 2 (HD 64) elements per lane
-  constexpr int kInFlight = 4;        // O rows loaded per batch
+  constexpr int kRegChunks = 8;       // rows with at most this many chunks load them all at once
+  constexpr int kInFlight = 4;        // O rows per batch beyond that
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // every attention CTA has finished: rewind the item queue for the next call
   if (blockIdx.x == 0 && threadIdx.x == 0) *prm.queue = 0;
   if (prm.plan->error) return;
-  const int C = prm.plan->chunk;
   const int n_rows = prm.plan->n_split * kBM;
   for (int u = blockIdx.x * kCombineRows + warp; u < n_rows; u += gridDim.x * kCombineRows) {
-    const int ti = prm.split_list[u / kBM];
+    const int4 d = prm.split_desc[u / kBM];
     const int row = u % kBM;
-    const int kvh = ti / prm.n_tiles, tile = ti % prm.n_tiles;
+    const int kvh = d.x / prm.n_tiles, tile = d.x % prm.n_tiles;
     const int64_t tok = static_cast<int64_t>(tile) * prm.tok_per_tile + row / prm.group;
     if (tok >= prm.n_sel) continue;   // padding row of the last tile
-    const int64_t slot0 = prm.tile_base[ti];
-    const int nc = (tile_key_tiles(prm.pos, prm.n_sel, prm.tok_per_tile, tile) + C - 1) / C;
-    // row maximum over the chunks with visible keys (a chunk without any has l = 0)
-    float M = -INFINITY;
-    for (int c0 = 0; c0 < nc; c0 += 32) {
-      float m = -INFINITY;
-      if (c0 + lane < nc) {
-        const float2 ml = prm.part_ml[(slot0 + c0 + lane) * kBM + row];
-        if (ml.y > 0.f) m = ml.x;
-      }
-      M = fmaxf(M, warp_max(m));
-    }
+    const int64_t slot0 = d.y;
+    const int nc = d.z;
     float acc[kPerLane];
 #pragma unroll
     for (int e = 0; e < kPerLane; ++e) acc[e] = 0.f;
-    float wsum = 0.f;
-    for (int c0 = 0; c0 < nc; c0 += 32) {
-      const int cn = min(32, nc - c0);
-      float w = 0.f;
-      if (lane < cn) {
-        const float2 ml = prm.part_ml[(slot0 + c0 + lane) * kBM + row];
-        if (ml.y > 0.f) w = ml.y * ex2(ml.x - M);
+    float wsum;
+    auto accumulate = [&](float wq, const uint32_t (&raw)[kPerLane / 2]) {
+#pragma unroll
+      for (int e = 0; e < kPerLane / 2; ++e) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&raw[e]));
+        acc[2 * e] = fmaf(wq, f.x, acc[2 * e]);
+        acc[2 * e + 1] = fmaf(wq, f.y, acc[2 * e + 1]);
       }
-      wsum += warp_sum(w);
-      for (int c = 0; c < cn; c += kInFlight) {
-        float wc[kInFlight];
-        uint32_t raw[kInFlight][kPerLane / 2];
+    };
+    auto load_o = [&](int64_t slot, uint32_t (&raw)[kPerLane / 2]) {
+      const __half* po = prm.part_o + (slot * kBM + row) * HD + lane * kPerLane;
+      if constexpr (kPerLane == 4) {
+        const uint2 r = *reinterpret_cast<const uint2*>(po);
+        raw[0] = r.x;
+        raw[1] = r.y;
+      } else {
+        raw[0] = *reinterpret_cast<const uint32_t*>(po);
+      }
+    };
+    if (nc <= kRegChunks) {
+      // (m, l) of chunk `lane` and the O rows of every chunk, all loads in flight together
+      float2 ml = make_float2(-INFINITY, 0.f);
+      if (lane < nc) ml = prm.part_ml[(slot0 + lane) * kBM + row];
+      uint32_t raw[kRegChunks][kPerLane / 2];
 #pragma unroll
-        for (int q = 0; q < kInFlight; ++q) {
-          const int cc = min(c + q, cn - 1);     // in range; weight 0 past the end
-          const float wq = __shfl_sync(0xffffffffu, w, cc);
-          wc[q] = (c + q < cn) ? wq : 0.f;
-          const __half* po = prm.part_o + ((slot0 + c0 + cc) * kBM + row) * HD + lane * kPerLane;
-          if constexpr (kPerLane == 4) {
-            const uint2 r = *reinterpret_cast<const uint2*>(po);
-            raw[q][0] = r.x;
-            raw[q][1] = r.y;
-          } else {
-            raw[q][0] = *reinterpret_cast<const uint32_t*>(po);
-          }
+      for (int q = 0; q < kRegChunks; ++q)
+        if (q < nc) load_o(slot0 + q, raw[q]);
+      // a chunk without visible keys has l = 0 and weight 0
+      const float M = warp_max(ml.y > 0.f ? ml.x : -INFINITY);
+      const float w = ml.y > 0.f ? ml.y * ex2(ml.x - M) : 0.f;
+      wsum = warp_sum(w);
+#pragma unroll
+      for (int q = 0; q < kRegChunks; ++q) {
+        const float wq = __shfl_sync(0xffffffffu, w, q);
+        if (q < nc) accumulate(wq, raw[q]);
+      }
+    } else {
+      float M = -INFINITY;
+      for (int c0 = 0; c0 < nc; c0 += 32) {
+        float m = -INFINITY;
+        if (c0 + lane < nc) {
+          const float2 ml = prm.part_ml[(slot0 + c0 + lane) * kBM + row];
+          if (ml.y > 0.f) m = ml.x;
         }
+        M = fmaxf(M, warp_max(m));
+      }
+      wsum = 0.f;
+      for (int c0 = 0; c0 < nc; c0 += 32) {
+        const int cn = min(32, nc - c0);
+        float w = 0.f;
+        if (lane < cn) {
+          const float2 ml = prm.part_ml[(slot0 + c0 + lane) * kBM + row];
+          if (ml.y > 0.f) w = ml.y * ex2(ml.x - M);
+        }
+        wsum += warp_sum(w);
+        for (int c = 0; c < cn; c += kInFlight) {
+          float wc[kInFlight];
+          uint32_t raw[kInFlight][kPerLane / 2];
 #pragma unroll
-        for (int q = 0; q < kInFlight; ++q)
-#pragma unroll
-          for (int e = 0; e < kPerLane / 2; ++e) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&raw[q][e]));
-            acc[2 * e] = fmaf(wc[q], f.x, acc[2 * e]);
-            acc[2 * e + 1] = fmaf(wc[q], f.y, acc[2 * e + 1]);
+          for (int q = 0; q < kInFlight; ++q) {
+            const int cc = min(c + q, cn - 1);     // in range; weight 0 past the end
+            const float wq = __shfl_sync(0xffffffffu, w, cc);
+            wc[q] = (c + q < cn) ? wq : 0.f;
+            load_o(slot0 + c0 + cc, raw[q]);
           }
+#pragma unroll
+          for (int q = 0; q < kInFlight; ++q) accumulate(wc[q], raw[q]);
+        }
       }
     }
     const float inv = 1.f / wsum;
@@ -918,7 +1003,7 @@ static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int 
   a.off_items = align256(sizeof(AttnPlanHeader));
   a.off_tile_base = a.off_items + align256(static_cast<size_t>(a.max_items) * sizeof(int4));
   a.off_split = a.off_tile_base + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int));
-  a.off_ml = a.off_split + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int));
+  a.off_ml = a.off_split + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int4));
   a.off_o = a.off_ml + align256(static_cast<size_t>(a.max_slots) * kBM * sizeof(float2));
   a.bytes = a.off_o + static_cast<size_t>(a.max_slots) * kBM * head_dim * sizeof(__half);
   return a;
@@ -943,7 +1028,7 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   prm.queue = &reinterpret_cast<AttnPlanHeader*>(ws)->next_item;
   prm.items = reinterpret_cast<const int4*>(ws + lay.off_items);
   prm.tile_base = reinterpret_cast<const int*>(ws + lay.off_tile_base);
-  prm.split_list = reinterpret_cast<const int*>(ws + lay.off_split);
+  prm.split_desc = reinterpret_cast<const int4*>(ws + lay.off_split);
   prm.part_ml = reinterpret_cast<float2*>(ws + lay.off_ml);
   prm.part_o = reinterpret_cast<__half*>(ws + lay.off_o);
   prm.n_sel = n_sel;
@@ -957,7 +1042,7 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
         pos, n_sel, lay.tok_per_tile, lay.n_tiles, n_kv_heads, lay.target, lay.min_chunk,
         lay.max_items, lay.max_slots, reinterpret_cast<AttnPlanHeader*>(ws),
         reinterpret_cast<int4*>(ws + lay.off_items), reinterpret_cast<int*>(ws + lay.off_tile_base),
-        reinterpret_cast<int*>(ws + lay.off_split), status);
+        reinterpret_cast<int4*>(ws + lay.off_split), status);
     if (int rc = check_launch("attn_plan_kernel")) return rc;
   }
   auto kern = partial_attn_kernel<DT, HD>;
