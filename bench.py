@@ -495,7 +495,7 @@ def run_kv_microbench(args):
     from cacheblend import ops
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    L, Hkv, S, D, CL, Hq = 32, 8, 32768, 128, 2048, 32
+    L, Hkv, S, D, CL, Hq = args.kv_layers, 8, 32768, 128, 2048, 32
     n_chunks = S // CL
     kv = Hkv * D
     g = torch.Generator(device=device).manual_seed(0)
@@ -517,14 +517,16 @@ def run_kv_microbench(args):
     q_fresh = torch.randn((k, Hq * D), generator=g, device=device).to(torch.bfloat16)
     k_fresh = torch.randn((k, kv), generator=g, device=device).to(torch.bfloat16)
     v_fresh = torch.randn((k, kv), generator=g, device=device).to(torch.bfloat16)
-    ws = torch.empty((S,), dtype=torch.float32, device=device)
     q_out = torch.empty((k, Hq * D), dtype=torch.bfloat16, device=device)
     rope_seq = ops.rope_table(invf, S)
 
     def step(i):
         ops.assemble_kv(table, 0, L, Hkv, D, rope, fk, fv, positions=positions)
         for l in range(L):
-            idx, _ = ops.hkvd_select(k_new[l], table, l, k, force_last=True, workspace=ws)
+            # HKVD as its two kernels, so the HBM-bound deviation pass and the
+            # latency-bound top-K select are timed apart
+            dev = ops.kv_deviation_rows(k_new[l], table, l)
+            idx = ops.topk_select(dev, k, force_last=True)
             ops.rope_scatter(q_fresh, k_fresh, v_fresh, idx, False, S, Hq, Hkv, D, rope_seq, fk[l], fv[l],
                              q_out=q_out)
 
@@ -534,12 +536,15 @@ def run_kv_microbench(args):
     hk_b = L * (2 * S * kv * 2 + 4 * S)
     sc_b = L * k * (Hq * D + 2 * kv) * 2 * 2
     out = {}
-    for name, nbytes, div in (("assemble_kv", asm_b, 1), ("hkvd_select", hk_b, 1), ("rope_scatter", sc_b, 1)):
+    for name, nbytes, div in (("assemble_kv", asm_b, 1), ("kv_deviation", hk_b, 1), ("rope_scatter", sc_b, 1)):
         n, t = kern.get(name, (0, 0.0))
         per_step = t / args.steps
         out[name] = {"launches_per_step": n // args.steps, "ms_per_step": round(per_step, 4),
                      "bytes_per_step": nbytes, "GB/s": round(nbytes / (per_step * 1e-3) / 1e9, 1),
                      "frac_hbm": round(nbytes / (per_step * 1e-3) / 1e9 / hbm, 3)}
+    n_tk, t_tk = kern.get("topk_select", (0, 0.0))
+    out["topk_select"] = {"launches_per_step": n_tk // args.steps, "bound": "latency (one CTA, S keys)",
+                          "us_per_launch": round(t_tk / max(n_tk, 1) * 1e3, 1)}
     total_b = asm_b + hk_b + sc_b
     print(json.dumps({
         "metric": "KV-kernel HBM GB/s (assemble + HKVD + scatter, microbench [32,8,32768,128])",
@@ -548,7 +553,7 @@ def run_kv_microbench(args):
         "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "kv-microbench", "layers": L, "kv_heads": Hkv, "tokens": S, "head_dim": D,
                    "chunks": f"{n_chunks}x{CL}", "topk": k,
-                   "l2": "inputs larger than L2 (4.3 GB chunk K/V + 2.1 GB recomputed K per step)"},
+                   "l2": f"inputs larger than L2 ({4 * L * S * kv / 1e9:.1f} GB chunk K/V, fresh K and fused K/V per step)"},
         "kernels": out, "hbm_peak_gbs": hbm, "hbm_peak_kind": src, "clocks": clk}), flush=True)
 
 
@@ -954,6 +959,7 @@ def main():
     ap.add_argument("--attn-k", type=int, default=931, help="selected rows (6208 = dense causal)")
     ap.add_argument("--attn-dist", default="uniform", choices=["uniform", "tail"])
     ap.add_argument("--sh-layers", type=int, default=80, help="layers of the sharded 128K workload")
+    ap.add_argument("--kv-layers", type=int, default=32, help="layers of the KV microbench")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -18,6 +18,7 @@
 namespace cbk {
 
 constexpr int kDevThreads = 256;
+constexpr int kDevBatch = 4;     // 16-byte vectors per lane per batch
 
 template <int DT>
 __global__ void __launch_bounds__(kDevThreads)
@@ -27,24 +28,42 @@ deviation_kernel(const uint16_t* __restrict__ k_new, int64_t new_stride,
   const int lane = threadIdx.x & 31;
   const int64_t t = (static_cast<int64_t>(blockIdx.x) * kDevThreads + threadIdx.x) >> 5;
   if (t >= S) return;
+  // A lane's vectors go kDevBatch at a time with all their loads issued first;
+  // the fresh row's first batch is requested before the chunk search.  The
+  // accumulation order above is unchanged.
+  const uint16_t* a = k_new + t * new_stride;
+  const int nvec = static_cast<int>(feat >> 3);
+  uint4 x[kDevBatch], y[kDevBatch];
+#pragma unroll
+  for (int q = 0; q < kDevBatch; ++q)
+    if (lane + q * 32 < nvec) x[q] = ld_vec(a + (lane + q * 32) * 8);
   int lo = 0, hi = n_chunks - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (chunk_start[mid] <= t) lo = mid; else hi = mid - 1;
   }
-  const uint16_t* a = k_new + t * new_stride;
   const uint16_t* b = static_cast<const uint16_t*>(old_srcs[lo].k) + (t - chunk_start[lo]) * feat;
-  const int nvec = static_cast<int>(feat >> 3);
   float acc = 0.f;
-  for (int v = lane; v < nvec; v += 32) {
-    const uint4 x = ld_vec(a + v * 8);
-    const uint4 y = ld_stream(b + v * 8);
-    const uint16_t* xs = reinterpret_cast<const uint16_t*>(&x);
-    const uint16_t* ys = reinterpret_cast<const uint16_t*>(&y);
+  for (int v0 = lane; v0 < nvec; v0 += 32 * kDevBatch) {
+    if (v0 != lane) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float d = __fsub_rn(Elem<DT>::to_f(xs[e]), Elem<DT>::to_f(ys[e]));
-      acc = __fadd_rn(acc, __fmul_rn(d, d));
+      for (int q = 0; q < kDevBatch; ++q)
+        if (v0 + q * 32 < nvec) x[q] = ld_vec(a + (v0 + q * 32) * 8);
+    }
+#pragma unroll
+    for (int q = 0; q < kDevBatch; ++q)
+      if (v0 + q * 32 < nvec) y[q] = ld_stream(b + (v0 + q * 32) * 8);
+#pragma unroll
+    for (int q = 0; q < kDevBatch; ++q) {
+      if (v0 + q * 32 < nvec) {
+        const uint16_t* xs = reinterpret_cast<const uint16_t*>(&x[q]);
+        const uint16_t* ys = reinterpret_cast<const uint16_t*>(&y[q]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = __fsub_rn(Elem<DT>::to_f(xs[e]), Elem<DT>::to_f(ys[e]));
+          acc = __fadd_rn(acc, __fmul_rn(d, d));
+        }
+      }
     }
   }
 #pragma unroll

@@ -82,16 +82,21 @@ __device__ __forceinline__ void rope_group(const uint16_t* src_row, uint16_t* ds
 }
 
 // ---------------------------------------------------------------------------
-// (a)+(b) assemble: rows of one layer per blockIdx.y, kRows rows per block.
-// Work items of a row: n_kv_heads * head_dim/16 K pair-groups (RoPE) followed
-// by kv_dim/8 V vectors (copy).
+// (a)+(b) assemble: one layer per blockIdx.y, kAsmRows rows per block, two warps
+// per row: the even warp rotates the row's K (n_kv_heads * head_dim/16 pair
+// groups), the odd warp copies its V (kv_dim/8 16-byte vectors).  Each lane
+// issues all the loads of a batch (2 K groups = 4 vectors, or 4 V vectors)
+// before any arithmetic or store, so a warp keeps 2 KB in flight.
 // ---------------------------------------------------------------------------
 constexpr int kAsmThreads = 256;
-constexpr int kAsmRows = 16;
+constexpr int kAsmRows = kAsmThreads / 64;   // rows in flight per block
+constexpr int kAsmRowIters = 4;               // rows per warp pair, in sequence
 constexpr int kMaxChunksSmem = 2048;
+constexpr int kAsmKBatch = 2;     // K pair groups per lane per batch
+constexpr int kAsmVBatch = 4;     // V vectors per lane per batch
 
 template <int DT>
-__global__ void __launch_bounds__(kAsmThreads)
+__global__ void __launch_bounds__(kAsmThreads, 3)
 assemble_kernel(const cbk_chunk_src* __restrict__ srcs, const int64_t* __restrict__ chunk_start,
                 int n_chunks, int64_t S, int n_kv_heads, int head_dim,
                 const float2* __restrict__ table, int64_t table_rows,
@@ -99,43 +104,74 @@ assemble_kernel(const cbk_chunk_src* __restrict__ srcs, const int64_t* __restric
                 uint16_t* __restrict__ v_out, int64_t layer_stride, int32_t* status) {
   __shared__ int64_t s_start[kMaxChunksSmem + 1];
   const int layer = blockIdx.y;
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kAsmRows;
   for (int c = threadIdx.x; c <= n_chunks; c += blockDim.x) s_start[c] = chunk_start[c];
   __syncthreads();
-
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int it = 0; it < kAsmRowIters; ++it) {
+  const int64_t t = (static_cast<int64_t>(blockIdx.x) * kAsmRowIters + it) * kAsmRows + (warp >> 1);
+  if (t >= S) break;
+  // chunk of row t: largest c with s_start[c] <= t (warp-uniform)
+  int lo = 0, hi = n_chunks - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_start[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  const int64_t local = t - s_start[lo];
   const int kv_dim = n_kv_heads * head_dim;
-  const int kgroups = n_kv_heads * (head_dim >> 4);   // K pair-groups per row
-  const int vvecs = kv_dim >> 3;                       // V 16-byte vectors per row
-  const int per_row = kgroups + vvecs;
-  const int n_items = kAsmRows * per_row;
-  const cbk_chunk_src* lsrc = srcs + static_cast<int64_t>(layer) * n_chunks;
-  uint16_t* kl = k_out + layer * layer_stride;
-  uint16_t* vl = v_out + layer * layer_stride;
-
-  for (int it = threadIdx.x; it < n_items; it += kAsmThreads) {
-    const int r = it / per_row;
-    const int w = it - r * per_row;
-    const int64_t t = row0 + r;
-    if (t >= S) continue;
-    // chunk of row t: largest c with s_start[c] <= t
-    int lo = 0, hi = n_chunks - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (s_start[mid] <= t) lo = mid; else hi = mid - 1;
+  const cbk_chunk_src src = srcs[static_cast<int64_t>(layer) * n_chunks + lo];
+  if ((warp & 1) == 0) {
+    const int64_t p = positions ? positions[t] : t;
+    if (p < 0 || p >= table_rows) {
+      if (lane == 0) report(status, CBK_STATUS_BAD_INDEX);
+      continue;
     }
-    const int64_t local = t - s_start[lo];
-    if (w < kgroups) {
-      const int64_t p = positions ? positions[t] : t;
-      if (p < 0 || p >= table_rows) { report(status, CBK_STATUS_BAD_INDEX); continue; }
-      const int h = w / (head_dim >> 4);
-      const int g = w - h * (head_dim >> 4);
-      const uint16_t* src = static_cast<const uint16_t*>(lsrc[lo].k) + local * kv_dim;
-      rope_group<DT, true>(src, kl + t * kv_dim, h, g, head_dim, table + p * (head_dim >> 1), mode);
-    } else {
-      const int vv = w - kgroups;
-      const uint16_t* src = static_cast<const uint16_t*>(lsrc[lo].v) + local * kv_dim + vv * 8;
-      st_vec(vl + t * kv_dim + vv * 8, ld_stream(src));
+    const int gph = head_dim >> 4;               // pair groups per head
+    const int kgroups = n_kv_heads * gph;
+    const int half = head_dim >> 1;
+    const uint16_t* krow = static_cast<const uint16_t*>(src.k) + local * kv_dim;
+    uint16_t* drow = k_out + layer * layer_stride + t * kv_dim;
+    const float2* cs = table + p * half;
+    for (int g0 = 0; g0 < kgroups; g0 += 32 * kAsmKBatch) {
+      uint4 xl[kAsmKBatch], xh[kAsmKBatch];
+#pragma unroll
+      for (int q = 0; q < kAsmKBatch; ++q) {
+        const int g = g0 + q * 32 + lane;
+        if (g < kgroups) {
+          const int off = (g / gph) * head_dim + (g % gph) * 8;
+          xl[q] = ld_stream(krow + off);
+          xh[q] = ld_stream(krow + off + half);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kAsmKBatch; ++q) {
+        const int g = g0 + q * 32 + lane;
+        if (g < kgroups) {
+          const int off = (g / gph) * head_dim + (g % gph) * 8;
+          uint4 ol, oh;
+          rope8<DT>(xl[q], xh[q], cs + (g % gph) * 8, mode, ol, oh);
+          st_vec(drow + off, ol);
+          st_vec(drow + off + half, oh);
+        }
+      }
     }
+  } else {
+    const int vvecs = kv_dim >> 3;
+    const uint16_t* vrow = static_cast<const uint16_t*>(src.v) + local * kv_dim;
+    uint16_t* drow = v_out + layer * layer_stride + t * kv_dim;
+    for (int v0 = 0; v0 < vvecs; v0 += 32 * kAsmVBatch) {
+      uint4 x[kAsmVBatch];
+#pragma unroll
+      for (int q = 0; q < kAsmVBatch; ++q) {
+        const int v = v0 + q * 32 + lane;
+        if (v < vvecs) x[q] = ld_stream(vrow + v * 8);
+      }
+#pragma unroll
+      for (int q = 0; q < kAsmVBatch; ++q) {
+        const int v = v0 + q * 32 + lane;
+        if (v < vvecs) st_vec(drow + v * 8, x[q]);
+      }
+    }
+  }
   }
 }
 
@@ -165,11 +201,16 @@ rope_rows_kernel(const uint16_t* in, uint16_t* out, int64_t n_rows, int n_heads,
 
 // ---------------------------------------------------------------------------
 // Fresh rows of one layer: RoPE(Q) -> q_out, RoPE(K) and V scattered into the
-// fused cache at the selected positions.  Items per selected row j:
-// Hq*D/16 Q groups, Hkv*D/16 K groups, Hkv*D/8 V vectors.
+// fused cache at the selected positions.  Work unit = one warp: 64 RoPE pair
+// groups of Q or of K (2 per lane), or 128 V vectors (4 per lane); a selected
+// row has ceil(Hq*D/16 / 64) + ceil(Hkv*D/16 / 64) + ceil(Hkv*D/8 / 128) units.
+// Each lane issues all the loads of its unit before any arithmetic or store.
 // ---------------------------------------------------------------------------
+constexpr int kScatGroups = 2;    // RoPE pair groups per lane
+constexpr int kScatVecs = 4;      // V vectors per lane
+
 template <int DT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)
 rope_scatter_kernel(const uint16_t* __restrict__ q_src, int64_t q_stride,
                     const uint16_t* __restrict__ k_src, int64_t k_stride,
                     const uint16_t* __restrict__ v_src, int64_t v_stride, int gather,
@@ -178,31 +219,88 @@ rope_scatter_kernel(const uint16_t* __restrict__ q_src, int64_t q_stride,
                     int64_t table_rows, int mode, uint16_t* __restrict__ q_out,
                     uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache,
                     int32_t* status) {
+  const int lane = threadIdx.x & 31;
   const int gpr = head_dim >> 4;
+  const int half = head_dim >> 1;
   const int qg = n_q_heads * gpr;
   const int kg = n_kv_heads * gpr;
   const int kv_dim = n_kv_heads * head_dim;
   const int vv = kv_dim >> 3;
-  const int per = qg + kg + vv;
-  const int64_t n = n_sel * per;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t j = e / per;
-    int w = static_cast<int>(e - j * per);
+  const int nq = (qg + 32 * kScatGroups - 1) / (32 * kScatGroups);
+  const int nk = (kg + 32 * kScatGroups - 1) / (32 * kScatGroups);
+  const int nv = (vv + 32 * kScatVecs - 1) / (32 * kScatVecs);
+  const int per = nq + nk + nv;
+  const int64_t n_units = n_sel * per;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n_units;
+       u += warps) {
+    const int64_t j = u / per;
+    const int part = static_cast<int>(u - j * per);
     const int64_t p = idx[j];
-    if (p < 0 || p >= S || p >= table_rows) { report(status, CBK_STATUS_BAD_INDEX); continue; }
-    const int64_t r = gather ? p : j;
-    const float2* cs = table + p * (head_dim >> 1);
-    if (w < qg) {
-      const int h = w / gpr, g = w - (w / gpr) * gpr;
-      rope_group<DT, false>(q_src + r * q_stride, q_out + j * (int64_t)(n_q_heads * head_dim), h, g,
-                            head_dim, cs, mode);
-    } else if ((w -= qg) < kg) {
-      const int h = w / gpr, g = w - (w / gpr) * gpr;
-      rope_group<DT, false>(k_src + r * k_stride, k_cache + p * kv_dim, h, g, head_dim, cs, mode);
+    const bool bad = p < 0 || p >= S || p >= table_rows;
+    // Without a gather the source row is j: its loads are issued before the
+    // position arrives (they do not depend on it); with a gather they wait.
+    if (part < nq + nk) {
+      const bool is_q = part < nq;
+      const int ng = is_q ? qg : kg;
+      const int g0 = (is_q ? part : part - nq) * 32 * kScatGroups;
+      const uint16_t* base = is_q ? q_src : k_src;
+      const int64_t stride = is_q ? q_stride : k_stride;
+      uint4 xl[kScatGroups], xh[kScatGroups];
+      auto load = [&](int64_t r) {
+        const uint16_t* src = base + r * stride;
+#pragma unroll
+        for (int q = 0; q < kScatGroups; ++q) {
+          const int g = g0 + q * 32 + lane;
+          if (g < ng) {
+            const int off = (g / gpr) * head_dim + (g % gpr) * 8;
+            xl[q] = ld_vec(src + off);
+            xh[q] = ld_vec(src + off + half);
+          }
+        }
+      };
+      if (!gather) load(j);
+      if (bad) {
+        if (lane == 0) report(status, CBK_STATUS_BAD_INDEX);
+        continue;
+      }
+      if (gather) load(p);
+      uint16_t* dst = is_q ? q_out + j * static_cast<int64_t>(n_q_heads * head_dim) : k_cache + p * kv_dim;
+      const float2* cs = table + p * half;
+#pragma unroll
+      for (int q = 0; q < kScatGroups; ++q) {
+        const int g = g0 + q * 32 + lane;
+        if (g < ng) {
+          const int off = (g / gpr) * head_dim + (g % gpr) * 8;
+          uint4 ol, oh;
+          rope8<DT>(xl[q], xh[q], cs + (g % gpr) * 8, mode, ol, oh);
+          st_vec(dst + off, ol);
+          st_vec(dst + off + half, oh);
+        }
+      }
     } else {
-      w -= kg;
-      st_vec(v_cache + p * kv_dim + w * 8, ld_vec(v_src + r * v_stride + w * 8));
+      const int v0 = (part - nq - nk) * 32 * kScatVecs;
+      uint4 x[kScatVecs];
+      auto load = [&](int64_t r) {
+        const uint16_t* src = v_src + r * v_stride;
+#pragma unroll
+        for (int q = 0; q < kScatVecs; ++q) {
+          const int v = v0 + q * 32 + lane;
+          if (v < vv) x[q] = ld_vec(src + v * 8);
+        }
+      };
+      if (!gather) load(j);
+      if (bad) {
+        if (lane == 0) report(status, CBK_STATUS_BAD_INDEX);
+        continue;
+      }
+      if (gather) load(p);
+      uint16_t* dst = v_cache + p * kv_dim;
+#pragma unroll
+      for (int q = 0; q < kScatVecs; ++q) {
+        const int v = v0 + q * 32 + lane;
+        if (v < vv) st_vec(dst + v * 8, x[q]);
+      }
     }
   }
 }
@@ -263,7 +361,8 @@ extern "C" int cbk_assemble_kv(const cbk_chunk_src* srcs, const int64_t* chunk_s
     return set_error(CBK_ERR_INVALID, "cbk_assemble_kv: outputs must be 16-byte aligned with a layer "
                      "stride >= S*kv_dim (multiple of 8)");
   if (int rc = check_mode("cbk_assemble_kv", rope_mode)) return rc;
-  dim3 grid(static_cast<unsigned>((S + kAsmRows - 1) / kAsmRows), static_cast<unsigned>(n_layers));
+  const int64_t rows_per_block = static_cast<int64_t>(kAsmRows) * kAsmRowIters;
+  dim3 grid(static_cast<unsigned>((S + rows_per_block - 1) / rows_per_block), static_cast<unsigned>(n_layers));
   auto st = static_cast<cudaStream_t>(stream);
   auto tab = static_cast<const float2*>(rope_table);
   if (dtype == CBK_BF16)
@@ -324,11 +423,14 @@ extern "C" int cbk_rope_scatter(const void* q_src, int64_t q_row_stride, const v
                      "cbk_rope_scatter: buffers must be 16-byte aligned, row strides multiples of 8");
   if (n_sel == 0) return CBK_OK;
   const int gpr = head_dim >> 4;
-  const int64_t items = n_sel * (n_q_heads * gpr + n_kv_heads * gpr + n_kv_heads * head_dim / 8);
+  const int64_t per = (n_q_heads * gpr + 32 * kScatGroups - 1) / (32 * kScatGroups) +
+                      (n_kv_heads * gpr + 32 * kScatGroups - 1) / (32 * kScatGroups) +
+                      (n_kv_heads * head_dim / 8 + 32 * kScatVecs - 1) / (32 * kScatVecs);
+  const int64_t warp_units = n_sel * per;            // 8 warps per 256-thread block
   auto st = static_cast<cudaStream_t>(stream);
   auto tab = static_cast<const float2*>(rope_table);
 #define CBK_LAUNCH_SCATTER(DT)                                                                  \
-  rope_scatter_kernel<DT><<<grid_for(items, 256), 256, 0, st>>>(                                \
+  rope_scatter_kernel<DT><<<grid_for(warp_units * 32, 256, 148 * 64), 256, 0, st>>>(             \
       static_cast<const uint16_t*>(q_src), q_row_stride, static_cast<const uint16_t*>(k_src),   \
       k_row_stride, static_cast<const uint16_t*>(v_src), v_row_stride, gather, idx, n_sel, S,   \
       n_q_heads, n_kv_heads, head_dim, tab, table_rows, rope_mode,                              \
