@@ -531,20 +531,51 @@ def run_kv_microbench(args):
                              q_out=q_out)
 
     ms, kern, clk = _timed(step, args.steps, args.warmup, device)
+    # Per-kernel rates: each kernel's L launches of one step back to back between
+    # one CUDA-event pair (a pair around every short launch would add its own
+    # record and launch latency to the kernel's time).
+    idx_l = [ops.topk_select(ops.kv_deviation_rows(k_new[l], table, l), k, force_last=True) for l in range(L)]
+    devs = [ops.kv_deviation_rows(k_new[l], table, l) for l in range(L)]
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+
+    def batch_ms(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    per_kernel = {
+        "assemble_kv": batch_ms(lambda: ops.assemble_kv(table, 0, L, Hkv, D, rope, fk, fv, positions=positions),
+                                args.steps),
+        "kv_deviation": batch_ms(lambda: [ops.kv_deviation_rows(k_new[l], table, l) for l in range(L)],
+                                 args.steps),
+        "topk_select": batch_ms(lambda: [ops.topk_select(devs[l], k, force_last=True) for l in range(L)],
+                                args.steps),
+        "rope_scatter": batch_ms(lambda: [ops.rope_scatter(q_fresh, k_fresh, v_fresh, idx_l[l], False, S, Hq,
+                                                           Hkv, D, rope_seq, fk[l], fv[l], q_out=q_out)
+                                          for l in range(L)], args.steps),
+    }
     hbm, _, _, src = load_peaks()
     asm_b = L * 4 * S * kv * 2
     hk_b = L * (2 * S * kv * 2 + 4 * S)
     sc_b = L * k * (Hq * D + 2 * kv) * 2 * 2
     out = {}
-    for name, nbytes, div in (("assemble_kv", asm_b, 1), ("kv_deviation", hk_b, 1), ("rope_scatter", sc_b, 1)):
+    for name, nbytes in (("assemble_kv", asm_b), ("kv_deviation", hk_b), ("rope_scatter", sc_b)):
         n, t = kern.get(name, (0, 0.0))
-        per_step = t / args.steps
+        per_step = per_kernel[name]
         out[name] = {"launches_per_step": n // args.steps, "ms_per_step": round(per_step, 4),
                      "bytes_per_step": nbytes, "GB/s": round(nbytes / (per_step * 1e-3) / 1e9, 1),
-                     "frac_hbm": round(nbytes / (per_step * 1e-3) / 1e9 / hbm, 3)}
-    n_tk, t_tk = kern.get("topk_select", (0, 0.0))
+                     "frac_hbm": round(nbytes / (per_step * 1e-3) / 1e9 / hbm, 3),
+                     "ms_per_step_in_step_spans": round(t / args.steps, 4)}
+    n_tk, _ = kern.get("topk_select", (0, 0.0))
     out["topk_select"] = {"launches_per_step": n_tk // args.steps, "bound": "latency (one CTA, S keys)",
-                          "us_per_launch": round(t_tk / max(n_tk, 1) * 1e3, 1)}
+                          "us_per_launch": round(per_kernel["topk_select"] / max(n_tk // args.steps, 1) * 1e3, 1)}
     total_b = asm_b + hk_b + sc_b
     print(json.dumps({
         "metric": "KV-kernel HBM GB/s (assemble + HKVD + scatter, microbench [32,8,32768,128])",

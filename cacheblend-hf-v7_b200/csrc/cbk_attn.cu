@@ -805,129 +805,114 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
 }
 
 // ---------------------------------------------------------------------------
-// Merge the partial results of split tiles.  One warp per row of a split tile;
-// the plan's descriptor of the tile (tile, first slot, chunk count) is the only
-// load the rest depends on, so no work is spent on unsplit tiles.  Lane c holds
-// chunk c's (m, l): the row maximum and the weight sum are warp reductions.
-// With up to 8 chunks, their (m, l) and O rows (HD contiguous fp16 each,
-// coalesced) are all loaded at once; longer rows go four O rows at a time:
-//   O = sum_c w_c Ohat_c / sum_c w_c,  w_c = l_c 2^(m_c - M),  Ohat_c = O_c / l_c.
+// Merge the partial results of split tiles:
+//   O = sum_c w_c Ohat_c / sum_c w_c,  w_c = l_c 2^(m_c - M),  Ohat_c = O_c / l_c
+// (a chunk without visible keys has l = 0 and weight 0).  Work unit = half a
+// split tile (64 rows), one CTA, from the plan's split-tile descriptors.  Row
+// maxima first (64 threads), then per group of up to 32 chunks the weights go to
+// shared memory in one coalesced round trip, and every thread accumulates its
+// four 8-element vectors with four chunk rows of loads in flight.  Sums run over
+// the chunks in increasing order, so results are deterministic.
 // ---------------------------------------------------------------------------
 constexpr int kCombineThreads = 256;
-constexpr int kCombineRows = kCombineThreads / 32;
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
+constexpr int kCombineRows = 64;        // rows per work unit
+constexpr int kCombineGroup = 32;       // chunks whose weights sit in shared memory at once
+constexpr int kCombinePre = 4;          // chunk rows loaded together
 
 template <int DT, int HD>
-__global__ void __launch_bounds__(kCombineThreads)
+__global__ void __launch_bounds__(kCombineThreads, 2)
 attn_combine_kernel(const AttnParams prm) {
-  constexpr int kPerLane = HD / 32;   // 4 (HD 128) or 2 (HD 64) elements per lane
-  constexpr int kRegChunks = 8;       // rows with at most this many chunks load them all at once
-  constexpr int kInFlight = 4;        // O rows per batch beyond that
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kVecRow = HD / 8;                                     // 8-element vectors per row
+  constexpr int kVecThr = kCombineRows * kVecRow / kCombineThreads;  // 4 (HD 128) or 2 (HD 64)
+  __shared__ float s_w[kCombineGroup][kCombineRows];
+  __shared__ float s_m[kCombineRows];
+  __shared__ float s_sum[kCombineRows];
+  const int tid = threadIdx.x;
   // every attention CTA has finished: rewind the item queue for the next call
-  if (blockIdx.x == 0 && threadIdx.x == 0) *prm.queue = 0;
+  if (blockIdx.x == 0 && tid == 0) *prm.queue = 0;
   if (prm.plan->error) return;
-  const int n_rows = prm.plan->n_split * kBM;
-  for (int u = blockIdx.x * kCombineRows + warp; u < n_rows; u += gridDim.x * kCombineRows) {
-    const int4 d = prm.split_desc[u / kBM];
-    const int row = u % kBM;
+  const int n_units = prm.plan->n_split * (kBM / kCombineRows);
+  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    const int4 d = prm.split_desc[u / (kBM / kCombineRows)];
+    const int row0 = (u % (kBM / kCombineRows)) * kCombineRows;
     const int kvh = d.x / prm.n_tiles, tile = d.x % prm.n_tiles;
-    const int64_t tok = static_cast<int64_t>(tile) * prm.tok_per_tile + row / prm.group;
-    if (tok >= prm.n_sel) continue;   // padding row of the last tile
     const int64_t slot0 = d.y;
     const int nc = d.z;
-    float acc[kPerLane];
-#pragma unroll
-    for (int e = 0; e < kPerLane; ++e) acc[e] = 0.f;
-    float wsum;
-    auto accumulate = [&](float wq, const uint32_t (&raw)[kPerLane / 2]) {
-#pragma unroll
-      for (int e = 0; e < kPerLane / 2; ++e) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&raw[e]));
-        acc[2 * e] = fmaf(wq, f.x, acc[2 * e]);
-        acc[2 * e + 1] = fmaf(wq, f.y, acc[2 * e + 1]);
-      }
-    };
-    auto load_o = [&](int64_t slot, uint32_t (&raw)[kPerLane / 2]) {
-      const __half* po = prm.part_o + (slot * kBM + row) * HD + lane * kPerLane;
-      if constexpr (kPerLane == 4) {
-        const uint2 r = *reinterpret_cast<const uint2*>(po);
-        raw[0] = r.x;
-        raw[1] = r.y;
-      } else {
-        raw[0] = *reinterpret_cast<const uint32_t*>(po);
-      }
-    };
-    if (nc <= kRegChunks) {
-      // (m, l) of chunk `lane` and the O rows of every chunk, all loads in flight together
-      float2 ml = make_float2(-INFINITY, 0.f);
-      if (lane < nc) ml = prm.part_ml[(slot0 + lane) * kBM + row];
-      uint32_t raw[kRegChunks][kPerLane / 2];
-#pragma unroll
-      for (int q = 0; q < kRegChunks; ++q)
-        if (q < nc) load_o(slot0 + q, raw[q]);
-      // a chunk without visible keys has l = 0 and weight 0
-      const float M = warp_max(ml.y > 0.f ? ml.x : -INFINITY);
-      const float w = ml.y > 0.f ? ml.y * ex2(ml.x - M) : 0.f;
-      wsum = warp_sum(w);
-#pragma unroll
-      for (int q = 0; q < kRegChunks; ++q) {
-        const float wq = __shfl_sync(0xffffffffu, w, q);
-        if (q < nc) accumulate(wq, raw[q]);
-      }
-    } else {
+    __syncthreads();                     // shared arrays of the previous unit are free
+    if (tid < kCombineRows) {
       float M = -INFINITY;
-      for (int c0 = 0; c0 < nc; c0 += 32) {
-        float m = -INFINITY;
-        if (c0 + lane < nc) {
-          const float2 ml = prm.part_ml[(slot0 + c0 + lane) * kBM + row];
-          if (ml.y > 0.f) m = ml.x;
-        }
-        M = fmaxf(M, warp_max(m));
+#pragma unroll 4
+      for (int c = 0; c < nc; ++c) {
+        const float2 ml = prm.part_ml[(slot0 + c) * kBM + row0 + tid];
+        if (ml.y > 0.f) M = fmaxf(M, ml.x);
       }
-      wsum = 0.f;
-      for (int c0 = 0; c0 < nc; c0 += 32) {
-        const int cn = min(32, nc - c0);
-        float w = 0.f;
-        if (lane < cn) {
-          const float2 ml = prm.part_ml[(slot0 + c0 + lane) * kBM + row];
-          if (ml.y > 0.f) w = ml.y * ex2(ml.x - M);
-        }
-        wsum += warp_sum(w);
-        for (int c = 0; c < cn; c += kInFlight) {
-          float wc[kInFlight];
-          uint32_t raw[kInFlight][kPerLane / 2];
+      s_m[tid] = M;
+      s_sum[tid] = 0.f;
+    }
+    float acc[kVecThr][8];
 #pragma unroll
-          for (int q = 0; q < kInFlight; ++q) {
-            const int cc = min(c + q, cn - 1);     // in range; weight 0 past the end
-            const float wq = __shfl_sync(0xffffffffu, w, cc);
-            wc[q] = (c + q < cn) ? wq : 0.f;
-            load_o(slot0 + c0 + cc, raw[q]);
+    for (int i = 0; i < kVecThr; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+    for (int g0 = 0; g0 < nc; g0 += kCombineGroup) {
+      const int gn = min(kCombineGroup, nc - g0);
+      __syncthreads();                   // s_m ready; s_w of the previous group consumed
+      for (int e = tid; e < gn * kCombineRows; e += kCombineThreads) {
+        const int c = e / kCombineRows, r = e % kCombineRows;
+        const float2 ml = prm.part_ml[(slot0 + g0 + c) * kBM + row0 + r];
+        s_w[c][r] = ml.y > 0.f ? ml.y * ex2(ml.x - s_m[r]) : 0.f;
+      }
+      __syncthreads();
+      if (tid < kCombineRows) {
+        float sum = s_sum[tid];
+        for (int c = 0; c < gn; ++c) sum += s_w[c][tid];
+        s_sum[tid] = sum;
+      }
+      for (int c0 = 0; c0 < gn; c0 += kCombinePre) {
+        uint4 raw[kCombinePre][kVecThr];
+#pragma unroll
+        for (int q = 0; q < kCombinePre; ++q)
+          if (c0 + q < gn) {
+#pragma unroll
+            for (int i = 0; i < kVecThr; ++i) {
+              const int vi = tid + i * kCombineThreads;
+              const int r = vi / kVecRow, v = vi % kVecRow;
+              raw[q][i] = ld_vec(prm.part_o + ((slot0 + g0 + c0 + q) * kBM + row0 + r) * HD + v * 8);
+            }
           }
 #pragma unroll
-          for (int q = 0; q < kInFlight; ++q) accumulate(wc[q], raw[q]);
-        }
+        for (int q = 0; q < kCombinePre; ++q)
+          if (c0 + q < gn) {
+#pragma unroll
+            for (int i = 0; i < kVecThr; ++i) {
+              const int r = (tid + i * kCombineThreads) / kVecRow;
+              const float w = s_w[c0 + q][r];
+              const __half2* h = reinterpret_cast<const __half2*>(&raw[q][i]);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(h[e]);
+                acc[i][2 * e] = fmaf(w, f.x, acc[i][2 * e]);
+                acc[i][2 * e + 1] = fmaf(w, f.y, acc[i][2 * e + 1]);
+              }
+            }
+          }
       }
     }
-    const float inv = 1.f / wsum;
-    const int hq = kvh * prm.group + row % prm.group;
-    uint16_t* orow = prm.out + (tok * prm.n_q_heads + hq) * static_cast<int64_t>(HD) + lane * kPerLane;
-    if constexpr (kPerLane == 4) {
-      *reinterpret_cast<uint2*>(orow) = make_uint2(pack2<DT>(acc[0] * inv, acc[1] * inv),
-                                                   pack2<DT>(acc[2] * inv, acc[3] * inv));
-    } else {
-      *reinterpret_cast<uint32_t*>(orow) = pack2<DT>(acc[0] * inv, acc[1] * inv);
+    __syncthreads();                     // s_sum complete
+#pragma unroll
+    for (int i = 0; i < kVecThr; ++i) {
+      const int vi = tid + i * kCombineThreads;
+      const int r = vi / kVecRow, v = vi % kVecRow;
+      const int row = row0 + r;
+      const int64_t tok = static_cast<int64_t>(tile) * prm.tok_per_tile + row / prm.group;
+      if (tok >= prm.n_sel) continue;    // padding row of the last tile
+      const float inv = 1.f / s_sum[r];
+      const int hq = kvh * prm.group + row % prm.group;
+      uint4 o;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[e] = pack2<DT>(acc[i][2 * e] * inv, acc[i][2 * e + 1] * inv);
+      st_vec(prm.out + (tok * prm.n_q_heads + hq) * static_cast<int64_t>(HD) + v * 8, o);
     }
   }
 }
@@ -1051,10 +1036,9 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   const int grid = std::min(lay.max_items, sm_count());   // persistent: one CTA per SM
   kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(mq, mk, mv, prm);
   if (int rc = check_launch("partial_attn_kernel")) return rc;
-  // one warp per row of a split tile; at most every tile is split
-  const int64_t max_rows = static_cast<int64_t>(n_kv_heads) * lay.n_tiles * kBM;
-  const int comb_grid = static_cast<int>(std::min<int64_t>((max_rows + kCombineRows - 1) / kCombineRows,
-                                                           16 * sm_count()));
+  // one CTA per half split tile; at most every tile is split
+  const int64_t max_units = static_cast<int64_t>(n_kv_heads) * lay.n_tiles * (kBM / kCombineRows);
+  const int comb_grid = static_cast<int>(std::min<int64_t>(max_units, 2 * sm_count()));
   attn_combine_kernel<DT, HD><<<static_cast<unsigned>(comb_grid), kCombineThreads, 0, st>>>(prm);
   return check_launch("attn_combine_kernel");
 }
