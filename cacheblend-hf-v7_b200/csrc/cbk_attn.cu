@@ -23,9 +23,10 @@
 //
 // Warp roles (384 threads):
 //   warp 0        producer: fetches items, loads both Q tiles, then K and V tiles
-//                 into two separate 2-stage rings (TMA)
-//   warp 1        MMA issuer: per key tile j, for t = 0, 1: O_t += P_t(j) V(j),
-//                 then S_t(j+1) = Q_t K(j+1)^T.  MMAs issued by one thread run
+//                 into two separate 2-stage rings (TMA; one elected lane issues)
+//   warp 1        MMA issuer (one elected lane of the converged warp): per key
+//                 tile j, for t = 0, 1: O_t += P_t(j) V(j),
+//                 then S_t(j+1) = Q_t K(j+1)^T.  MMAs issued by one lane run
 //                 in order, so S_t(j+1) overwrites P_t(j) only after the PV
 //                 that reads it; while one tile's softmax runs, the tensor core
 //                 works on the other tile.
@@ -196,10 +197,11 @@ __device__ __forceinline__ void exp2_fma_pair(float x0, float x1, float& y0, flo
   y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
-// Pairs e (of the 16 per 32 columns) whose exponentials go to the FMA pipe on
+// Pairs e (of the 16 per 32 columns; 6 of 16, the best of a 25-62 % sweep)
+// whose exponentials go to the FMA pipe on
 // fully visible key tiles; the others use ex2.approx.
 #ifndef CBK_ATTN_EMU_MASK
-#define CBK_ATTN_EMU_MASK 0x8888
+#define CBK_ATTN_EMU_MASK 0x9292
 #endif
 
 // number of 128-key tiles a Q tile needs (its last token has the largest position)
@@ -302,126 +304,161 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     return true;
   };
 
-  if (warp == 0 && lane == 0) {
+  // warp-uniform bounded wait
+  auto wait_all = [&](uint32_t b, uint32_t parity) {
+    return __all_sync(0xffffffffu, wait_or_abort(b, parity, abort_flag));
+  };
+
+  if (warp == 0) {
     // ------------------------------------------------ item queue + TMA producer
-    tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_k);
-    tma_prefetch_desc(&tm_v);
+    // The whole warp runs the loop; one elected lane issues (see elect_one).
+    const bool leader = elect_one();
+    const int leader_lane = __ffs(__ballot_sync(0xffffffffu, leader)) - 1;
+    if (leader) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+    }
     int g = 0;                               // K/V tiles loaded by this CTA
     int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
     int n_q = 0;                             // Q loads issued
     for (int n = 0; !failed; ++n) {
-      if (n >= 2 && !wait_or_abort(bar(B_IEMPTY + (n & 1)), ((n >> 1) - 1) & 1, abort_flag)) {
+      if (n >= 2 && !wait_all(bar(B_IEMPTY + (n & 1)), ((n >> 1) - 1) & 1)) {
         failed = true;
         break;
       }
-      const int idx = atomicAdd(prm.queue, 1);
+      int idx = 0;
+      if (leader) idx = atomicAdd(prm.queue, 1);
+      idx = __shfl_sync(0xffffffffu, idx, leader_lane);
       const int4 item = idx < n_items ? prm.items[idx] : make_int4(-1, 0, 0, 0);
-      s_item[n & 1].x = item.x;
-      s_item[n & 1].y = item.y;
-      s_item[n & 1].z = item.z;
-      s_item[n & 1].w = item.w;
-      mbar_arrive(bar(B_IFULL + (n & 1)));   // release: the slot is visible to the waiters
+      if (leader) {
+        s_item[n & 1].x = item.x;
+        s_item[n & 1].y = item.y;
+        s_item[n & 1].z = item.z;
+        s_item[n & 1].w = item.w;
+        mbar_arrive(bar(B_IFULL + (n & 1)));   // release: the slot is visible to the waiters
+      }
       if (item.x < 0) break;
       const ItemGeom ig = item_geom(item, C, prm);
       // Q of this item once the previous item's last S = Q K^T has been issued
-      if (n_q > 0 && !wait_or_abort(bar(B_QEMPTY), (n_q - 1) & 1, abort_flag)) {
+      if (n_q > 0 && !wait_all(bar(B_QEMPTY), (n_q - 1) & 1)) {
         failed = true;
         break;
       }
-      mbar_expect_tx(bar(B_QFULL), ig.n_q_tiles * L::kQBytes);
-      for (int t = 0; t < ig.n_q_tiles; ++t)
+      if (leader) {
+        mbar_expect_tx(bar(B_QFULL), ig.n_q_tiles * L::kQBytes);
+        for (int t = 0; t < ig.n_q_tiles; ++t)
 #pragma unroll
-        for (int h = 0; h < HD / 64; ++h)
-          tma_load_3d(sQ + t * L::kQBytes + h * (kBM * 128), &tm_q, bar(B_QFULL), h * 64,
-                      ig.kvh * prm.group, static_cast<int>(ig.tok0[t]));
+          for (int h = 0; h < HD / 64; ++h)
+            tma_load_3d(sQ + t * L::kQBytes + h * (kBM * 128), &tm_q, bar(B_QFULL), h * 64,
+                        ig.kvh * prm.group, static_cast<int>(ig.tok0[t]));
+      }
       ++n_q;
       for (int j = 0; j < ig.n_all; ++j, ++g) {
         const int st = g & 1;
-        if (g >= 2 && !wait_or_abort(bar(B_KEMPTY + st), ((g >> 1) - 1) & 1, abort_flag)) {
+        if (g >= 2 && !wait_all(bar(B_KEMPTY + st), ((g >> 1) - 1) & 1)) {
           failed = true;
           break;
         }
-        mbar_expect_tx(bar(B_KFULL + st), L::kKVBytes);
+        if (leader) {
+          mbar_expect_tx(bar(B_KFULL + st), L::kKVBytes);
 #pragma unroll
-        for (int h = 0; h < HD / 64; ++h)
-          tma_load_3d(sK0 + st * L::kKVBytes + h * (kBN * 128), &tm_k, bar(B_KFULL + st), h * 64, ig.kvh,
-                      (ig.j0 + j) * kBN);
+          for (int h = 0; h < HD / 64; ++h)
+            tma_load_3d(sK0 + st * L::kKVBytes + h * (kBN * 128), &tm_k, bar(B_KFULL + st), h * 64, ig.kvh,
+                        (ig.j0 + j) * kBN);
+        }
         last_k[st] = g;
-        if (g >= 2 && !wait_or_abort(bar(B_VEMPTY + st), ((g >> 1) - 1) & 1, abort_flag)) {
+        if (g >= 2 && !wait_all(bar(B_VEMPTY + st), ((g >> 1) - 1) & 1)) {
           failed = true;
           break;
         }
-        mbar_expect_tx(bar(B_VFULL + st), L::kKVBytes);
+        if (leader) {
+          mbar_expect_tx(bar(B_VFULL + st), L::kKVBytes);
 #pragma unroll
-        for (int h = 0; h < HD / 64; ++h)
-          tma_load_3d(sV0 + st * L::kKVBytes + h * (kBN * 128), &tm_v, bar(B_VFULL + st), h * 64, ig.kvh,
-                      (ig.j0 + j) * kBN);
+          for (int h = 0; h < HD / 64; ++h)
+            tma_load_3d(sV0 + st * L::kKVBytes + h * (kBN * 128), &tm_v, bar(B_VFULL + st), h * 64, ig.kvh,
+                        (ig.j0 + j) * kBN);
+        }
         last_v[st] = g;
       }
     }
     // Drain: every armed copy must land before the CTA can retire.
-    if (n_q > 0 && !mbar_wait(bar(B_QFULL), (n_q - 1) & 1)) failed = true;
+    if (n_q > 0 && !__all_sync(0xffffffffu, mbar_wait(bar(B_QFULL), (n_q - 1) & 1))) failed = true;
     for (int st = 0; st < 2; ++st) {
-      if (last_k[st] >= 0 && !mbar_wait(bar(B_KFULL + st), (last_k[st] >> 1) & 1)) failed = true;
-      if (last_v[st] >= 0 && !mbar_wait(bar(B_VFULL + st), (last_v[st] >> 1) & 1)) failed = true;
+      if (last_k[st] >= 0 && !__all_sync(0xffffffffu, mbar_wait(bar(B_KFULL + st), (last_k[st] >> 1) & 1)))
+        failed = true;
+      if (last_v[st] >= 0 && !__all_sync(0xffffffffu, mbar_wait(bar(B_VFULL + st), (last_v[st] >> 1) & 1)))
+        failed = true;
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer
+    // The whole warp runs the loop; one elected lane issues the MMAs and commits
+    // (see elect_one).
+    const bool leader = elect_one();
     const uint32_t idesc_s = umma_idesc_f16(DT, kBM, kBN, 0);
     const uint32_t idesc_o = umma_idesc_f16(DT, kBM, HD, 1);
+    // Base descriptors of the Q tiles and K/V stages, built once: a slice's
+    // descriptor is its base plus the slice offset in 16-byte units (the start
+    // address field; shared-memory offsets stay below 2^18 bytes, so no carry).
+    uint64_t dq[2], dk[2], dv[2];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      dq[b] = umma_desc_sw128(sQ + b * L::kQBytes, 16, 1024);
+      dk[b] = umma_desc_sw128(sK0 + b * L::kKVBytes, 16, 1024);
+      dv[b] = umma_desc_sw128(sV0 + b * L::kKVBytes, kBN * 128, 1024);
+    }
     auto issue_s = [&](int t, int g) {
-      const uint32_t kb = sK0 + (g & 1) * L::kKVBytes;
-      const uint32_t qb = sQ + t * L::kQBytes;
+      const uint64_t q0 = t ? dq[1] : dq[0];
+      const uint64_t k0 = (g & 1) ? dk[1] : dk[0];
 #pragma unroll
       for (int kk = 0; kk < HD / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-        const uint32_t offk = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
-        umma_f16_ss(tmem + 256 * t, umma_desc_sw128(qb + off, 16, 1024),
-                    umma_desc_sw128(kb + offk, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        const uint32_t off = ((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4;
+        const uint32_t offk = ((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4;
+        if (leader) umma_f16_ss(tmem + 256 * t, q0 + off, k0 + offk, idesc_s, kk > 0 ? 1u : 0u);
       }
-      umma_commit(bar(B_SFULL + t));
+      if (leader) umma_commit(bar(B_SFULL + t));
     };
     auto issue_pv = [&](int t, int g, bool acc) {
-      const uint32_t vb = sV0 + (g & 1) * L::kKVBytes;
+      const uint64_t v0 = (g & 1) ? dv[1] : dv[0];
 #pragma unroll
       for (int kk = 0; kk < kBN / 16; ++kk)
-        umma_f16_ts(tmem + 256 * t + kBN, tmem + 256 * t + kk * 8,
-                    umma_desc_sw128(vb + kk * 16 * 128, kBN * 128, 1024), idesc_o,
-                    (acc || kk > 0) ? 1u : 0u);
+        if (leader)
+          umma_f16_ts(tmem + 256 * t + kBN, tmem + 256 * t + kk * 8, v0 + ((kk * 16 * 128) >> 4), idesc_o,
+                      (acc || kk > 0) ? 1u : 0u);
     };
     int g = 0;                 // K/V tiles consumed
     int pc[2] = {0, 0};        // P tiles consumed per Q-tile slot
     int oc[2] = {0, 0};        // O results handed to the epilogue per Q-tile slot
     for (int n = 0; !failed; ++n) {
       int4 item;
-      if (!take_item(n, item)) {
+      if (!__all_sync(0xffffffffu, take_item(n, item))) {
         failed = true;
         break;
       }
-      mbar_arrive(bar(B_IEMPTY + (n & 1)));
+      if (leader) mbar_arrive(bar(B_IEMPTY + (n & 1)));
       if (item.x < 0) break;
       const ItemGeom ig = item_geom(item, C, prm);
-      if (!wait_or_abort(bar(B_QFULL), n & 1, abort_flag) ||
-          !wait_or_abort(bar(B_KFULL + (g & 1)), (g >> 1) & 1, abort_flag)) {
+      if (!wait_all(bar(B_QFULL), n & 1) || !wait_all(bar(B_KFULL + (g & 1)), (g >> 1) & 1)) {
         failed = true;
         break;
       }
       tc_fence_after();
       // S(0): the previous item's PVs that read P from these columns were issued
-      // earlier by this thread, so they complete first
+      // earlier by this warp, so they complete first
       if (ig.n_kv[0] > 0) issue_s(0, g);
       if (ig.n_kv[1] > 0) issue_s(1, g);
-      umma_commit(bar(B_KEMPTY + (g & 1)));
-      if (ig.n_all == 1) umma_commit(bar(B_QEMPTY));
+      if (leader) {
+        umma_commit(bar(B_KEMPTY + (g & 1)));
+        if (ig.n_all == 1) umma_commit(bar(B_QEMPTY));
+      }
       for (int j = 0; j < ig.n_all && !failed; ++j) {
         const int gj = g + j;
         const bool next_k = j + 1 < ig.n_all;
-        if (next_k && !wait_or_abort(bar(B_KFULL + ((gj + 1) & 1)), ((gj + 1) >> 1) & 1, abort_flag)) {
+        if (next_k && !wait_all(bar(B_KFULL + ((gj + 1) & 1)), ((gj + 1) >> 1) & 1)) {
           failed = true;
           break;
         }
-        if (!wait_or_abort(bar(B_VFULL + (gj & 1)), (gj >> 1) & 1, abort_flag)) {
+        if (!wait_all(bar(B_VFULL + (gj & 1)), (gj >> 1) & 1)) {
           failed = true;
           break;
         }
@@ -429,13 +466,13 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int t = 0; t < 2; ++t) {
           const int n_t = ig.n_kv[t];
           if (j >= n_t) continue;
-          if (!wait_or_abort(bar(B_PFULL + t), pc[t] & 1, abort_flag)) {
+          if (!wait_all(bar(B_PFULL + t), pc[t] & 1)) {
             failed = true;
             break;
           }
           ++pc[t];
           // the first PV of an item overwrites O: the previous epilogue must have read it
-          if (j == 0 && oc[t] > 0 && !wait_or_abort(bar(B_OFREE + t), (oc[t] - 1) & 1, abort_flag)) {
+          if (j == 0 && oc[t] > 0 && !wait_all(bar(B_OFREE + t), (oc[t] - 1) & 1)) {
             failed = true;
             break;
           }
@@ -444,20 +481,22 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           if (j + 1 < n_t) {
             issue_s(t, gj + 1);
           } else {
-            umma_commit(bar(B_ODONE + t));
+            if (leader) umma_commit(bar(B_ODONE + t));
             ++oc[t];
           }
         }
         if (failed) break;
-        umma_commit(bar(B_VEMPTY + (gj & 1)));
-        if (next_k) umma_commit(bar(B_KEMPTY + ((gj + 1) & 1)));
-        if (j + 2 == ig.n_all) umma_commit(bar(B_QEMPTY));   // last S of the item issued
+        if (leader) {
+          umma_commit(bar(B_VEMPTY + (gj & 1)));
+          if (next_k) umma_commit(bar(B_KEMPTY + ((gj + 1) & 1)));
+          if (j + 2 == ig.n_all) umma_commit(bar(B_QEMPTY));   // last S of the item issued
+        }
       }
       g += ig.n_all;
     }
-    // Drain: all MMAs issued by this thread complete before TMEM is released.
-    umma_commit(bar(B_DRAIN));
-    if (!mbar_wait(bar(B_DRAIN), 0)) failed = true;
+    // Drain: all MMAs issued by this warp complete before TMEM is released.
+    if (leader) umma_commit(bar(B_DRAIN));
+    if (!__all_sync(0xffffffffu, mbar_wait(bar(B_DRAIN), 0))) failed = true;
   } else if (warp >= 4) {
     // ----------------------------------------------- softmax + epilogue warps
     const int t = (warp - 4) >> 2;            // Q tile of this warpgroup
