@@ -149,12 +149,20 @@ def run_ours(args):
 
     model = build_model(device)
     lw = cb.LayerwiseModel.from_hf(model)
-    store = cb.KVStore()
     reqs = [build_request(model, cb, seed=1000 * rank + r, device=device) for r in range(args.requests)]
-    for chunks in reqs:
-        for c in chunks:
-            K, V = cb.precompute_chunk_kv(lw, c)
-            store.put(c.chunk_id, K, V)
+    if args.kv_arena:
+        kv_dim = MISTRAL_7B["num_key_value_heads"] * MISTRAL_7B["head_dim"]
+        n_tok = sum(c.length for chunks in reqs for c in chunks)
+        store = cb.KVArena(MISTRAL_7B["num_hidden_layers"], kv_dim, n_tok, device)
+        for chunks in reqs:
+            for c in chunks:
+                cb.precompute_chunk_kv_into(lw, c, store)
+    else:
+        store = cb.KVStore()
+        for chunks in reqs:
+            for c in chunks:
+                K, V = cb.precompute_chunk_kv(lw, c)
+                store.put(c.chunk_id, K, V)
     S = sum(c.length for c in reqs[0])
     stream = torch.cuda.current_stream(device)
 
@@ -279,6 +287,7 @@ def run_ours(args):
                    "selection": {"min_pos": int(min(idx_l)), "median_pos": int(sorted(idx_l)[len(idx_l) // 2]),
                                  "frac_in_last_1088": round(sum(p >= S - 1088 for p in idx_l) / len(idx_l), 3)},
                    "requests_per_rank": args.requests, "parallelism": f"by-request x{world}",
+                   "kv_store": "KVArena (one device pool)" if args.kv_arena else "KVStore (tensor per chunk and layer)",
                    "l2": "inputs larger than L2 (14.5 GB weights, 0.81 GB fused KV per step)"},
         "e2e": {"value": round(world * S / (e2e_step * 1e-3), 1), "unit": "tokens/s",
                 "ttft_ms": round(e2e_step, 3), "h2d_bytes_per_step": S * 8, "d2h_bytes_per_step": 8},
@@ -991,6 +1000,7 @@ def main():
     ap.add_argument("--attn-dist", default="uniform", choices=["uniform", "tail"])
     ap.add_argument("--sh-layers", type=int, default=80, help="layers of the sharded 128K workload")
     ap.add_argument("--kv-layers", type=int, default=32, help="layers of the KV microbench")
+    ap.add_argument("--kv-arena", action="store_true", help="chunk K/V in one KVArena device pool")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -13,16 +13,16 @@ __version__ = "0.7.0+b200"
 from cacheblend import _native  # noqa: F401  (loads libcbk.so or raises ImportError)
 from cacheblend.tolerance import Tolerance, ToleranceResult, assert_logits_close
 from cacheblend.model import LayerwiseModel, LayerwiseOutput
-from cacheblend.kv_store import KVStore
+from cacheblend.kv_store import KVArena, KVStore
 from cacheblend.chunker import Chunk, chunk_texts, fused_input_ids, chunk_offsets
 from cacheblend.rope import apply_rope_shift
-from cacheblend.precompute import precompute_chunk_kv, precompute_from_cache_prompt
+from cacheblend.precompute import precompute_chunk_kv, precompute_chunk_kv_into, precompute_from_cache_prompt
 from cacheblend.fusor import fuse_full_recompute, fuse_full_reuse, fuse_selective, fuse_prefix_cache
 from cacheblend.hkvd import kv_deviation, select_top_k
 
 __all__ = [
     "Tolerance", "ToleranceResult", "assert_logits_close", "LayerwiseModel", "LayerwiseOutput",
-    "KVStore", "Chunk", "chunk_texts", "fused_input_ids", "chunk_offsets", "apply_rope_shift",
-    "precompute_chunk_kv", "precompute_from_cache_prompt", "fuse_full_recompute",
+    "KVStore", "KVArena", "Chunk", "chunk_texts", "fused_input_ids", "chunk_offsets", "apply_rope_shift",
+    "precompute_chunk_kv", "precompute_chunk_kv_into", "precompute_from_cache_prompt", "fuse_full_recompute",
     "fuse_full_reuse", "fuse_selective", "fuse_prefix_cache", "kv_deviation", "select_top_k",
 ]

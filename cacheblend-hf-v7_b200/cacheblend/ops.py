@@ -10,6 +10,8 @@ from __future__ import annotations
 import ctypes
 from typing import Sequence
 
+import numpy as np
+
 import torch
 
 from cacheblend import _native as N
@@ -110,6 +112,27 @@ class ChunkTable:
         host = torch.empty((len(self.layers), self.n_chunks, 2), dtype=torch.int64, pin_memory=True)
         hv = host.numpy()
         kv_dim = None
+        slabs = [e.get("_slab") for e in entries]
+        if self.n_chunks and all(sl is not None for sl in slabs) and \
+                len({(sl[0], sl[3], sl[4], sl[5]) for sl in slabs}) == 1:
+            # chunks of one KVArena: the table follows from the slab offsets
+            pool, _, _, row_elems, n_layers, kv_dim = slabs[0]
+            t0 = entries[0]["K"][self.layers[0]]
+            if t0.device != device:
+                raise RuntimeError(f"chunk tensor on {t0.device}, model on {device}")
+            esz = t0.element_size()
+            first = np.array([sl[1] for sl in slabs], dtype=np.int64)
+            lens_a = np.array([sl[2] for sl in slabs], dtype=np.int64)
+            lay = np.array(self.layers, dtype=np.int64)
+            if lay.min() < 0 or lay.max() >= n_layers:
+                raise ValueError("chunk table layer out of range of the arena")
+            kptr = pool + (first * row_elems)[None, :] * esz + lay[:, None] * (2 * lens_a * kv_dim * esz)[None, :]
+            hv[:, :, 0] = kptr
+            hv[:, :, 1] = kptr + (lens_a * kv_dim * esz)[None, :]
+            lens = lens_a.tolist()
+            self._keep = [e["K"][self.layers[0]] for e in entries]   # views keep the pool alive
+            self._finish(host, lens, kv_dim, t0.dtype, device)
+            return
         for c, e in enumerate(entries):
             for li, l in enumerate(self.layers):
                 k = _chunk_rows(e["K"][l], device)
@@ -127,6 +150,9 @@ class ChunkTable:
                     lens.append(k.shape[0])
                 elif k.shape[0] != lens[c]:
                     raise ValueError("chunk length differs across layers")
+        self._finish(host, lens, kv_dim, self._keep[0].dtype, device)
+
+    def _finish(self, host, lens, kv_dim, dtype, device):
         starts = [0]
         for n in lens:
             starts.append(starts[-1] + n)
@@ -136,7 +162,7 @@ class ChunkTable:
         self.lengths = lens
         self.srcs = host.to(device, non_blocking=True)
         self.starts = hs.to(device, non_blocking=True)
-        self.dtype = self._keep[0].dtype
+        self.dtype = dtype
 
     def layer_ptr(self, layer: int) -> int:
         """Device address of the srcs row of one layer (n_chunks entries)."""

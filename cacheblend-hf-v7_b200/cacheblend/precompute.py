@@ -41,6 +41,19 @@ def precompute_chunk_kv(layerwise_model, chunk: Chunk):
     return K, V
 
 
+def precompute_chunk_kv_into(layerwise_model, chunk: Chunk, arena):
+    """precompute_chunk_kv writing straight into a KVArena slab (one copy of each
+    layer's K and V, no intermediate clone); returns the chunk's entry."""
+    ids = torch.tensor([chunk.token_ids], dtype=torch.long, device=layerwise_model.device)
+    v_dict = _forward_capture(layerwise_model, ids)
+    entry = arena.reserve(chunk.chunk_id, len(chunk.token_ids))
+    with torch.no_grad():
+        for i in range(layerwise_model.num_layers):
+            entry["K"][i].copy_(layerwise_model.get_pre_rope_k(i))
+            entry["V"][i].copy_(v_dict[i])
+    return entry
+
+
 def precompute_from_cache_prompt(layerwise_model, chunks_in_cache_order, skip_chunk_ids=None):
     """One forward over the whole cache prompt; each chunk's K / V is sliced at
     its position (cross-chunk attention included).  Returns a KVStore."""
