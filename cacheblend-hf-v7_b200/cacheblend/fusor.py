@@ -227,63 +227,77 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
                             mode=rope_mode, status=status)
         assembled = torch.cuda.Event()
         assembled.record(side)
-        fused_k.record_stream(side)
-        fused_v.record_stream(side)
+        # No record_stream: the current stream waits for `assembled` below, before
+        # anything can free these buffers, so their memory returns to the caching
+        # allocator in stream order.  (record_stream would hold it until the side
+        # stream's event completes, and with the device running behind the host the
+        # next blend could not reuse it and would allocate anew.)
 
-        if input_ids is None:
-            ids = fused_input_ids(chunks, device=device)
-        else:
-            ids = input_ids.reshape(1, -1).to(device, non_blocking=True)
-            if ids.shape[1] != S:
-                raise ValueError(f"input_ids has {ids.shape[1]} tokens, chunks have {S}")
-        lw._pre_rope_k = {}
-        pos_all = torch.arange(S, device=device, dtype=torch.int64)
-        h = inner.embed_tokens(ids)     # residual stream; updated in place by the fused norms
-        m = None                        # pending MLP output, added by the next norm
+        # the side stream writes fused_k / fused_v until `assembled`: whatever
+        # happens below, the current stream is ordered after it before they can
+        # be freed
+        try:
+            if input_ids is None:
+                ids = fused_input_ids(chunks, device=device)
+            else:
+                ids = input_ids.reshape(1, -1).to(device, non_blocking=True)
+                if ids.shape[1] != S:
+                    raise ValueError(f"input_ids has {ids.shape[1]} tokens, chunks have {S}")
+            lw._pre_rope_k = {}
+            pos_all = torch.arange(S, device=device, dtype=torch.int64)
+            h = inner.embed_tokens(ids)     # residual stream; updated in place by the fused norms
+            m = None                        # pending MLP output, added by the next norm
 
-        ws_dense = ops.attn_workspace(S, S, geo.n_q, geo.n_kv, geo.head_dim, device) if ck else None
-        for li in range(ck):                                  # dense layers (one shared plan)
-            layer = inner.layers[li]
-            hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None,
-                       status=status)
-            a, _ = _attention_block(layer, geo, hn, pos_all, S, rope,
-                                    fused_k[li], fused_v[li], False, status, rope_mode, ws_dense, li > 0,
-                                    tag="_dense")
-            m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=a, sum_out=h, status=status))
+            ws_dense = ops.attn_workspace(S, S, geo.n_q, geo.n_kv, geo.head_dim, device) if ck else None
+            for li in range(ck):                                  # dense layers (one shared plan)
+                layer = inner.layers[li]
+                hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None,
+                           status=status)
+                a, _ = _attention_block(layer, geo, hn, pos_all, S, rope,
+                                        fused_k[li], fused_v[li], False, status, rope_mode, ws_dense, li > 0,
+                                        tag="_dense")
+                m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=a, sum_out=h, status=status))
 
-        # check layer: full-row K, HKVD, then sparse from here on
-        layer = inner.layers[ck]
-        attn = layer.self_attn
-        hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None, status=status)
-        k_pre = attn.k_proj(hn)             # every row: HKVD compares each token's fresh K
-        idx, deviations = ops.hkvd_select(k_pre[0], table, ck, k_sel, force_last=True, status=status)
-        # Q and V only for the selected rows (the reference projects all S rows,
-        # fusor.py:333-335, and keeps these)
-        hn_sel = hn.index_select(1, idx)
-        q = attn.q_proj(hn_sel)
-        v = attn.v_proj(hn_sel)
-        k_rows = k_pre.index_select(1, idx)
-        cur.wait_event(assembled)
-        q_rot = ops.rope_scatter(q[0], k_rows[0], v[0], idx, False, S, geo.n_q, geo.n_kv, geo.head_dim,
-                                 rope, fused_k[ck], fused_v[ck], mode=rope_mode, status=status)
-        ws_sparse = ops.attn_workspace(k_sel, S, geo.n_q, geo.n_kv, geo.head_dim, device)
-        a = ops.partial_attn(q_rot, fused_k[ck], fused_v[ck], idx, geo.n_q, geo.n_kv, geo.head_dim,
-                             geo.scaling, status=status, workspace=ws_sparse, reuse_plan=False)
-        # selected residual rows gathered inside the norm launch
-        o = attn.o_proj(a.unsqueeze(0))
-        hs = torch.empty_like(o)
-        m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=o, rows=idx, sum_out=hs, status=status))
+            # check layer: full-row K, HKVD, then sparse from here on
+            layer = inner.layers[ck]
+            attn = layer.self_attn
+            hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None, status=status)
+            k_pre = attn.k_proj(hn)             # every row: HKVD compares each token's fresh K
+            idx, deviations = ops.hkvd_select(k_pre[0], table, ck, k_sel, force_last=True, status=status)
+            # Q and V only for the selected rows (the reference projects all S rows,
+            # fusor.py:333-335, and keeps these)
+            hn_sel = hn.index_select(1, idx)
+            q = attn.q_proj(hn_sel)
+            v = attn.v_proj(hn_sel)
+            k_rows = k_pre.index_select(1, idx)
+            cur.wait_event(assembled)
+            q_rot = ops.rope_scatter(q[0], k_rows[0], v[0], idx, False, S, geo.n_q, geo.n_kv, geo.head_dim,
+                                     rope, fused_k[ck], fused_v[ck], mode=rope_mode, status=status)
+            ws_sparse = ops.attn_workspace(k_sel, S, geo.n_q, geo.n_kv, geo.head_dim, device)
+            a = ops.partial_attn(q_rot, fused_k[ck], fused_v[ck], idx, geo.n_q, geo.n_kv, geo.head_dim,
+                                 geo.scaling, status=status, workspace=ws_sparse, reuse_plan=False)
+            # selected residual rows gathered inside the norm launch
+            o = attn.o_proj(a.unsqueeze(0))
+            hs = torch.empty_like(o)
+            m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=o, rows=idx, sum_out=hs, status=status))
 
-        for li in range(ck + 1, n_layers):                    # sparse layers
-            layer = inner.layers[li]
-            hn = _norm(layer.input_layernorm, hs, delta=m, sum_out=hs, status=status)
-            a, _ = _attention_block(layer, geo, hn, idx, S, rope,
-                                    fused_k[li], fused_v[li], False, status, rope_mode, ws_sparse, True)
-            m = _mlp(layer, _norm(layer.post_attention_layernorm, hs, delta=a, sum_out=hs, status=status))
+            for li in range(ck + 1, n_layers):                    # sparse layers
+                layer = inner.layers[li]
+                hn = _norm(layer.input_layernorm, hs, delta=m, sum_out=hs, status=status)
+                a, _ = _attention_block(layer, geo, hn, idx, S, rope,
+                                        fused_k[li], fused_v[li], False, status, rope_mode, ws_sparse, True)
+                m = _mlp(layer, _norm(layer.post_attention_layernorm, hs, delta=a, sum_out=hs, status=status))
 
-        logits_sparse = lw.model.lm_head(_norm(inner.norm, hs, delta=m, status=status))   # (1, k, vocab)
-        logits = torch.zeros((1, S, logits_sparse.shape[-1]), dtype=logits_sparse.dtype, device=device)
-        logits[0].index_copy_(0, idx, logits_sparse[0])
+            logits_sparse = lw.model.lm_head(_norm(inner.norm, hs, delta=m, status=status))   # (1, k, vocab)
+            # dense (1, S, vocab) with zero rows outside the selection, one write pass
+            # (rows whose byte length is not a multiple of 16 take torch's zeros + index_copy_)
+            if (logits_sparse.shape[-1] * logits_sparse.element_size()) % 16 == 0:
+                logits = ops.scatter_rows(logits_sparse[0], idx, S).unsqueeze(0)
+            else:
+                logits = torch.zeros((1, S, logits_sparse.shape[-1]), dtype=logits_sparse.dtype, device=device)
+                logits[0].index_copy_(0, idx, logits_sparse[0])
+        finally:
+            cur.wait_event(assembled)
 
     result = logits
     if return_layerwise_output:

@@ -380,3 +380,24 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = No
                                    dtype_code(gate.dtype), _vp(o2), o2.stride(0), _stream(dev)),
                 "cbk_silu_mul")
     return out
+
+
+def scatter_rows(src: torch.Tensor, idx: torch.Tensor, n_rows: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Dense [n_rows][...] rows: out[idx[j]] = src[j], zeros elsewhere (idx ascending,
+    distinct), every output byte written once."""
+    dev = require_cuda(src, idx, out)
+    s2 = _rows(src, "src")
+    if idx.dtype != torch.int64 or idx.numel() != s2.shape[0]:
+        raise ValueError("scatter_rows: idx must be int64 with one entry per source row")
+    idx = idx.contiguous()
+    if out is None:
+        out = torch.empty((n_rows, s2.shape[1]), dtype=src.dtype, device=dev)
+    o2 = out.view(-1, s2.shape[1])
+    if o2.shape[0] != n_rows:
+        raise ValueError(f"scatter_rows: out has {o2.shape[0]} rows, expected {n_rows}")
+    row_bytes = s2.shape[1] * s2.element_size()
+    with TIMES.span("scatter_rows", dev):
+        N.check(N.LIB.cbk_scatter_rows(_vp(s2), s2.stride(0) * s2.element_size(), _vp(idx), idx.numel(), _vp(o2),
+                                       o2.stride(0) * o2.element_size(), int(n_rows), row_bytes, _stream(dev)),
+                "cbk_scatter_rows")
+    return out

@@ -123,6 +123,42 @@ __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, int64_t g_stride
   }
 }
 
+// Dense rows from selected rows: dst[r] = src[j] where idx[j] == r, zeros for
+// the rows no index names.  idx is ascending and distinct; a row finds its
+// source by binary search (thread 0 of the block, broadcast through shared
+// memory), then the block writes it with 16-byte stores, so every output byte
+// is written exactly once.
+constexpr int kScatterRowThreads = 256;
+
+__global__ void __launch_bounds__(kScatterRowThreads)
+scatter_rows_kernel(const uint8_t* __restrict__ src, int64_t src_stride, const int64_t* __restrict__ idx,
+                    int64_t k, uint8_t* __restrict__ dst, int64_t dst_stride, int64_t S, int64_t row_bytes) {
+  __shared__ int64_t s_src;
+  const int64_t n_vec = row_bytes >> 4;
+  for (int64_t r = blockIdx.x; r < S; r += gridDim.x) {
+    if (threadIdx.x == 0) {
+      int64_t lo = 0, hi = k - 1, found = -1;
+      while (lo <= hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        const int64_t v = idx[mid];
+        if (v == r) { found = mid; break; }
+        if (v < r) lo = mid + 1; else hi = mid - 1;
+      }
+      s_src = found;
+    }
+    __syncthreads();
+    const int64_t j = s_src;
+    uint4* d = reinterpret_cast<uint4*>(dst + r * dst_stride);
+    if (j >= 0) {
+      const uint4* sr = reinterpret_cast<const uint4*>(src + j * src_stride);
+      for (int64_t v = threadIdx.x; v < n_vec; v += kScatterRowThreads) d[v] = ld_stream(sr + v);
+    } else {
+      for (int64_t v = threadIdx.x; v < n_vec; v += kScatterRowThreads) d[v] = make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();                      // s_src is rewritten for the next row
+  }
+}
+
 int sm_count_layer() {
   static int cache[64] = {};
   int dev = 0;
@@ -204,4 +240,23 @@ extern "C" int cbk_silu_mul(const void* gate, int64_t gate_stride, const void* u
   else
     silu_mul_kernel<CBK_F16><<<grid, threads, 0, st>>>(g, gate_stride, u, up_stride, cols, n_rows, o, out_stride);
   return check_launch("silu_mul_kernel");
+}
+
+extern "C" int cbk_scatter_rows(const void* src, int64_t src_stride_bytes, const int64_t* idx, int64_t k,
+                                void* dst, int64_t dst_stride_bytes, int64_t S, int64_t row_bytes,
+                                void* stream) {
+  if (!dst || (k > 0 && (!src || !idx)))
+    return set_error(CBK_ERR_INVALID, "cbk_scatter_rows: null pointer argument");
+  if (S < 0 || k < 0 || k > S || row_bytes <= 0 || row_bytes % 16 != 0)
+    return set_error(CBK_ERR_INVALID, "cbk_scatter_rows: need 0 <= k <= S and row_bytes %% 16 == 0");
+  if (dst_stride_bytes < row_bytes || (k > 0 && src_stride_bytes < row_bytes) ||
+      (dst_stride_bytes | (k > 0 ? src_stride_bytes : 0)) % 16 != 0 || !aligned16(dst) ||
+      (k > 0 && !aligned16(src)))
+    return set_error(CBK_ERR_INVALID, "cbk_scatter_rows: rows must be 16-byte aligned and strided");
+  if (S == 0) return CBK_OK;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(S, 8LL * sm_count_layer()));
+  scatter_rows_kernel<<<grid, kScatterRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), src_stride_bytes, idx, k, static_cast<uint8_t*>(dst), dst_stride_bytes, S,
+      row_bytes);
+  return check_launch("scatter_rows_kernel");
 }

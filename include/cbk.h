@@ -205,6 +205,13 @@ int cbk_add_rmsnorm(const void* x, int64_t x_stride, int64_t x_rows, const int64
 int cbk_silu_mul(const void* gate, int64_t gate_stride, const void* up, int64_t up_stride,
                  int64_t n_rows, int cols, int dtype, void* out, int64_t out_stride, void* stream);
 
+/* Dense logits of the selected rows (fusor.py:483-491, the (1, S, vocab) zeros
+ * plus index_copy_): dst[r] = src[j] for idx[j] == r, zero rows elsewhere, each
+ * output byte written once.  idx: k int64 ascending distinct positions in
+ * [0, S); rows of row_bytes (multiple of 16), 16-byte aligned, byte strides. */
+int cbk_scatter_rows(const void* src, int64_t src_stride_bytes, const int64_t* idx, int64_t k, void* dst,
+                     int64_t dst_stride_bytes, int64_t S, int64_t row_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -69,6 +69,13 @@ def test_abi_version_and_pure_helpers():
     ("cbk_silu_mul(16, 64, None, 64, 4, 64, 0, 16, 64, None)", -1),
     ("cbk_silu_mul(16, 64, 16, 60, 4, 64, 0, 16, 64, None)", -1),
     ("cbk_silu_mul(16, 64, 16, 64, 0, 64, 0, 16, 64, None)", 0),
+    # scatter_rows(src, src_stride, idx, k, dst, dst_stride, S, row_bytes, stream)
+    ("cbk_scatter_rows(16, 64, 16, 2, None, 64, 4, 64, None)", -1),
+    ("cbk_scatter_rows(16, 64, 16, 5, 16, 64, 4, 64, None)", -1),
+    ("cbk_scatter_rows(16, 64, 16, 2, 16, 64, 4, 60, None)", -1),
+    ("cbk_scatter_rows(16, 64, 16, 2, 24, 64, 4, 64, None)", -1),
+    ("cbk_scatter_rows(16, 32, 16, 2, 16, 64, 4, 64, None)", -1),
+    ("cbk_scatter_rows(16, 64, 16, 0, 16, 64, 0, 64, None)", 0),
 ])
 def test_validation_errors_before_any_launch(call, code):
     from cacheblend import _native as N

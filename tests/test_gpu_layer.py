@@ -137,3 +137,19 @@ def test_silu_mul_strided_halves():
     gate, up = gu[:, :1024], gu[:, 1024:]
     with torch.inference_mode():
         assert torch.equal(ops.silu_mul(gate, up), torch.nn.functional.silu(gate) * up)
+
+
+@pytest.mark.parametrize("S,k,V,dtype", [(544, 81, 1000, torch.bfloat16), (6208, 931, 32000, torch.bfloat16),
+                                         (100, 100, 512, torch.float32), (50, 1, 64, torch.float16),
+                                         (10, 0, 64, torch.bfloat16)])
+def test_scatter_rows_dense_logits(S, k, V, dtype):
+    """ops.scatter_rows == torch zeros + index_copy_ (the reference's dense logits), bit for bit."""
+    from cacheblend import ops
+    g = torch.Generator(device=DEV).manual_seed(S + k)
+    idx = torch.sort(torch.randperm(S, generator=g, device=DEV)[:k])[0]
+    src = torch.randn((k, V), generator=g, device=DEV).to(dtype)
+    ref = torch.zeros((S, V), dtype=dtype, device=DEV)
+    ref.index_copy_(0, idx, src)
+    out = torch.full((S, V), 7.0, dtype=dtype, device=DEV)       # every byte must be rewritten
+    ops.scatter_rows(src, idx, S, out=out)
+    assert torch.equal(out, ref)
