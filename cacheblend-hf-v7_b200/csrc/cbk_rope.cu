@@ -202,15 +202,17 @@ rope_rows_kernel(const uint16_t* in, uint16_t* out, int64_t n_rows, int n_heads,
 // ---------------------------------------------------------------------------
 // Fresh rows of one layer: RoPE(Q) -> q_out, RoPE(K) and V scattered into the
 // fused cache at the selected positions.  Work unit = one warp: 64 RoPE pair
-// groups of Q or of K (2 per lane), or 128 V vectors (4 per lane); a selected
-// row has ceil(Hq*D/16 / 64) + ceil(Hkv*D/16 / 64) + ceil(Hkv*D/8 / 128) units.
+// groups of Q or of K (2 per lane), or 64 V vectors (2 per lane); a selected
+// row has ceil(Hq*D/16 / 64) + ceil(Hkv*D/16 / 64) + ceil(Hkv*D/8 / 64) units.
+// (Latency-bound: each unit is a position -> table -> rotate -> store chain;
+// 1-4 loads per lane and 3-6 CTAs per SM all measured within 10 %.)
 // Each lane issues all the loads of its unit before any arithmetic or store.
 // ---------------------------------------------------------------------------
 constexpr int kScatGroups = 2;    // RoPE pair groups per lane
-constexpr int kScatVecs = 4;      // V vectors per lane
+constexpr int kScatVecs = 2;      // V vectors per lane
 
 template <int DT>
-__global__ void __launch_bounds__(256, 3)
+__global__ void __launch_bounds__(256, 4)
 rope_scatter_kernel(const uint16_t* __restrict__ q_src, int64_t q_stride,
                     const uint16_t* __restrict__ k_src, int64_t k_stride,
                     const uint16_t* __restrict__ v_src, int64_t v_stride, int gather,
