@@ -191,7 +191,36 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
         return fuse_full_recompute(layerwise_model, chunks, return_layerwise_output)
     if len(chunks) <= 1:
         return fuse_full_recompute(layerwise_model, chunks, return_layerwise_output)
+    pre = _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check_layer, rope_mode,
+                             status, input_ids, extra_tokens=0)
+    result = pre.logits
+    if return_layerwise_output:
+        result = LayerwiseOutput(logits=pre.logits, past_key_values=pre.dynamic_cache())
+    if return_hkvd_indices:
+        return result, pre.idx
+    return result
 
+
+class _Prefill:
+    """Result of a selective prefill: logits, the fused cache (capacity S + extra
+    rows per layer, the first S filled) and the selection."""
+
+    def __init__(self, logits, fused_k, fused_v, idx, geo, S, rope):
+        self.logits, self.fused_k, self.fused_v, self.idx = logits, fused_k, fused_v, idx
+        self.geo, self.S, self.rope = geo, S, rope
+
+    def dynamic_cache(self):
+        g, S = self.geo, self.S
+        kv = [(self.fused_k[l, :S].view(S, g.n_kv, g.head_dim).permute(1, 0, 2).unsqueeze(0),
+               self.fused_v[l, :S].view(S, g.n_kv, g.head_dim).permute(1, 0, 2).unsqueeze(0))
+              for l in range(self.fused_k.shape[0])]
+        return attach_cache_layers(new_dynamic_cache(), kv)
+
+
+def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check_layer, rope_mode, status,
+                       input_ids, extra_tokens: int = 0) -> _Prefill:
+    """Body of fuse_selective's selective path; the fused cache gets extra_tokens
+    spare rows per layer (room for decode)."""
     lw = layerwise_model
     inner = lw._inner
     n_layers = lw.num_layers
@@ -215,9 +244,10 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
         table = ops.ChunkTable(entries, range(ck, n_layers), device)
         if table.S != S:
             raise ValueError(f"stored chunk lengths sum to {table.S}, chunks say {S}")
-        rope = rope_table_for(lw, S, device)
-        fused_k = torch.empty((n_layers, S, geo.kv_dim), dtype=dtype, device=device)
+        rope = rope_table_for(lw, S + extra_tokens, device)
+        fused_k = torch.empty((n_layers, S + extra_tokens, geo.kv_dim), dtype=dtype, device=device)
         fused_v = torch.empty_like(fused_k)
+        fk, fv = fused_k[:, :S], fused_v[:, :S]     # the blended rows of every layer
 
         # (a)+(b): all cached layers in one launch, overlapped with layers < ck
         side = _side_stream(lw, device)
@@ -254,7 +284,7 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
                 hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None,
                            status=status)
                 a, _ = _attention_block(layer, geo, hn, pos_all, S, rope,
-                                        fused_k[li], fused_v[li], False, status, rope_mode, ws_dense, li > 0,
+                                        fk[li], fv[li], False, status, rope_mode, ws_dense, li > 0,
                                         tag="_dense")
                 m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=a, sum_out=h, status=status))
 
@@ -272,9 +302,9 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
             k_rows = k_pre.index_select(1, idx)
             cur.wait_event(assembled)
             q_rot = ops.rope_scatter(q[0], k_rows[0], v[0], idx, False, S, geo.n_q, geo.n_kv, geo.head_dim,
-                                     rope, fused_k[ck], fused_v[ck], mode=rope_mode, status=status)
+                                     rope, fk[ck], fv[ck], mode=rope_mode, status=status)
             ws_sparse = ops.attn_workspace(k_sel, S, geo.n_q, geo.n_kv, geo.head_dim, device)
-            a = ops.partial_attn(q_rot, fused_k[ck], fused_v[ck], idx, geo.n_q, geo.n_kv, geo.head_dim,
+            a = ops.partial_attn(q_rot, fk[ck], fv[ck], idx, geo.n_q, geo.n_kv, geo.head_dim,
                                  geo.scaling, status=status, workspace=ws_sparse, reuse_plan=False)
             # selected residual rows gathered inside the norm launch
             o = attn.o_proj(a.unsqueeze(0))
@@ -285,7 +315,7 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
                 layer = inner.layers[li]
                 hn = _norm(layer.input_layernorm, hs, delta=m, sum_out=hs, status=status)
                 a, _ = _attention_block(layer, geo, hn, idx, S, rope,
-                                        fused_k[li], fused_v[li], False, status, rope_mode, ws_sparse, True)
+                                        fk[li], fv[li], False, status, rope_mode, ws_sparse, True)
                 m = _mlp(layer, _norm(layer.post_attention_layernorm, hs, delta=a, sum_out=hs, status=status))
 
             logits_sparse = lw.model.lm_head(_norm(inner.norm, hs, delta=m, status=status))   # (1, k, vocab)
@@ -299,12 +329,4 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
         finally:
             cur.wait_event(assembled)
 
-    result = logits
-    if return_layerwise_output:
-        kv = [(fused_k[l].view(S, geo.n_kv, geo.head_dim).permute(1, 0, 2).unsqueeze(0),
-               fused_v[l].view(S, geo.n_kv, geo.head_dim).permute(1, 0, 2).unsqueeze(0))
-              for l in range(n_layers)]
-        result = LayerwiseOutput(logits=logits, past_key_values=attach_cache_layers(new_dynamic_cache(), kv))
-    if return_hkvd_indices:
-        return result, idx
-    return result
+    return _Prefill(logits, fused_k, fused_v, idx, geo, S, rope)
