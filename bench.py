@@ -936,6 +936,56 @@ def run_kv_sharded(args):
         print(json.dumps(res), flush=True)
 
 
+def run_decode(args):
+    """Mistral-7B 7K blend followed by greedy decode over the blended cache
+    (generate_greedy): ms per decoded token after the prefill, device time."""
+    import torch
+    import cacheblend as cb
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    model = build_model(device)
+    lw = cb.LayerwiseModel.from_hf(model)
+    store = cb.KVStore()
+    chunks = build_request(model, cb, seed=0, device=device)
+    for c in chunks:
+        K, V = cb.precompute_chunk_kv(lw, c)
+        store.put(c.chunk_id, K, V)
+    n_new = args.decode_tokens
+    for _ in range(args.warmup):
+        cb.generate_greedy(lw, chunks, store, 2, recompute_ratio=RATIO, check_layer=CHECK_LAYER)
+    torch.cuda.synchronize()
+    res = []
+    for n in (1, n_new):
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            toks = cb.generate_greedy(lw, chunks, store, n, recompute_ratio=RATIO, check_layer=CHECK_LAYER)
+        torch.cuda.synchronize()
+        res.append((time.perf_counter() - t0) * 1e3 / args.steps)
+    per_tok = (res[1] - res[0]) / (n_new - 1)
+    # the reference's decode on the same blended cache: HF forward with past_key_values
+    with torch.inference_mode():
+        out = cb.fuse_selective(lw, chunks, store, recompute_ratio=RATIO, check_layer=CHECK_LAYER,
+                                return_layerwise_output=True)
+        cache, nxt = out.past_key_values, out.logits[0, -1].argmax().view(1, 1)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n_new - 1):
+            step = model(input_ids=nxt, past_key_values=cache, use_cache=True)
+            cache, nxt = step.past_key_values, step.logits[0, -1].argmax().view(1, 1)
+            int(nxt.item())
+        torch.cuda.synchronize()
+        hf_per_tok = (time.perf_counter() - t0) * 1e3 / (n_new - 1)
+    print(json.dumps({
+        "metric": "greedy decode over the blended cache, ms per token (Mistral-7B 7K blend)",
+        "value": round(per_tok, 3), "unit": "ms/token", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": False, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "mistral7b-7k-decode", "S": sum(c.length for c in chunks), "new_tokens": n_new,
+                   "prefill_plus_first_token_ms": round(res[0], 2), "tokens": toks[:8]},
+        "hf_decode_ms_per_token": round(hf_per_tok, 3),
+        "note": "host wall time per call (each token is read back to choose the next, as in the reference)"}),
+        flush=True)
+
+
 def run_attn_layers(args):
     """Partial attention alone at the Mistral-7B sparse-layer shape: S = 6208 keys,
     k = 931 selected rows (uniform random, last position included), 32 q / 8 KV heads,
@@ -994,13 +1044,14 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=30.0)
     ap.add_argument("--workload", default="mistral7b-7k-blend",
                     choices=["mistral7b-7k-blend", "kv-microbench", "attn-layers", "llama70b-128k-sharded",
-                             "llama3-8b-32k-x64"])
+                             "llama3-8b-32k-x64", "mistral7b-7k-decode"])
     ap.add_argument("--attn-layers", type=int, default=31)
     ap.add_argument("--attn-k", type=int, default=931, help="selected rows (6208 = dense causal)")
     ap.add_argument("--attn-dist", default="uniform", choices=["uniform", "tail"])
     ap.add_argument("--sh-layers", type=int, default=80, help="layers of the sharded 128K workload")
     ap.add_argument("--kv-layers", type=int, default=32, help="layers of the KV microbench")
     ap.add_argument("--kv-arena", action="store_true", help="chunk K/V in one KVArena device pool")
+    ap.add_argument("--decode-tokens", type=int, default=32, help="tokens of the decode workload")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1014,6 +1065,8 @@ def main():
         run_kv_sharded(args)
     elif args.workload == "llama3-8b-32k-x64":
         run_llama8b_32k(args)
+    elif args.workload == "mistral7b-7k-decode":
+        run_decode(args)
     else:
         run_ours(args)
 
