@@ -248,6 +248,11 @@ def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check
         fused_k = torch.empty((n_layers, S + extra_tokens, geo.kv_dim), dtype=dtype, device=device)
         fused_v = torch.empty_like(fused_k)
         fk, fv = fused_k[:, :S], fused_v[:, :S]     # the blended rows of every layer
+        if extra_tokens:
+            # spare rows hold zeros until decode writes them: attention over the whole
+            # capacity multiplies P = 0 by them, and 0 * (uninitialised NaN) would not be 0
+            fused_k[:, S:].zero_()
+            fused_v[:, S:].zero_()
 
         # (a)+(b): all cached layers in one launch, overlapped with layers < ck
         side = _side_stream(lw, device)

@@ -19,34 +19,67 @@ from cacheblend.fusor import _mlp, _norm, _selective_prefill, fuse_selective
 from cacheblend.kv_store import KVStore
 
 
-def _decode_step(lw, pre, token: torch.Tensor, p: int, status):
-    """Logits (vocab,) of one token at position p; its K/V land in cache row p."""
+class _DecodeState:
+    """Static device buffers of a decode: the current token and position, the
+    attention workspace, and the chosen tokens / logits rows by step."""
+
+    def __init__(self, lw, pre, n_new: int, first_row: torch.Tensor, keep_rows: bool):
+        device, geo = lw.device, pre.geo
+        cap = pre.fused_k.shape[1]
+        self.tokens = torch.zeros((n_new,), dtype=torch.int64, device=device)
+        self.rows = torch.zeros((n_new, first_row.shape[-1]), dtype=first_row.dtype, device=device) if keep_rows else None
+        first = first_row.argmax().view(1)
+        self.tokens[0:1].copy_(first)
+        if keep_rows:
+            self.rows[0].copy_(first_row)
+        self.token = first.view(1, 1).clone()
+        self.pos = torch.full((1,), pre.S, dtype=torch.int64, device=device)
+        self.base = pre.S - 1               # token t of the output was chosen at position base + t
+        self.ws = ops.attn_workspace(1, cap, geo.n_q, geo.n_kv, geo.head_dim, device)
+
+
+def _decode_step(lw, pre, st: _DecodeState, status):
+    """One token at position st.pos: its K/V into cache row pos, the next token
+    into st.token / st.tokens, pos advanced -- all on the device, no host sync
+    (so the step can be captured in a CUDA graph)."""
     inner, geo = lw._inner, pre.geo
-    device = lw.device
-    pos = torch.full((1,), p, dtype=torch.int64, device=device)
     cap = pre.fused_k.shape[1]
-    h = inner.embed_tokens(token.view(1, 1))
+    h = inner.embed_tokens(st.token)
     m = None
     for li, layer in enumerate(inner.layers):
         attn = layer.self_attn
         hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None, status=status)
         q, k, v = attn.q_proj(hn), attn.k_proj(hn), attn.v_proj(hn)
-        q_rot = ops.rope_scatter(q[0], k[0], v[0], pos, False, cap, geo.n_q, geo.n_kv, geo.head_dim, pre.rope,
+        q_rot = ops.rope_scatter(q[0], k[0], v[0], st.pos, False, cap, geo.n_q, geo.n_kv, geo.head_dim, pre.rope,
                                  pre.fused_k[li], pre.fused_v[li], status=status)
-        a = ops.partial_attn(q_rot, pre.fused_k[li, :p + 1], pre.fused_v[li, :p + 1], pos, geo.n_q, geo.n_kv,
-                             geo.head_dim, geo.scaling, status=status)
+        # the whole capacity with the position as the causal bound: rows past pos are
+        # invisible (and zero), so the call does not change from step to step
+        a = ops.partial_attn(q_rot, pre.fused_k[li], pre.fused_v[li], st.pos, geo.n_q, geo.n_kv, geo.head_dim,
+                             geo.scaling, status=status, workspace=st.ws)
         o = attn.o_proj(a.unsqueeze(0))
         m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=o, sum_out=h, status=status))
-    return lw.model.lm_head(_norm(inner.norm, h, delta=m, status=status))[0, -1]
+    row = lw.model.lm_head(_norm(inner.norm, h, delta=m, status=status))[0, -1]
+    nxt = row.argmax().view(1)
+    slot = st.pos - st.base
+    st.tokens.index_copy_(0, slot, nxt)
+    if st.rows is not None:
+        st.rows.index_copy_(0, slot, row.view(1, -1))
+    st.token.copy_(nxt.view(1, 1))
+    st.pos.add_(1)
 
 
 def generate_greedy(layerwise_model, chunks: list[Chunk], kv_store: KVStore, max_new_tokens: int,
                     recompute_ratio: float = 0.15, check_layer: int = 1, eos_token_id: int | None = None,
-                    rope_mode: str = "ref", status: torch.Tensor | None = None, return_logits: bool = False):
+                    rope_mode: str = "ref", status: torch.Tensor | None = None, return_logits: bool = False,
+                    use_graph: bool = True):
     """CacheBlend selective prefill, then greedy decode over the blended cache.
 
     Returns the generated token ids (token 1 from the prefill's last row), and
-    with ``return_logits`` the logits row that chose each of them.  The
+    with ``return_logits`` the logits row that chose each of them.  Decode
+    steps run back to back on the device (one CUDA graph of a step, replayed,
+    unless ``use_graph`` is False); the tokens are read once at the end and cut
+    after the first ``eos_token_id``, so a run that meets EOS early decodes the
+    remaining steps for nothing but returns what the reference returns.  The
     shortcut cases of fuse_selective (ratio 0, ratio >= 1, one chunk) run the
     reference path: HF prefill and HF decode with ``past_key_values``."""
     if max_new_tokens <= 0:
@@ -70,12 +103,29 @@ def generate_greedy(layerwise_model, chunks: list[Chunk], kv_store: KVStore, max
         else:
             pre = _selective_prefill(lw, chunks, kv_store, recompute_ratio, check_layer, rope_mode, status,
                                      None, extra_tokens=max_new_tokens)
-            row = pre.logits[0, -1]
-            for i in range(max_new_tokens):
-                nxt = row.argmax()
-                tokens.append(int(nxt.item()))
-                rows.append(row)
-                if (eos_token_id is not None and tokens[-1] == eos_token_id) or i + 1 == max_new_tokens:
-                    break
-                row = _decode_step(lw, pre, nxt, pre.S + i, status)
+            st = _DecodeState(lw, pre, max_new_tokens, pre.logits[0, -1], return_logits)
+            n_steps = max_new_tokens - 1
+            if n_steps >= 1:
+                _decode_step(lw, pre, st, status)          # eager: first use sets up every kernel
+            if n_steps >= 2:
+                if use_graph:
+                    cur = torch.cuda.current_stream(lw.device)
+                    side = torch.cuda.Stream(device=lw.device)
+                    side.wait_stream(cur)
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.stream(side):
+                        with torch.cuda.graph(graph, stream=side):
+                            _decode_step(lw, pre, st, status)
+                    cur.wait_stream(side)
+                    # capture recorded the step without running it
+                    for _ in range(n_steps - 1):
+                        graph.replay()
+                    del graph
+                else:
+                    for _ in range(n_steps - 1):
+                        _decode_step(lw, pre, st, status)
+            tokens = st.tokens.tolist()
+            if eos_token_id is not None and eos_token_id in tokens:
+                tokens = tokens[:tokens.index(eos_token_id) + 1]
+            rows = list(st.rows[:len(tokens)]) if return_logits else []
     return (tokens, rows) if return_logits else tokens

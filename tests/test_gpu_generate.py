@@ -55,3 +55,14 @@ def test_decode_shortcut_path_and_eos():
     stopped = cb.generate_greedy(lw, chunks, store, 5, eos_token_id=first[0])
     assert stopped == first                                                    # eos right away
     assert cb.generate_greedy(lw, chunks, store, 0) == []
+
+
+def test_decode_graph_replay_equals_eager():
+    """The decode step captured once and replayed gives the eager loop's tokens
+    and logits bit for bit (same kernels, same buffers)."""
+    cb, lw, model, chunks, store = _setup()
+    t1, r1 = cb.generate_greedy(lw, chunks, store, 7, return_logits=True, use_graph=True)
+    t2, r2 = cb.generate_greedy(lw, chunks, store, 7, return_logits=True, use_graph=False)
+    assert t1 == t2
+    for a, b in zip(r1, r2):
+        assert torch.equal(a, b)
