@@ -20,11 +20,12 @@ from cacheblend.precompute import precompute_chunk_kv, precompute_chunk_kv_into,
 from cacheblend.fusor import fuse_full_recompute, fuse_full_reuse, fuse_selective, fuse_prefix_cache
 from cacheblend.hkvd import kv_deviation, select_top_k
 from cacheblend.generate import generate_greedy
+from cacheblend.graph import BlendGraph
 
 __all__ = [
     "Tolerance", "ToleranceResult", "assert_logits_close", "LayerwiseModel", "LayerwiseOutput",
     "KVStore", "KVArena", "Chunk", "chunk_texts", "fused_input_ids", "chunk_offsets", "apply_rope_shift",
     "precompute_chunk_kv", "precompute_chunk_kv_into", "precompute_from_cache_prompt", "fuse_full_recompute",
     "fuse_full_reuse", "fuse_selective", "fuse_prefix_cache", "kv_deviation", "select_top_k",
-    "generate_greedy",
+    "generate_greedy", "BlendGraph",
 ]

@@ -218,9 +218,10 @@ class _Prefill:
 
 
 def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check_layer, rope_mode, status,
-                       input_ids, extra_tokens: int = 0) -> _Prefill:
+                       input_ids, extra_tokens: int = 0, table=None) -> _Prefill:
     """Body of fuse_selective's selective path; the fused cache gets extra_tokens
-    spare rows per layer (room for decode)."""
+    spare rows per layer (room for decode).  ``table``: a prebuilt chunk table
+    of layers check_layer.. (a captured graph keeps one and refreshes it)."""
     lw = layerwise_model
     inner = lw._inner
     n_layers = lw.num_layers
@@ -241,7 +242,8 @@ def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check
     cur = torch.cuda.current_stream(device)
 
     with torch.inference_mode():
-        table = ops.ChunkTable(entries, range(ck, n_layers), device)
+        if table is None:
+            table = ops.ChunkTable(entries, range(ck, n_layers), device)
         if table.S != S:
             raise ValueError(f"stored chunk lengths sum to {table.S}, chunks say {S}")
         rope = rope_table_for(lw, S + extra_tokens, device)

@@ -164,6 +164,15 @@ class ChunkTable:
         self.starts = hs.to(device, non_blocking=True)
         self.dtype = dtype
 
+    def refresh(self, entries: Sequence[dict]) -> None:
+        """Point the same device table at other chunks of the same lengths
+        (a captured graph reads it in place); ordered on the current stream."""
+        new = ChunkTable(entries, self.layers, self.srcs.device)
+        if new.lengths != self.lengths or new.kv_dim != self.kv_dim or new.dtype != self.dtype:
+            raise ValueError("ChunkTable.refresh: chunk lengths / width / dtype differ from the table's")
+        self.srcs.copy_(new.srcs, non_blocking=True)
+        self._keep = new._keep
+
     def layer_ptr(self, layer: int) -> int:
         """Device address of the srcs row of one layer (n_chunks entries)."""
         li = self.layers.index(layer)
