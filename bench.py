@@ -552,10 +552,12 @@ def run_kv_microbench(args):
     fk = torch.empty((L, S, kv), dtype=torch.bfloat16, device=device)
     fv = torch.empty_like(fk)
     k = ops.topk_count(S, 0.10)
-    q_fresh = torch.randn((k, Hq * D), generator=g, device=device).to(torch.bfloat16)
-    k_fresh = torch.randn((k, kv), generator=g, device=device).to(torch.bfloat16)
-    v_fresh = torch.randn((k, kv), generator=g, device=device).to(torch.bfloat16)
-    q_out = torch.empty((k, Hq * D), dtype=torch.bfloat16, device=device)
+    # fresh Q/K/V rows and the rotated Q per layer, as a model's projections give
+    # them (one set for all layers would be read from L2 after the first)
+    q_fresh = torch.randn((L, k, Hq * D), generator=g, device=device).to(torch.bfloat16)
+    k_fresh = torch.randn((L, k, kv), generator=g, device=device).to(torch.bfloat16)
+    v_fresh = torch.randn((L, k, kv), generator=g, device=device).to(torch.bfloat16)
+    q_out = torch.empty((L, k, Hq * D), dtype=torch.bfloat16, device=device)
     rope_seq = ops.rope_table(invf, S)
 
     def step(i):
@@ -565,13 +567,32 @@ def run_kv_microbench(args):
             # latency-bound top-K select are timed apart
             dev = ops.kv_deviation_rows(k_new[l], table, l)
             idx = ops.topk_select(dev, k, force_last=True)
-            ops.rope_scatter(q_fresh, k_fresh, v_fresh, idx, False, S, Hq, Hkv, D, rope_seq, fk[l], fv[l],
-                             q_out=q_out)
+            ops.rope_scatter(q_fresh[l], k_fresh[l], v_fresh[l], idx, False, S, Hq, Hkv, D, rope_seq, fk[l],
+                             fv[l], q_out=q_out[l])
 
     ms, kern, clk = _timed(step, args.steps, args.warmup, device)
-    # Per-kernel rates: each kernel's L launches of one step back to back between
-    # one CUDA-event pair (a pair around every short launch would add its own
-    # record and launch latency to the kernel's time).
+    eager_ms = ms
+    graph_note = None
+    if not args.no_cuda_graph:
+        # the same step captured once as a CUDA graph and replayed: 1 + 3L launches
+        # with no Python between them (what BlendGraph does for a request)
+        side = torch.cuda.Stream(device=device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            step(0)
+            side.synchronize()
+            with torch.cuda.graph(step_graph, stream=side):
+                step(0)
+        torch.cuda.current_stream(device).wait_stream(side)
+        ms, _, clk = _timed(lambda i: step_graph.replay(), args.steps, args.warmup, device)
+        del step_graph
+        graph_note = "step captured once as a CUDA graph and replayed (eager launches from Python: eager_ms_per_step)"
+    # Per-kernel rates: each kernel's L launches of one step captured once in a
+    # CUDA graph and replayed between one CUDA-event pair, so the time is the
+    # kernels' own (launched one by one from Python, a 20-30 us launch would
+    # leave the device idle between these short kernels; a pair of events
+    # around every launch would add its own latency).
     idx_l = [ops.topk_select(ops.kv_deviation_rows(k_new[l], table, l), k, force_last=True) for l in range(L)]
     devs = [ops.kv_deviation_rows(k_new[l], table, l) for l in range(L)]
     torch.cuda.synchronize()
@@ -579,13 +600,24 @@ def run_kv_microbench(args):
 
     def batch_ms(fn, reps):
         fn()
+        side = torch.cuda.Stream(device=device)
+        side.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            fn()
+            side.synchronize()
+            with torch.cuda.graph(graph, stream=side):
+                fn()
+        stream.wait_stream(side)
+        graph.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(reps):
-            fn()
+            graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
+        del graph
         return e0.elapsed_time(e1) / reps
 
     per_kernel = {
@@ -595,8 +627,8 @@ def run_kv_microbench(args):
                                  args.steps),
         "topk_select": batch_ms(lambda: [ops.topk_select(devs[l], k, force_last=True) for l in range(L)],
                                 args.steps),
-        "rope_scatter": batch_ms(lambda: [ops.rope_scatter(q_fresh, k_fresh, v_fresh, idx_l[l], False, S, Hq,
-                                                           Hkv, D, rope_seq, fk[l], fv[l], q_out=q_out)
+        "rope_scatter": batch_ms(lambda: [ops.rope_scatter(q_fresh[l], k_fresh[l], v_fresh[l], idx_l[l], False,
+                                                           S, Hq, Hkv, D, rope_seq, fk[l], fv[l], q_out=q_out[l])
                                           for l in range(L)], args.steps),
     }
     hbm, _, _, src = load_peaks()
@@ -619,10 +651,11 @@ def run_kv_microbench(args):
         "metric": "KV-kernel HBM GB/s (assemble + HKVD + scatter, microbench [32,8,32768,128])",
         "value": round(total_b / (ms / args.steps * 1e-3) / 1e9, 1), "unit": "GB/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+        "eager_ms_per_step": round(eager_ms / args.steps, 3), "launch": graph_note or "eager",
         "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "kv-microbench", "layers": L, "kv_heads": Hkv, "tokens": S, "head_dim": D,
                    "chunks": f"{n_chunks}x{CL}", "topk": k,
-                   "l2": f"inputs larger than L2 ({4 * L * S * kv / 1e9:.1f} GB chunk K/V, fresh K and fused K/V per step)"},
+                   "l2": f"inputs larger than L2 ({4 * L * S * kv / 1e9:.1f} GB chunk K/V; recomputed K, fresh Q/K/V rows and fused K/V per layer)"},
         "kernels": out, "hbm_peak_gbs": hbm, "hbm_peak_kind": src, "clocks": clk}), flush=True)
 
 

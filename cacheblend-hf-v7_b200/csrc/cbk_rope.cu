@@ -1,6 +1,7 @@
 // RoPE table, chunk-KV assembly (concat + RoPE shift), row RoPE and the
 // per-layer fresh-row RoPE + scatter.  All of these are HBM-bound byte movers:
-// 128-bit loads/stores, one pass over the data, rotation in fp32 registers.
+// 128-bit loads/stores, one pass over the data, rotation in registers (packed
+// 16-bit ops for the torch-rounded mode, fp32 for the fp32 mode).
 #include "cbk_common.cuh"
 
 namespace cbk {
@@ -29,42 +30,106 @@ __global__ void rope_table_kernel(const float* __restrict__ inv_freq, int half_d
 // (rotate_half layout: element j pairs with j + D/2, both use frequency j).
 // CBK_ROPE_REF reproduces the 16-bit torch op sequence of apply_rotary_pos_emb:
 // cos/sin rounded to the element type, each product rounded, the sum rounded.
+// It runs on packed 16-bit pairs (mul/add/sub.rn.{bf16x2,f16x2}): torch rounds
+// the fp32 result of each op, and for 16-bit operands that fp32 result is the
+// exact one wherever the rounding can tell (a product of two 8- or 11-bit
+// significands fits fp32's 24; a sum whose operands' exponents differ by more
+// than 24 - 8 bits lands within half an ulp of the larger operand either way),
+// so one correctly rounded 16-bit op gives the same bits as torch's two steps.
 // ---------------------------------------------------------------------------
+template <int DT> struct Pk;
+template <> struct Pk<CBK_BF16> {
+  // lo -> bits 0-15, hi -> bits 16-31
+  static __device__ __forceinline__ uint32_t cvt(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+};
+template <> struct Pk<CBK_F16> {
+  static __device__ __forceinline__ uint32_t cvt(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+};
+
+// c4: the table entries (cos, sin) of 8 consecutive frequencies, as 4 float4
 template <int DT>
-__device__ __forceinline__ void rope8(const uint4& lo, const uint4& hi, const float2* cs,
-                                      int mode, uint4& olo, uint4& ohi) {
+__device__ __forceinline__ void rope8t(const uint4& lo, const uint4& hi, const float4 (&c4)[4],
+                                       int mode, uint4& olo, uint4& ohi) {
+  float2 t[8];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    t[2 * q] = make_float2(c4[q].x, c4[q].y);
+    t[2 * q + 1] = make_float2(c4[q].z, c4[q].w);
+  }
+  if (mode == CBK_ROPE_REF) {
+    const uint32_t* al = reinterpret_cast<const uint32_t*>(&lo);
+    const uint32_t* bh = reinterpret_cast<const uint32_t*>(&hi);
+    uint32_t* yl = reinterpret_cast<uint32_t*>(&olo);
+    uint32_t* yh = reinterpret_cast<uint32_t*>(&ohi);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t c = Pk<DT>::cvt(t[2 * w].x, t[2 * w + 1].x);
+      const uint32_t s = Pk<DT>::cvt(t[2 * w].y, t[2 * w + 1].y);
+      yl[w] = Pk<DT>::sub(Pk<DT>::mul(al[w], c), Pk<DT>::mul(bh[w], s));
+      yh[w] = Pk<DT>::add(Pk<DT>::mul(bh[w], c), Pk<DT>::mul(al[w], s));
+    }
+    return;
+  }
   const uint16_t* xl = reinterpret_cast<const uint16_t*>(&lo);
   const uint16_t* xh = reinterpret_cast<const uint16_t*>(&hi);
   uint16_t* yl = reinterpret_cast<uint16_t*>(&olo);
   uint16_t* yh = reinterpret_cast<uint16_t*>(&ohi);
-  // table entries for 8 consecutive frequencies: 4 x 16-byte loads
-  float2 t[8];
-  const float4* c4 = reinterpret_cast<const float4*>(cs);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float4 v = c4[q];
-    t[2 * q] = make_float2(v.x, v.y);
-    t[2 * q + 1] = make_float2(v.z, v.w);
-  }
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const float a = Elem<DT>::to_f(xl[e]);
     const float b = Elem<DT>::to_f(xh[e]);
-    float c = t[e].x, s = t[e].y;
-    if (mode == CBK_ROPE_REF) {
-      c = round16<DT>(c);
-      s = round16<DT>(s);
-      const float ac = round16<DT>(__fmul_rn(a, c));
-      const float bs = round16<DT>(__fmul_rn(b, s));
-      const float bc = round16<DT>(__fmul_rn(b, c));
-      const float as = round16<DT>(__fmul_rn(a, s));
-      yl[e] = Elem<DT>::from_f(__fadd_rn(ac, -bs));
-      yh[e] = Elem<DT>::from_f(__fadd_rn(bc, as));
-    } else {
+    const float c = t[e].x, s = t[e].y;
+    {
       yl[e] = Elem<DT>::from_f(__fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)));
       yh[e] = Elem<DT>::from_f(__fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s)));
     }
   }
+}
+
+template <int DT>
+__device__ __forceinline__ void rope8(const uint4& lo, const uint4& hi, const float2* cs,
+                                      int mode, uint4& olo, uint4& ohi) {
+  const float4* p = reinterpret_cast<const float4*>(cs);
+  const float4 c4[4] = {p[0], p[1], p[2], p[3]};
+  rope8t<DT>(lo, hi, c4, mode, olo, ohi);
 }
 
 // Rotate one 8-pair group (head h, pair group g) of a row and store it.
@@ -201,18 +266,41 @@ rope_rows_kernel(const uint16_t* in, uint16_t* out, int64_t n_rows, int n_heads,
 
 // ---------------------------------------------------------------------------
 // Fresh rows of one layer: RoPE(Q) -> q_out, RoPE(K) and V scattered into the
-// fused cache at the selected positions.  Work unit = one warp: 64 RoPE pair
-// groups of Q or of K (2 per lane), or 64 V vectors (2 per lane); a selected
-// row has ceil(Hq*D/16 / 64) + ceil(Hkv*D/16 / 64) + ceil(Hkv*D/8 / 64) units.
-// (Latency-bound: each unit is a position -> table -> rotate -> store chain;
-// 1-4 loads per lane and 3-6 CTAs per SM all measured within 10 %.)
-// Each lane issues all the loads of its unit before any arithmetic or store.
+// fused cache at the selected positions.  Q, K and V rows are all read and
+// written as 8-element (lo, hi) pair groups -- elements [8f, 8f+8) and
+// [8f+D/2, 8f+D/2+8) of a head, f < D/16 -- rotated for Q and K, copied for V.
+// A unit is 64 groups (2 KB, two groups per lane); a selected row has
+// ceil(Hq*D/16 / 64) Q units, then ceil(Hkv*D/16 / 64) K units and as many V
+// units.  A warp pass takes kScatUnits consecutive units of one row and issues
+// every load of the pass -- the row's position, its source vectors, the
+// cos/sin slice -- before the first rotation or store.  When D/16 divides 32,
+// lane L always holds pair group L mod D/16 of some head: its element offset
+// is the unit's first group * 16 + a per-lane constant, and one 8-entry
+// cos/sin slice per lane serves every unit of the pass.
 // ---------------------------------------------------------------------------
-constexpr int kScatGroups = 2;    // RoPE pair groups per lane
-constexpr int kScatVecs = 2;      // V vectors per lane
+// Units per pass and CTAs per SM, measured at [32 layers, 3277 of 32768 rows,
+// 32 Q / 8 KV heads, D = 128] with every source row read from HBM: 1 unit at
+// 4 CTAs/SM (64 registers) 16.4 us per launch; 2 at 3 CTAs 17.4; 3 at 2 CTAs
+// 17.0; 2 at 4 CTAs spills and takes 23 us.
+constexpr int kScatGroups = 2;    // pair groups per lane per unit
+#ifndef CBK_SCAT_UNITS
+#define CBK_SCAT_UNITS 1
+#endif
+#ifndef CBK_SCAT_MINB
+#define CBK_SCAT_MINB 4
+#endif
+constexpr int kScatUnits = CBK_SCAT_UNITS;
 
-template <int DT>
-__global__ void __launch_bounds__(256, 4)
+__device__ __forceinline__ void ld_cs(const float2* cs, float4 (&c4)[4]) {
+  const float4* p = reinterpret_cast<const float4*>(cs);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) c4[q] = p[q];
+}
+
+// GPR: pair groups per head (head_dim / 16) when fixed at compile time, else 0;
+// MODE: the RoPE mode (a template parameter, so each instance holds one path)
+template <int DT, int GPR, int MODE>
+__global__ void __launch_bounds__(256, CBK_SCAT_MINB)
 rope_scatter_kernel(const uint16_t* __restrict__ q_src, int64_t q_stride,
                     const uint16_t* __restrict__ k_src, int64_t k_stride,
                     const uint16_t* __restrict__ v_src, int64_t v_stride, int gather,
@@ -221,87 +309,91 @@ rope_scatter_kernel(const uint16_t* __restrict__ q_src, int64_t q_stride,
                     int64_t table_rows, int mode, uint16_t* __restrict__ q_out,
                     uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache,
                     int32_t* status) {
+  constexpr int U = kScatUnits;
+  constexpr int kUnitGroups = 32 * kScatGroups;
   const int lane = threadIdx.x & 31;
+  if (GPR) head_dim = GPR * 16;
   const int gpr = head_dim >> 4;
   const int half = head_dim >> 1;
   const int qg = n_q_heads * gpr;
   const int kg = n_kv_heads * gpr;
   const int kv_dim = n_kv_heads * head_dim;
-  const int vv = kv_dim >> 3;
-  const int nq = (qg + 32 * kScatGroups - 1) / (32 * kScatGroups);
-  const int nk = (kg + 32 * kScatGroups - 1) / (32 * kScatGroups);
-  const int nv = (vv + 32 * kScatVecs - 1) / (32 * kScatVecs);
-  const int per = nq + nk + nv;
-  const int64_t n_units = n_sel * per;
+  const int64_t q_dim = static_cast<int64_t>(n_q_heads) * head_dim;
+  const int nq = (qg + kUnitGroups - 1) / kUnitGroups;
+  const int nk = (kg + kUnitGroups - 1) / kUnitGroups;
+  const int per = nq + 2 * nk;
+  const int passes = (per + U - 1) / U;         // warp passes per row
+  const bool shared_f = (32 % gpr) == 0;
+  const int lane_off = (lane / gpr) * head_dim + (lane % gpr) * 8;
+  // element offset (lo half) of group `first + 32 q + lane`
+  auto offset = [&](int first, int q) -> int {
+    if (shared_f) return (first + 32 * q) * 16 + lane_off;
+    const int g = first + 32 * q + lane;
+    return (g / gpr) * head_dim + (g % gpr) * 8;
+  };
+  const int64_t n_items = n_sel * passes;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t u = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n_units;
-       u += warps) {
-    const int64_t j = u / per;
-    const int part = static_cast<int>(u - j * per);
-    const int64_t p = idx[j];
-    const bool bad = p < 0 || p >= S || p >= table_rows;
-    // Without a gather the source row is j: its loads are issued before the
-    // position arrives (they do not depend on it); with a gather they wait.
-    if (part < nq + nk) {
-      const bool is_q = part < nq;
-      const int ng = is_q ? qg : kg;
-      const int g0 = (is_q ? part : part - nq) * 32 * kScatGroups;
-      const uint16_t* base = is_q ? q_src : k_src;
-      const int64_t stride = is_q ? q_stride : k_stride;
-      uint4 xl[kScatGroups], xh[kScatGroups];
-      auto load = [&](int64_t r) {
-        const uint16_t* src = base + r * stride;
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       w < n_items; w += warps) {
+    const int64_t j = w / passes;
+    const int part0 = static_cast<int>(w - j * passes) * U;
+    int kind[U], first[U];   // kind: 0 Q, 1 K, 2 V, -1 past the row's end
+    bool rope = false;
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const int part = part0 + k;
+      kind[k] = part >= per ? -1 : part < nq ? 0 : (part < nq + nk ? 1 : 2);
+      first[k] = (part - (kind[k] == 0 ? 0 : kind[k] == 1 ? nq : nq + nk)) * kUnitGroups;
+      rope |= kind[k] == 0 || kind[k] == 1;
+    }
+    uint4 x[U][2 * kScatGroups];
+    auto load = [&](int64_t r) {
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        if (kind[k] < 0) continue;
+        const uint16_t* src = kind[k] == 0 ? q_src + r * q_stride
+                            : kind[k] == 1 ? k_src + r * k_stride : v_src + r * v_stride;
+        const int ng = kind[k] == 0 ? qg : kg;
 #pragma unroll
         for (int q = 0; q < kScatGroups; ++q) {
-          const int g = g0 + q * 32 + lane;
-          if (g < ng) {
-            const int off = (g / gpr) * head_dim + (g % gpr) * 8;
-            xl[q] = ld_vec(src + off);
-            xh[q] = ld_vec(src + off + half);
+          if (first[k] + 32 * q + lane < ng) {
+            const int o = offset(first[k], q);
+            x[k][2 * q] = ld_vec(src + o);
+            x[k][2 * q + 1] = ld_vec(src + o + half);
           }
         }
-      };
-      if (!gather) load(j);
-      if (bad) {
-        if (lane == 0) report(status, CBK_STATUS_BAD_INDEX);
-        continue;
       }
-      if (gather) load(p);
-      uint16_t* dst = is_q ? q_out + j * static_cast<int64_t>(n_q_heads * head_dim) : k_cache + p * kv_dim;
-      const float2* cs = table + p * half;
+    };
+    const int64_t p = idx[j];
+    // without a gather the source row is j: its loads go out before the position arrives
+    if (!gather) load(j);
+    if (p < 0 || p >= S || p >= table_rows) {
+      if (lane == 0) report(status, CBK_STATUS_BAD_INDEX);
+      continue;
+    }
+    if (gather) load(p);
+    const float2* cs = table + p * half;
+    float4 c4[4];
+    if (rope && shared_f) ld_cs(cs + (lane % gpr) * 8, c4);
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      if (kind[k] < 0) continue;
+      uint16_t* dst = kind[k] == 0 ? q_out + j * q_dim : (kind[k] == 1 ? k_cache : v_cache) + p * kv_dim;
+      const int ng = kind[k] == 0 ? qg : kg;
 #pragma unroll
       for (int q = 0; q < kScatGroups; ++q) {
-        const int g = g0 + q * 32 + lane;
+        const int g = first[k] + 32 * q + lane;
         if (g < ng) {
-          const int off = (g / gpr) * head_dim + (g % gpr) * 8;
-          uint4 ol, oh;
-          rope8<DT>(xl[q], xh[q], cs + (g % gpr) * 8, mode, ol, oh);
-          st_vec(dst + off, ol);
-          st_vec(dst + off + half, oh);
+          const int o = offset(first[k], q);
+          uint4 lo = x[k][2 * q], hi = x[k][2 * q + 1];
+          if (kind[k] != 2) {
+            if (!shared_f) ld_cs(cs + (g % gpr) * 8, c4);
+            const uint4 a = lo, b = hi;
+            rope8t<DT>(a, b, c4, MODE, lo, hi);
+          }
+          st_vec(dst + o, lo);
+          st_vec(dst + o + half, hi);
         }
-      }
-    } else {
-      const int v0 = (part - nq - nk) * 32 * kScatVecs;
-      uint4 x[kScatVecs];
-      auto load = [&](int64_t r) {
-        const uint16_t* src = v_src + r * v_stride;
-#pragma unroll
-        for (int q = 0; q < kScatVecs; ++q) {
-          const int v = v0 + q * 32 + lane;
-          if (v < vv) x[q] = ld_vec(src + v * 8);
-        }
-      };
-      if (!gather) load(j);
-      if (bad) {
-        if (lane == 0) report(status, CBK_STATUS_BAD_INDEX);
-        continue;
-      }
-      if (gather) load(p);
-      uint16_t* dst = v_cache + p * kv_dim;
-#pragma unroll
-      for (int q = 0; q < kScatVecs; ++q) {
-        const int v = v0 + q * 32 + lane;
-        if (v < vv) st_vec(dst + v * 8, x[q]);
       }
     }
   }
@@ -426,19 +518,29 @@ extern "C" int cbk_rope_scatter(const void* q_src, int64_t q_row_stride, const v
   if (n_sel == 0) return CBK_OK;
   const int gpr = head_dim >> 4;
   const int64_t per = (n_q_heads * gpr + 32 * kScatGroups - 1) / (32 * kScatGroups) +
-                      (n_kv_heads * gpr + 32 * kScatGroups - 1) / (32 * kScatGroups) +
-                      (n_kv_heads * head_dim / 8 + 32 * kScatVecs - 1) / (32 * kScatVecs);
-  const int64_t warp_units = n_sel * per;            // 8 warps per 256-thread block
+                      2 * ((n_kv_heads * gpr + 32 * kScatGroups - 1) / (32 * kScatGroups));
+  const int64_t warp_items = n_sel * ((per + kScatUnits - 1) / kScatUnits);   // 8 warps per block
   auto st = static_cast<cudaStream_t>(stream);
   auto tab = static_cast<const float2*>(rope_table);
-#define CBK_LAUNCH_SCATTER(DT)                                                                  \
-  rope_scatter_kernel<DT><<<grid_for(warp_units * 32, 256, 148 * 64), 256, 0, st>>>(             \
+#define CBK_LAUNCH_SCATTER(DT, GPR, MODE)                                                       \
+  rope_scatter_kernel<DT, GPR, MODE><<<grid_for(warp_items * 32, 256, 148 * 64), 256, 0, st>>>(   \
       static_cast<const uint16_t*>(q_src), q_row_stride, static_cast<const uint16_t*>(k_src),   \
       k_row_stride, static_cast<const uint16_t*>(v_src), v_row_stride, gather, idx, n_sel, S,   \
       n_q_heads, n_kv_heads, head_dim, tab, table_rows, rope_mode,                              \
       static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_cache),                          \
       static_cast<uint16_t*>(v_cache), status)
-  if (dtype == CBK_BF16) CBK_LAUNCH_SCATTER(CBK_BF16); else CBK_LAUNCH_SCATTER(CBK_F16);
+#define CBK_LAUNCH_SCATTER_M(DT, GPR)                                                           \
+  if (rope_mode == CBK_ROPE_REF) CBK_LAUNCH_SCATTER(DT, GPR, CBK_ROPE_REF);                     \
+  else CBK_LAUNCH_SCATTER(DT, GPR, CBK_ROPE_FP32)
+#define CBK_LAUNCH_SCATTER_DT(GPR)                                                              \
+  if (dtype == CBK_BF16) { CBK_LAUNCH_SCATTER_M(CBK_BF16, GPR); } else { CBK_LAUNCH_SCATTER_M(CBK_F16, GPR); }
+  if (head_dim == 128) {
+    CBK_LAUNCH_SCATTER_DT(8);
+  } else {
+    CBK_LAUNCH_SCATTER_DT(0);
+  }
+#undef CBK_LAUNCH_SCATTER_DT
+#undef CBK_LAUNCH_SCATTER_M
 #undef CBK_LAUNCH_SCATTER
   return check_launch("rope_scatter_kernel");
 }

@@ -147,9 +147,18 @@ def test_assemble_reports_bad_positions(ops):
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("gather", [True, False])
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-def test_rope_scatter(ops, gather, dtype):
+@pytest.mark.parametrize("nq,nkv,D,mode", [
+    (8, 2, 128, "ref"),      # head_dim 128: the compile-time instance
+    (8, 2, 128, "fp32"),
+    (3, 1, 128, "ref"),      # Q and K units only partly filled
+    (4, 2, 64, "ref"),       # generic instance, D/16 divides 32 (one cos/sin slice per lane)
+    (6, 3, 96, "ref"),       # D/16 = 6 does not divide 32: a cos/sin slice per pair group
+    (6, 3, 96, "fp32"),
+    (2, 1, 256, "ref"),
+])
+def test_rope_scatter(ops, gather, dtype, nq, nkv, D, mode):
     g = torch.Generator().manual_seed(5)
-    S, nq, nkv, D = 700, 8, 2, 128
+    S = 700
     idx = torch.sort(torch.randperm(S, generator=g)[:105]).values
     n_src = S if gather else idx.numel()
     q = rand16((n_src, nq * D), dtype, g, 2.0).to(DEV)
@@ -161,14 +170,14 @@ def test_rope_scatter(ops, gather, dtype):
     invf = invf_for(1e6, D)
     rope = ops.rope_table(invf.to(DEV), S)
     st = status_word()
-    qo = ops.rope_scatter(q, k, v, idx.to(DEV), gather, S, nq, nkv, D, rope, kc, vc, status=st)
+    qo = ops.rope_scatter(q, k, v, idx.to(DEV), gather, S, nq, nkv, D, rope, kc, vc, mode=mode, status=st)
     assert_status_clean(st)
     tab = rope.cpu().numpy()
     rows = idx.numpy() if gather else np.arange(idx.numel())
     pos = idx.numpy()
-    exp_q = hp.apply_rope(to_bits(q)[rows], pos, invf.numpy(), D, dtype, "ref", cos_sin=tab)
+    exp_q = hp.apply_rope(to_bits(q)[rows], pos, invf.numpy(), D, dtype, mode, cos_sin=tab)
     np.testing.assert_array_equal(to_bits(qo), ENC[dtype](exp_q))
-    exp_k = hp.apply_rope(to_bits(k)[rows], pos, invf.numpy(), D, dtype, "ref", cos_sin=tab)
+    exp_k = hp.apply_rope(to_bits(k)[rows], pos, invf.numpy(), D, dtype, mode, cos_sin=tab)
     np.testing.assert_array_equal(to_bits(kc), hp.scatter_rows(kc0, pos, ENC[dtype](exp_k)))
     np.testing.assert_array_equal(to_bits(vc), hp.scatter_rows(vc0, pos, to_bits(v)[rows]))
 
