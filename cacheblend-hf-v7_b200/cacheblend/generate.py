@@ -15,7 +15,7 @@ import torch
 
 from cacheblend import ops
 from cacheblend.chunker import Chunk
-from cacheblend.fusor import _mlp, _norm, _selective_prefill, fuse_selective
+from cacheblend.fusor import _fused_w, _mlp, _norm, _qkv, _selective_prefill, fuse_selective
 from cacheblend.kv_store import KVStore
 
 
@@ -48,8 +48,9 @@ def _decode_step(lw, pre, st: _DecodeState, status):
     m = None
     for li, layer in enumerate(inner.layers):
         attn = layer.self_attn
+        w_qkv, w_gu = _fused_w(lw, li, 1)      # one row: the stacked GEMMs
         hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None, status=status)
-        q, k, v = attn.q_proj(hn), attn.k_proj(hn), attn.v_proj(hn)
+        q, k, v = _qkv(attn, hn, w_qkv)
         q_rot = ops.rope_scatter(q[0], k[0], v[0], st.pos, False, cap, geo.n_q, geo.n_kv, geo.head_dim, pre.rope,
                                  pre.fused_k[li], pre.fused_v[li], status=status)
         # the whole capacity with the position as the causal bound: rows past pos are
@@ -57,7 +58,7 @@ def _decode_step(lw, pre, st: _DecodeState, status):
         a = ops.partial_attn(q_rot, pre.fused_k[li], pre.fused_v[li], st.pos, geo.n_q, geo.n_kv, geo.head_dim,
                              geo.scaling, status=status, workspace=st.ws)
         o = attn.o_proj(a.unsqueeze(0))
-        m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=o, sum_out=h, status=status))
+        m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=o, sum_out=h, status=status), w_gu)
     row = lw.model.lm_head(_norm(inner.norm, h, delta=m, status=status))[0, -1]
     nxt = row.argmax().view(1)
     slot = st.pos - st.base

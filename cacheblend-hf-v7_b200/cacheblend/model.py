@@ -49,6 +49,25 @@ def attach_cache_layers(cache, kv: list[tuple[torch.Tensor, torch.Tensor]]):
     return cache
 
 
+def _stack_linear(mods) -> Optional[torch.Tensor]:
+    """One weight for bias-free nn.Linear modules that share an input size: each
+    module's rows in order.  The modules' weights become row views of it (same
+    values, one copy).  None if a module is not a bias-free nn.Linear or the
+    weights differ in input size, dtype or device."""
+    if any(not isinstance(m, torch.nn.Linear) or m.bias is not None for m in mods):
+        return None
+    ws = [m.weight for m in mods]
+    if len({(w.shape[1], w.dtype, w.device) for w in ws}) != 1:
+        return None
+    stacked = torch.cat([w.detach() for w in ws], 0)
+    off = 0
+    for m in mods:
+        n = m.weight.shape[0]
+        m.weight.data = stacked[off:off + n]
+        off += n
+    return stacked
+
+
 class LayerwiseModel:
     """HF causal LM wrapper with layer-by-layer forward and pre-RoPE K hooks."""
 
@@ -82,6 +101,28 @@ class LayerwiseModel:
         self._pre_rope_k: dict[int, torch.Tensor] = {}
         self._hook_handles: list = []
         self._install_k_proj_hooks()
+
+    def fused_projections(self, layer_idx: int):
+        """(W_qkv, W_gate_up) of decoder layer ``layer_idx``: the q/k/v and the
+        gate/up projection weights stacked along the output dimension, so one
+        GEMM computes each group (at a few hundred to a few thousand rows, or
+        one decode row, a single GEMM is faster than its parts).  On first use
+        the modules' own weights become row views of the stacked ones -- same
+        values, no second copy; a state dict taken afterwards holds views of
+        one buffer per group.  An entry is None where the layer's projections
+        are not bias-free nn.Linear modules of one input size."""
+        fused = getattr(self, "_fused", None)
+        if fused is None:
+            fused = []
+            with torch.inference_mode(False), torch.no_grad():
+                for layer in self._inner.layers:
+                    attn, mlp = layer.self_attn, getattr(layer, "mlp", None)
+                    qkv = [getattr(attn, n, None) for n in ("q_proj", "k_proj", "v_proj")]
+                    gu = [getattr(mlp, n, None) for n in ("gate_proj", "up_proj")]
+                    fused.append((_stack_linear(qkv) if all(m is not None for m in qkv) else None,
+                                  _stack_linear(gu) if all(m is not None for m in gu) else None))
+            self._fused = fused
+        return fused[layer_idx]
 
     # -- hooks ----------------------------------------------------------------
     def _install_k_proj_hooks(self) -> None:
