@@ -35,55 +35,9 @@ __global__ void rope_table_kernel(const float* __restrict__ inv_freq, int half_d
 // exact one wherever the rounding can tell (a product of two 8- or 11-bit
 // significands fits fp32's 24; a sum whose operands' exponents differ by more
 // than 24 - 8 bits lands within half an ulp of the larger operand either way),
-// so one correctly rounded 16-bit op gives the same bits as torch's two steps.
+// so one correctly rounded 16-bit op gives the same bits as torch's two steps
+// (Pk in cbk_common.cuh).
 // ---------------------------------------------------------------------------
-template <int DT> struct Pk;
-template <> struct Pk<CBK_BF16> {
-  // lo -> bits 0-15, hi -> bits 16-31
-  static __device__ __forceinline__ uint32_t cvt(float lo, float hi) {
-    uint32_t d;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-    return d;
-  }
-  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-  }
-  static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-  }
-  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-  }
-};
-template <> struct Pk<CBK_F16> {
-  static __device__ __forceinline__ uint32_t cvt(float lo, float hi) {
-    uint32_t d;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-    return d;
-  }
-  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-  }
-  static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-  }
-  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-  }
-};
-
 // c4: the table entries (cos, sin) of 8 consecutive frequencies, as 4 float4
 template <int DT>
 __device__ __forceinline__ void rope8t(const uint4& lo, const uint4& hi, const float4 (&c4)[4],

@@ -129,6 +129,23 @@ def test_silu_mul_bit_exact_vs_torch(dtype, rows, cols):
     assert torch.equal(out, ref)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_silu_every_16bit_input(dtype):
+    """The activation depends on the gate's 16 bits alone: all 65536 of them
+    against torch's own SiLU kernel (up = 1, so the output is the rounded
+    activation), NaN inputs giving NaN."""
+    from cacheblend import ops
+    bits = torch.arange(-32768, 32768, dtype=torch.int32, device=DEV).to(torch.int16)
+    gate = bits.view(dtype).reshape(1, 256, 256)
+    up = torch.ones_like(gate)
+    with torch.inference_mode():
+        ref = torch.nn.functional.silu(gate)
+        out = ops.silu_mul(gate, up)
+    nan = torch.isnan(ref)
+    assert torch.equal(torch.isnan(out), nan)
+    assert torch.equal(out.view(torch.int16)[~nan], ref.view(torch.int16)[~nan])
+
+
 def test_silu_mul_strided_halves():
     """gate and up as the two halves of one wider row (a merged projection)."""
     from cacheblend import ops
