@@ -204,9 +204,25 @@ __device__ __forceinline__ void exp2_fma_pair(float x0, float x1, float& y0, flo
 #define CBK_ATTN_EMU_MASK 0x9292
 #endif
 
+// Pair p holds tiles 2p - o and 2p + 1 - o, o = n_tiles mod 2: with an odd
+// count the tile without a partner is tile 0, the shortest, not the last one.
+__device__ __forceinline__ int pair_tile(int n_tiles, int pair, int t) {
+  return 2 * pair + t - (n_tiles & 1);
+}
+
+// Q tiles are aligned to the end of the selection: tile t holds tokens
+// [n_sel - (n_tiles - t) * tok_per_tile, + tok_per_tile), so the one partly
+// filled tile is tile 0, whose tokens come first and see the fewest keys (the
+// last selected tokens, which see every key, fill whole tiles).  Tile 0's
+// first token may be negative: those rows load as zeros and are not stored.
+__device__ __forceinline__ int64_t tile_tok0(int64_t n_sel, int n_tiles, int tok_per_tile, int tile) {
+  return n_sel - static_cast<int64_t>(n_tiles - tile) * tok_per_tile;
+}
+
 // number of 128-key tiles a Q tile needs (its last token has the largest position)
-__device__ __forceinline__ int tile_key_tiles(const int64_t* pos, int64_t n_sel, int tok_per_tile, int tile) {
-  const int64_t last = min(static_cast<int64_t>(tile + 1) * tok_per_tile, n_sel) - 1;
+__device__ __forceinline__ int tile_key_tiles(const int64_t* pos, int64_t n_sel, int n_tiles, int tok_per_tile,
+                                              int tile) {
+  const int64_t last = tile_tok0(n_sel, n_tiles, tok_per_tile, tile) + tok_per_tile - 1;
   return static_cast<int>(pos[last] / kBN) + 1;
 }
 
@@ -215,7 +231,8 @@ struct ItemGeom {
   int kvh, pair, chunk, j0;
   int n_kv[2];          // key tiles of this item for tile 0 / 1 (0: tile absent or done)
   int n_all;            // max of the two
-  int n_q_tiles;        // 1 when the pair's second tile does not exist
+  int tile[2];           // tile index of slot 0 / 1 (out of range: slot empty)
+  bool has[2];           // the slot holds a tile
   int64_t tok0[2], tok_end[2], p_max[2];
 };
 
@@ -227,21 +244,22 @@ __device__ __forceinline__ ItemGeom item_geom(const int4 item, int C, const Attn
   g.j0 = item.z * C;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    const int tile = 2 * g.pair + t;
-    g.tok0[t] = static_cast<int64_t>(tile) * prm.tok_per_tile;
-    if (tile >= prm.n_tiles) {
+    const int tile = pair_tile(prm.n_tiles, g.pair, t);
+    g.tile[t] = tile;
+    g.has[t] = tile >= 0 && tile < prm.n_tiles;
+    g.tok0[t] = tile_tok0(prm.n_sel, prm.n_tiles, prm.tok_per_tile, tile);
+    if (!g.has[t]) {
       g.tok_end[t] = g.tok0[t];
       g.p_max[t] = 0;
       g.n_kv[t] = 0;
     } else {
-      g.tok_end[t] = min(g.tok0[t] + prm.tok_per_tile, prm.n_sel);
+      g.tok_end[t] = g.tok0[t] + prm.tok_per_tile;
       g.p_max[t] = prm.pos[g.tok_end[t] - 1];
       const int n_full = static_cast<int>(g.p_max[t] / kBN) + 1;
       g.n_kv[t] = max(0, min(C, n_full - g.j0));
     }
   }
   g.n_all = max(g.n_kv[0], g.n_kv[1]);
-  g.n_q_tiles = (2 * g.pair + 1 < prm.n_tiles) ? 2 : 1;
   return g;
 }
 
@@ -346,12 +364,14 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         break;
       }
       if (leader) {
-        mbar_expect_tx(bar(B_QFULL), ig.n_q_tiles * L::kQBytes);
-        for (int t = 0; t < ig.n_q_tiles; ++t)
+        mbar_expect_tx(bar(B_QFULL), (ig.has[0] + ig.has[1]) * L::kQBytes);
+        for (int t = 0; t < 2; ++t) {
+          if (!ig.has[t]) continue;
 #pragma unroll
           for (int h = 0; h < HD / 64; ++h)
             tma_load_3d(sQ + t * L::kQBytes + h * (kBM * 128), &tm_q, bar(B_QFULL), h * 64,
                         ig.kvh * prm.group, static_cast<int>(ig.tok0[t]));
+        }
       }
       ++n_q;
       for (int j = 0; j < ig.n_all; ++j, ++g) {
@@ -521,7 +541,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       const int n_t = t ? ig.n_kv[1] : ig.n_kv[0];
       if (n_t == 0) continue;
       const int64_t tok = (t ? ig.tok0[1] : ig.tok0[0]) + row / prm.group;
-      const bool row_valid = tok < (t ? ig.tok_end[1] : ig.tok_end[0]);
+      const bool row_valid = tok >= 0 && tok < (t ? ig.tok_end[1] : ig.tok_end[0]);
       const int64_t p_row = row_valid ? prm.pos[tok] : (t ? ig.p_max[1] : ig.p_max[0]);
       float m_used = -INFINITY, l_sum = 0.f;
       for (int j = 0; j < n_t; ++j, ++sc) {
@@ -629,7 +649,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       ++oc;
       tc_fence_after();
-      const int slot0 = prm.tile_base[ig.kvh * prm.n_tiles + 2 * ig.pair + t];
+      const int slot0 = prm.tile_base[ig.kvh * prm.n_tiles + (t ? ig.tile[1] : ig.tile[0])];
       if (slot0 >= 0) {
         // split tile: this chunk's O / l (fp16), running max and row sum
         const int64_t slot = slot0 + ig.chunk;
@@ -748,8 +768,8 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
   }
   for (int i = tid; i <= kMaxKvTiles; i += kPlanThreads) s_hist[i] = 0;
   __syncthreads();
-  auto pair_tiles = [&](int p) {   // the later tile of a pair has the larger key range
-    return tile_key_tiles(pos, n_sel, tok_per_tile, min(2 * p + 1, n_tiles - 1));
+  auto pair_tiles = [&](int p) {   // the later tile of a pair (always present) has the larger key range
+    return tile_key_tiles(pos, n_sel, n_tiles, tok_per_tile, pair_tile(n_tiles, p, 1));
   };
   // 1. key-tile iterations of all pairs
   unsigned long long local = 0;
@@ -819,7 +839,7 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
     const int i = b0 + tid;
     int cnt = 0;
     if (i < n_all) {
-      const int nc = (tile_key_tiles(pos, n_sel, tok_per_tile, i % n_tiles) + C - 1) / C;
+      const int nc = (tile_key_tiles(pos, n_sel, n_tiles, tok_per_tile, i % n_tiles) + C - 1) / C;
       cnt = nc > 1 ? nc : 0;
     }
     int tot, tot_split;
@@ -943,8 +963,8 @@ attn_combine_kernel(const AttnParams prm) {
       const int vi = tid + i * kCombineThreads;
       const int r = vi / kVecRow, v = vi % kVecRow;
       const int row = row0 + r;
-      const int64_t tok = static_cast<int64_t>(tile) * prm.tok_per_tile + row / prm.group;
-      if (tok >= prm.n_sel) continue;    // padding row of the last tile
+      const int64_t tok = tile_tok0(prm.n_sel, prm.n_tiles, prm.tok_per_tile, tile) + row / prm.group;
+      if (tok < 0) continue;             // padding row of the first tile
       const float inv = 1.f / s_sum[r];
       const int hq = kvh * prm.group + row % prm.group;
       uint4 o;
