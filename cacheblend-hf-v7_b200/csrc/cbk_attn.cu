@@ -867,15 +867,15 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
 // Merge the partial results of split tiles:
 //   O = sum_c w_c Ohat_c / sum_c w_c,  w_c = l_c 2^(m_c - M),  Ohat_c = O_c / l_c
 // (a chunk without visible keys has l = 0 and weight 0).  Work unit = half a
-// split tile (64 rows), one CTA, from the plan's split-tile descriptors.  Row
-// maxima first (64 threads), then per group of up to 32 chunks the weights go to
-// shared memory in one coalesced round trip, and every thread accumulates its
-// four 8-element vectors with four chunk rows of loads in flight.  Sums run over
-// the chunks in increasing order, so results are deterministic.
+// split tile (64 rows), one CTA; a thread owns kVecThr 8-element vectors of
+// different rows and computes those rows' maxima and weights itself from the
+// (m, l) pairs (no shared memory, no block barriers).  The first kCombinePre
+// chunks' O vectors are loaded together with the (m, l) pairs, so a unit of up
+// to kCombinePre chunks costs one round trip to L2.  Sums run over the chunks in
+// increasing order, so results are deterministic.
 // ---------------------------------------------------------------------------
 constexpr int kCombineThreads = 256;
 constexpr int kCombineRows = 64;        // rows per work unit
-constexpr int kCombineGroup = 32;       // chunks whose weights sit in shared memory at once
 constexpr int kCombinePre = 4;          // chunk rows loaded together
 
 template <int DT, int HD>
@@ -883,89 +883,80 @@ __global__ void __launch_bounds__(kCombineThreads, 2)
 attn_combine_kernel(const AttnParams prm) {
   constexpr int kVecRow = HD / 8;                                     // 8-element vectors per row
   constexpr int kVecThr = kCombineRows * kVecRow / kCombineThreads;  // 4 (HD 128) or 2 (HD 64)
-  __shared__ float s_w[kCombineGroup][kCombineRows];
-  __shared__ float s_m[kCombineRows];
-  __shared__ float s_sum[kCombineRows];
+  constexpr int kRowStep = kCombineThreads / kVecRow;                 // rows between a thread's vectors
   const int tid = threadIdx.x;
   // every attention CTA has finished: rewind the item queue for the next call
   if (blockIdx.x == 0 && tid == 0) *prm.queue = 0;
   if (prm.plan->error) return;
   const int n_units = prm.plan->n_split * (kBM / kCombineRows);
+  const int v = tid % kVecRow;                   // the thread's vector within each of its rows
   for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
     const int4 d = prm.split_desc[u / (kBM / kCombineRows)];
-    const int row0 = (u % (kBM / kCombineRows)) * kCombineRows;
+    const int row0 = (u % (kBM / kCombineRows)) * kCombineRows + tid / kVecRow;   // row of vector 0
     const int kvh = d.x / prm.n_tiles, tile = d.x % prm.n_tiles;
     const int64_t slot0 = d.y;
     const int nc = d.z;
-    __syncthreads();                     // shared arrays of the previous unit are free
-    if (tid < kCombineRows) {
-      float M = -INFINITY;
+    auto o_ptr = [&](int c, int i) {
+      return prm.part_o + ((slot0 + c) * kBM + row0 + i * kRowStep) * HD + v * 8;
+    };
+    auto ml_ptr = [&](int c, int i) { return prm.part_ml + (slot0 + c) * kBM + row0 + i * kRowStep; };
+    uint4 raw[kCombinePre][kVecThr];
+#pragma unroll
+    for (int q = 0; q < kCombinePre; ++q)
+      if (q < nc) {
+#pragma unroll
+        for (int i = 0; i < kVecThr; ++i) raw[q][i] = ld_vec(o_ptr(q, i));
+      }
+    float M[kVecThr];
+#pragma unroll
+    for (int i = 0; i < kVecThr; ++i) M[i] = -INFINITY;
 #pragma unroll 4
-      for (int c = 0; c < nc; ++c) {
-        const float2 ml = prm.part_ml[(slot0 + c) * kBM + row0 + tid];
-        if (ml.y > 0.f) M = fmaxf(M, ml.x);
+    for (int c = 0; c < nc; ++c)
+#pragma unroll
+      for (int i = 0; i < kVecThr; ++i) {
+        const float2 ml = *ml_ptr(c, i);
+        if (ml.y > 0.f) M[i] = fmaxf(M[i], ml.x);
       }
-      s_m[tid] = M;
-      s_sum[tid] = 0.f;
-    }
-    float acc[kVecThr][8];
-#pragma unroll
-    for (int i = 0; i < kVecThr; ++i)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
-    for (int g0 = 0; g0 < nc; g0 += kCombineGroup) {
-      const int gn = min(kCombineGroup, nc - g0);
-      __syncthreads();                   // s_m ready; s_w of the previous group consumed
-      for (int e = tid; e < gn * kCombineRows; e += kCombineThreads) {
-        const int c = e / kCombineRows, r = e % kCombineRows;
-        const float2 ml = prm.part_ml[(slot0 + g0 + c) * kBM + row0 + r];
-        s_w[c][r] = ml.y > 0.f ? ml.y * ex2(ml.x - s_m[r]) : 0.f;
-      }
-      __syncthreads();
-      if (tid < kCombineRows) {
-        float sum = s_sum[tid];
-        for (int c = 0; c < gn; ++c) sum += s_w[c][tid];
-        s_sum[tid] = sum;
-      }
-      for (int c0 = 0; c0 < gn; c0 += kCombinePre) {
-        uint4 raw[kCombinePre][kVecThr];
-#pragma unroll
-        for (int q = 0; q < kCombinePre; ++q)
-          if (c0 + q < gn) {
-#pragma unroll
-            for (int i = 0; i < kVecThr; ++i) {
-              const int vi = tid + i * kCombineThreads;
-              const int r = vi / kVecRow, v = vi % kVecRow;
-              raw[q][i] = ld_vec(prm.part_o + ((slot0 + g0 + c0 + q) * kBM + row0 + r) * HD + v * 8);
-            }
-          }
-#pragma unroll
-        for (int q = 0; q < kCombinePre; ++q)
-          if (c0 + q < gn) {
-#pragma unroll
-            for (int i = 0; i < kVecThr; ++i) {
-              const int r = (tid + i * kCombineThreads) / kVecRow;
-              const float w = s_w[c0 + q][r];
-              const __half2* h = reinterpret_cast<const __half2*>(&raw[q][i]);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 f = __half22float2(h[e]);
-                acc[i][2 * e] = fmaf(w, f.x, acc[i][2 * e]);
-                acc[i][2 * e + 1] = fmaf(w, f.y, acc[i][2 * e + 1]);
-              }
-            }
-          }
-      }
-    }
-    __syncthreads();                     // s_sum complete
+    float acc[kVecThr][8], sum[kVecThr];
 #pragma unroll
     for (int i = 0; i < kVecThr; ++i) {
-      const int vi = tid + i * kCombineThreads;
-      const int r = vi / kVecRow, v = vi % kVecRow;
-      const int row = row0 + r;
+      sum[i] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+    }
+    for (int c0 = 0; c0 < nc; c0 += kCombinePre) {
+      if (c0 > 0) {
+#pragma unroll
+        for (int q = 0; q < kCombinePre; ++q)
+          if (c0 + q < nc) {
+#pragma unroll
+            for (int i = 0; i < kVecThr; ++i) raw[q][i] = ld_vec(o_ptr(c0 + q, i));
+          }
+      }
+#pragma unroll
+      for (int q = 0; q < kCombinePre; ++q)
+        if (c0 + q < nc) {
+#pragma unroll
+          for (int i = 0; i < kVecThr; ++i) {
+            const float2 ml = *ml_ptr(c0 + q, i);
+            const float w = ml.y > 0.f ? ml.y * ex2(ml.x - M[i]) : 0.f;
+            sum[i] += w;
+            const __half2* h = reinterpret_cast<const __half2*>(&raw[q][i]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(h[e]);
+              acc[i][2 * e] = fmaf(w, f.x, acc[i][2 * e]);
+              acc[i][2 * e + 1] = fmaf(w, f.y, acc[i][2 * e + 1]);
+            }
+          }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kVecThr; ++i) {
+      const int row = row0 + i * kRowStep;
       const int64_t tok = tile_tok0(prm.n_sel, prm.n_tiles, prm.tok_per_tile, tile) + row / prm.group;
       if (tok < 0) continue;             // padding row of the first tile
-      const float inv = 1.f / s_sum[r];
+      const float inv = 1.f / sum[i];
       const int hq = kvh * prm.group + row % prm.group;
       uint4 o;
       uint32_t* w = reinterpret_cast<uint32_t*>(&o);
