@@ -42,7 +42,13 @@ add_rmsnorm_kernel(const uint16_t* x, int64_t x_stride, int64_t x_rows, const in
   }
   const int n_vec = cols / 8;
   const uint16_t* xr = x + src * x_stride;
-  uint4 v[kNormMaxVec];
+  uint4 v[kNormMaxVec], wv[kNormMaxVec];
+  // the weight does not depend on the row: its loads go out before the reduction
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int c = (i * kNormThreads + threadIdx.x);
+    if (c < n_vec) wv[i] = ld_vec(weight + c * 8);
+  }
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < kNormMaxVec; ++i) {
@@ -81,9 +87,8 @@ add_rmsnorm_kernel(const uint16_t* x, int64_t x_stride, int64_t x_rows, const in
   for (int i = 0; i < kNormMaxVec; ++i) {
     const int c = (i * kNormThreads + threadIdx.x);
     if (c < n_vec) {
-      const uint4 wv = ld_vec(weight + c * 8);
       const uint16_t* h = reinterpret_cast<const uint16_t*>(&v[i]);
-      const uint16_t* hw = reinterpret_cast<const uint16_t*>(&wv);
+      const uint16_t* hw = reinterpret_cast<const uint16_t*>(&wv[i]);
       uint4 o;
       uint16_t* ho = reinterpret_cast<uint16_t*>(&o);
 #pragma unroll
