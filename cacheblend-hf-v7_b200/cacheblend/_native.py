@@ -48,6 +48,7 @@ SIGNATURES = {
                                _vp, _i64, _vp, _vp]),
     "cbk_silu_mul": (_i32, [_vp, _i64, _vp, _i64, _i64, _i32, _i32, _vp, _i64, _vp]),
     "cbk_scatter_rows": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp]),
+    "cbk_gemv": (_i32, [_vp, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
 }
 
 

@@ -2,10 +2,12 @@
 runners, ``runners.py:106-152``) on the libcbk kernels.
 
 The selective prefill keeps its fused cache with spare rows; each decode step
-then runs the decoder for one token at position p: residual add + RMSNorm and
-SiLU * up as the fused row kernels, RoPE of the token's Q and K with its K/V
-written into cache row p (``rope_scatter`` with one index), and attention of
-the one query row over rows [0, p] (``partial_attn``).  Token 1 is the argmax of
+then runs the decoder for one token at position p: residual add + RMSNorm as
+the fused row kernel, the projections as one-row GEMV kernels (q/k/v and
+gate/up over the stacked weights, SiLU * up formed inside the down
+projection's GEMV, lm_head), RoPE of the token's Q and K with its K/V written
+into cache row p (``rope_scatter`` with one index), and attention of the one
+query row over rows [0, p] (``partial_attn``).  Token 1 is the argmax of
 the last prefill row, as in the reference; decoding stops after
 ``max_new_tokens`` tokens or at ``eos_token_id``.
 """
@@ -15,7 +17,7 @@ import torch
 
 from cacheblend import ops
 from cacheblend.chunker import Chunk
-from cacheblend.fusor import _fused_w, _mlp, _norm, _qkv, _selective_prefill, fuse_selective
+from cacheblend.fusor import _MLPS, _SILUS, _fused_w, _mlp, _norm, _qkv, _selective_prefill, fuse_selective
 from cacheblend.kv_store import KVStore
 
 
@@ -38,6 +40,40 @@ class _DecodeState:
         self.ws = ops.attn_workspace(1, cap, geo.n_q, geo.n_kv, geo.head_dim, device)
 
 
+def _gemv_ok(w: torch.Tensor, x: torch.Tensor) -> bool:
+    return w.dtype == x.dtype and w.shape[1] % 8 == 0 and w.shape[1] <= 16384 and w.stride(1) == 1
+
+
+def _lin1(mod, x):
+    """A Linear at one decode row on the GEMV kernel (bias-free, the input's
+    dtype), else the module itself."""
+    if isinstance(mod, torch.nn.Linear) and mod.bias is None and _gemv_ok(mod.weight, x):
+        return ops.gemv(mod.weight, x)
+    return mod(x)
+
+
+def _qkv1(attn, hn, w_qkv):
+    if w_qkv is None or not _gemv_ok(w_qkv, hn):
+        return _qkv(attn, hn, w_qkv)
+    qkv = ops.gemv(w_qkv, hn)
+    nq, nk = attn.q_proj.weight.shape[0], attn.k_proj.weight.shape[0]
+    return qkv[..., :nq], qkv[..., nq:nq + nk], qkv[..., nq + nk:]
+
+
+def _mlp1(layer, hn, w_gu):
+    """MLP at one decode row: the stacked gate/up GEMV, then the down GEMV with
+    silu(gate) * up formed as it stages its input."""
+    mlp = layer.mlp
+    down = getattr(mlp, "down_proj", None)
+    if (w_gu is None or type(mlp).__name__ not in _MLPS or type(mlp.act_fn).__name__ not in _SILUS
+            or not isinstance(down, torch.nn.Linear) or down.bias is not None or not _gemv_ok(w_gu, hn)
+            or not _gemv_ok(down.weight, hn)):
+        return _mlp(layer, hn, w_gu)
+    gu = ops.gemv(w_gu, hn)
+    inter = mlp.gate_proj.weight.shape[0]
+    return ops.gemv(down.weight, gate=gu[..., :inter], up=gu[..., inter:])
+
+
 def _decode_step(lw, pre, st: _DecodeState, status):
     """One token at position st.pos: its K/V into cache row pos, the next token
     into st.token / st.tokens, pos advanced -- all on the device, no host sync
@@ -50,16 +86,16 @@ def _decode_step(lw, pre, st: _DecodeState, status):
         attn = layer.self_attn
         w_qkv, w_gu = _fused_w(lw, li, 1)      # one row: the stacked GEMMs
         hn = _norm(layer.input_layernorm, h, delta=m, sum_out=h if m is not None else None, status=status)
-        q, k, v = _qkv(attn, hn, w_qkv)
+        q, k, v = _qkv1(attn, hn, w_qkv)
         q_rot = ops.rope_scatter(q[0], k[0], v[0], st.pos, False, cap, geo.n_q, geo.n_kv, geo.head_dim, pre.rope,
                                  pre.fused_k[li], pre.fused_v[li], status=status)
         # the whole capacity with the position as the causal bound: rows past pos are
         # invisible (and zero), so the call does not change from step to step
         a = ops.partial_attn(q_rot, pre.fused_k[li], pre.fused_v[li], st.pos, geo.n_q, geo.n_kv, geo.head_dim,
                              geo.scaling, status=status, workspace=st.ws)
-        o = attn.o_proj(a.unsqueeze(0))
-        m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=o, sum_out=h, status=status), w_gu)
-    row = lw.model.lm_head(_norm(inner.norm, h, delta=m, status=status))[0, -1]
+        o = _lin1(attn.o_proj, a.unsqueeze(0))
+        m = _mlp1(layer, _norm(layer.post_attention_layernorm, h, delta=o, sum_out=h, status=status), w_gu)
+    row = _lin1(lw.model.lm_head, _norm(inner.norm, h, delta=m, status=status))[0, -1]
     nxt = row.argmax().view(1)
     slot = st.pos - st.base
     st.tokens.index_copy_(0, slot, nxt)

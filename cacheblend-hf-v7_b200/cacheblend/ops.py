@@ -391,6 +391,29 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = No
     return out
 
 
+def gemv(weight: torch.Tensor, x: torch.Tensor | None = None, gate: torch.Tensor | None = None,
+         up: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """One-row projection x @ weight.T (a decode step's Linear), fp32 accumulation,
+    shape (..., N) for x of shape (..., K) with one row.  With gate and up instead
+    of x, the input is round16(round16(silu(gate)) * up) (silu_mul's arithmetic)."""
+    src = x if x is not None else gate
+    dev = require_cuda(weight, src, up, out)
+    if (x is None) == (gate is None) or (gate is None) != (up is None):
+        raise ValueError("gemv: pass x, or gate and up")
+    k = weight.shape[1]
+    if src.shape[-1] != k or src.numel() != k or (up is not None and up.shape != gate.shape):
+        raise ValueError(f"gemv: one input row of {k} elements expected, got {list(src.shape)}")
+    if weight.stride(1) != 1:
+        raise ValueError("gemv: weight rows must be contiguous")
+    if out is None:
+        out = torch.empty((*src.shape[:-1], weight.shape[0]), dtype=weight.dtype, device=dev)
+    xs = [t if t is None or t.is_contiguous() else t.contiguous() for t in (x, gate, up)]
+    with TIMES.span("gemv", dev):
+        N.check(N.LIB.cbk_gemv(_vp(weight), weight.stride(0), _vp(xs[0]), _vp(xs[1]), _vp(xs[2]), weight.shape[0],
+                               k, dtype_code(weight.dtype), _vp(out), _stream(dev)), "cbk_gemv")
+    return out
+
+
 def scatter_rows(src: torch.Tensor, idx: torch.Tensor, n_rows: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """Dense [n_rows][...] rows: out[idx[j]] = src[j], zeros elsewhere (idx ascending,
     distinct), every output byte written once."""

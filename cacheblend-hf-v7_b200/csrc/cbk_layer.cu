@@ -128,6 +128,75 @@ __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, int64_t g_stride
   }
 }
 
+// One-row projection (a decode step): y[n] = round16(sum_k W[n][k] x[k]) in
+// fp32, W row-major [N][K].  HBM-bound, every weight byte read once: a warp
+// owns one output row at a time and each lane keeps kGemvVecs 16-byte weight
+// loads in flight (issued before any arithmetic); x is staged once per CTA in
+// shared memory.  With gate/up given, x[k] = round16(round16(silu(gate[k])) *
+// up[k]) is formed while staging (silu_mul's arithmetic), so the MLP's down
+// projection needs no separate activation launch.
+constexpr int kGemvThreads = 256;
+constexpr int kGemvVecs = 8;
+constexpr int kGemvMaxK = 16384;      // x in shared memory: K * 2 bytes <= 32 KB
+
+template <int DT>
+__global__ void __launch_bounds__(kGemvThreads)
+gemv_kernel(const uint16_t* __restrict__ w, int64_t w_stride, const uint16_t* __restrict__ x,
+            const uint16_t* __restrict__ gate, const uint16_t* __restrict__ up, int K, int64_t N,
+            uint16_t* __restrict__ y) {
+  using E = Elem<DT>;
+  __shared__ uint4 s_x[kGemvMaxK / 8];
+  const int kv = K / 8;
+  for (int i = threadIdx.x; i < kv; i += kGemvThreads) {
+    if (gate) {
+      const uint4 a = ld_vec(gate + i * 8), b = ld_vec(up + i * 8);
+      const uint16_t* ha = reinterpret_cast<const uint16_t*>(&a);
+      const uint16_t* hb = reinterpret_cast<const uint16_t*>(&b);
+      uint4 o;
+      uint16_t* ho = reinterpret_cast<uint16_t*>(&o);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float xg = E::to_f(ha[e]);
+        const float act = round16<DT>(xg / (1.0f + expf(-xg)));
+        ho[e] = E::from_f(act * E::to_f(hb[e]));
+      }
+      s_x[i] = o;
+    } else {
+      s_x[i] = ld_vec(x + i * 8);
+    }
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kGemvThreads / 32);
+  for (int64_t n = static_cast<int64_t>(blockIdx.x) * (kGemvThreads / 32) + (threadIdx.x >> 5); n < N;
+       n += warps) {
+    const uint16_t* wr = w + n * w_stride;
+    float acc0 = 0.f, acc1 = 0.f;
+    for (int v0 = lane; v0 < kv; v0 += 32 * kGemvVecs) {
+      uint4 wv[kGemvVecs];
+#pragma unroll
+      for (int u = 0; u < kGemvVecs; ++u)
+        if (v0 + 32 * u < kv) wv[u] = ld_stream(wr + (v0 + 32 * u) * 8);
+#pragma unroll
+      for (int u = 0; u < kGemvVecs; ++u) {
+        if (v0 + 32 * u >= kv) break;
+        const uint4 xv = s_x[v0 + 32 * u];
+        const uint16_t* hw = reinterpret_cast<const uint16_t*>(&wv[u]);
+        const uint16_t* hx = reinterpret_cast<const uint16_t*>(&xv);
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          acc0 = fmaf(E::to_f(hw[e]), E::to_f(hx[e]), acc0);
+          acc1 = fmaf(E::to_f(hw[e + 1]), E::to_f(hx[e + 1]), acc1);
+        }
+      }
+    }
+    float acc = acc0 + acc1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) y[n] = E::from_f(acc);
+  }
+}
+
 // Dense rows from selected rows: dst[r] = src[j] where idx[j] == r, zeros for
 // the rows no index names.  idx is ascending and distinct; a row finds its
 // source by binary search (thread 0 of the block, broadcast through shared
@@ -264,4 +333,32 @@ extern "C" int cbk_scatter_rows(const void* src, int64_t src_stride_bytes, const
       static_cast<const uint8_t*>(src), src_stride_bytes, idx, k, static_cast<uint8_t*>(dst), dst_stride_bytes, S,
       row_bytes);
   return check_launch("scatter_rows_kernel");
+}
+
+extern "C" int cbk_gemv(const void* w, int64_t w_row_stride, const void* x, const void* gate, const void* up,
+                        int64_t n, int k, int dtype, void* y, void* stream) {
+  if (dtype != CBK_BF16 && dtype != CBK_F16)
+    return set_error(CBK_ERR_UNSUPPORTED, "cbk_gemv: dtype %d not supported", dtype);
+  if (n < 0 || k <= 0 || k % 8 != 0 || k > kGemvMaxK)
+    return set_error(CBK_ERR_INVALID, "cbk_gemv: need 0 <= n, 0 < k <= %d, k %% 8 == 0 (n %lld, k %d)",
+                     kGemvMaxK, (long long)n, k);
+  if (!w || !y || (gate == nullptr) != (up == nullptr) || (!x && !gate))
+    return set_error(CBK_ERR_INVALID, "cbk_gemv: null pointer argument (x, or gate and up together)");
+  if (w_row_stride < k || w_row_stride % 8 != 0 || !aligned16(w) || (x && !aligned16(x)) ||
+      (gate && (!aligned16(gate) || !aligned16(up))))
+    return set_error(CBK_ERR_INVALID, "cbk_gemv: 16-byte aligned pointers and a row stride >= k, multiple of 8");
+  if (n == 0) return CBK_OK;
+  auto st = static_cast<cudaStream_t>(stream);
+  const int64_t want = (n + kGemvThreads / 32 - 1) / (kGemvThreads / 32);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(want, 16LL * sm_count_layer()));
+  auto wp = static_cast<const uint16_t*>(w);
+  auto xp = static_cast<const uint16_t*>(x);
+  auto gp = static_cast<const uint16_t*>(gate);
+  auto upp = static_cast<const uint16_t*>(up);
+  auto yp = static_cast<uint16_t*>(y);
+  if (dtype == CBK_BF16)
+    gemv_kernel<CBK_BF16><<<grid, kGemvThreads, 0, st>>>(wp, w_row_stride, xp, gp, upp, k, n, yp);
+  else
+    gemv_kernel<CBK_F16><<<grid, kGemvThreads, 0, st>>>(wp, w_row_stride, xp, gp, upp, k, n, yp);
+  return check_launch("gemv_kernel");
 }

@@ -205,6 +205,17 @@ int cbk_add_rmsnorm(const void* x, int64_t x_stride, int64_t x_rows, const int64
 int cbk_silu_mul(const void* gate, int64_t gate_stride, const void* up, int64_t up_stride,
                  int64_t n_rows, int cols, int dtype, void* out, int64_t out_stride, void* stream);
 
+/* One-row projection of a decode step (the HF q/k/v, o, gate/up, down and
+ * lm_head Linear layers at one token, runners.py:106-152 via the model
+ * forward): y[i] = round16(sum_j w[i][j] x[j]) for i < n, accumulated in fp32
+ * (order differs from cuBLAS: results agree within fp32 rounding).  w: n rows
+ * of k elements with row stride w_row_stride (elements, multiple of 8), k % 8
+ * == 0, k <= 16384; 16-byte aligned pointers.  When gate and up are given
+ * (both, instead of x), x[j] = round16(round16(silu(gate[j])) * up[j]) as in
+ * cbk_silu_mul. */
+int cbk_gemv(const void* w, int64_t w_row_stride, const void* x, const void* gate, const void* up,
+             int64_t n, int k, int dtype, void* y, void* stream);
+
 /* Dense logits of the selected rows (fusor.py:483-491, the (1, S, vocab) zeros
  * plus index_copy_): dst[r] = src[j] for idx[j] == r, zero rows elsewhere, each
  * output byte written once.  idx: k int64 ascending distinct positions in

@@ -70,6 +70,14 @@ def test_abi_version_and_pure_helpers():
     ("cbk_silu_mul(16, 64, 16, 60, 4, 64, 0, 16, 64, None)", -1),
     ("cbk_silu_mul(16, 64, 16, 64, 0, 64, 0, 16, 64, None)", 0),
     # scatter_rows(src, src_stride, idx, k, dst, dst_stride, S, row_bytes, stream)
+    ("cbk_gemv(16, 64, 16, None, None, 4, 64, 2, 16, None)", -2),
+    ("cbk_gemv(16, 64, 16, None, None, 4, 12, 0, 16, None)", -1),
+    ("cbk_gemv(16, 64, 16, None, None, 4, 64, 0, None, None)", -1),
+    ("cbk_gemv(16, 64, None, 16, None, 4, 64, 0, 16, None)", -1),
+    ("cbk_gemv(24, 64, 16, None, None, 4, 64, 0, 16, None)", -1),
+    ("cbk_gemv(16, 60, 16, None, None, 4, 64, 0, 16, None)", -1),
+    ("cbk_gemv(16, 32768, 16, None, None, 4, 32768, 0, 16, None)", -1),
+    ("cbk_gemv(16, 64, 16, None, None, 0, 64, 0, 16, None)", 0),
     ("cbk_scatter_rows(16, 64, 16, 2, None, 64, 4, 64, None)", -1),
     ("cbk_scatter_rows(16, 64, 16, 5, 16, 64, 4, 64, None)", -1),
     ("cbk_scatter_rows(16, 64, 16, 2, 16, 64, 4, 60, None)", -1),

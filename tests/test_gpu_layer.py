@@ -170,3 +170,35 @@ def test_scatter_rows_dense_logits(S, k, V, dtype):
     out = torch.full((S, V), 7.0, dtype=dtype, device=DEV)       # every byte must be rewritten
     ops.scatter_rows(src, idx, S, out=out)
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n,k", [(4096, 4096), (300, 14336), (33, 1000), (5, 8)])
+def test_gemv_one_row(dtype, n, k):
+    """ops.gemv against an fp64 product of the same 16-bit inputs: within half
+    a 16-bit ulp of the result plus the fp32 accumulation error."""
+    from cacheblend import ops
+    g = torch.Generator(device=DEV).manual_seed(n + k)
+    w = (torch.randn((n, k), generator=g, device=DEV) * 0.05).to(dtype)
+    x = torch.randn((1, 1, k), generator=g, device=DEV).to(dtype)
+    y = ops.gemv(w, x)
+    assert y.shape == (1, 1, n) and y.dtype == dtype
+    ref = w.double() @ x.view(-1).double()
+    mag = w.double().abs() @ x.view(-1).double().abs()
+    ulp = 2.0 ** (-8 if dtype == torch.bfloat16 else -11)
+    # (fp16 results below 2^-14 are subnormal: their rounding step is 2^-24 absolute)
+    bound = ref.abs() * ulp + mag * (k * 2.0 ** -23) + (2.0 ** -24 if dtype == torch.float16 else 1e-30)
+    assert torch.all((y.view(-1).double() - ref).abs() <= bound)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gemv_with_silu_mul_input(dtype):
+    """gate/up given: the same bits as silu_mul followed by the plain GEMV."""
+    from cacheblend import ops
+    g = torch.Generator(device=DEV).manual_seed(7)
+    inter, n = 2048, 512
+    gu = (torch.randn((1, 1, 2 * inter), generator=g, device=DEV) * 3).to(dtype)
+    w = (torch.randn((n, inter), generator=g, device=DEV) * 0.05).to(dtype)
+    fused = ops.gemv(w, gate=gu[..., :inter], up=gu[..., inter:])
+    plain = ops.gemv(w, ops.silu_mul(gu[..., :inter], gu[..., inter:]))
+    assert torch.equal(fused, plain)
