@@ -91,8 +91,9 @@ def _decode_step(lw, pre, st: _DecodeState, status):
                                  pre.fused_k[li], pre.fused_v[li], status=status)
         # the whole capacity with the position as the causal bound: rows past pos are
         # invisible (and zero), so the call does not change from step to step
+        # the plan depends on the position only: made by the first layer, reused by the rest
         a = ops.partial_attn(q_rot, pre.fused_k[li], pre.fused_v[li], st.pos, geo.n_q, geo.n_kv, geo.head_dim,
-                             geo.scaling, status=status, workspace=st.ws)
+                             geo.scaling, status=status, workspace=st.ws, reuse_plan=li > 0)
         o = _lin1(attn.o_proj, a.unsqueeze(0))
         m = _mlp1(layer, _norm(layer.post_attention_layernorm, h, delta=o, sum_out=h, status=status), w_gu)
     row = _lin1(lw.model.lm_head, _norm(inner.norm, h, delta=m, status=status))[0, -1]
