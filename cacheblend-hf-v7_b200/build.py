@@ -19,7 +19,7 @@ PKG_DIR = os.path.join(ROOT, "cacheblend")
 CSRC = os.path.join(ROOT, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libcbk.so")
-SOURCES = ["cbk_api.cu", "cbk_rope.cu", "cbk_hkvd.cu", "cbk_attn.cu", "cbk_layer.cu"]
+SOURCES = ["cbk_api.cu", "cbk_rope.cu", "cbk_hkvd.cu", "cbk_attn.cu", "cbk_layer.cu", "cbk_decode.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr"]
 

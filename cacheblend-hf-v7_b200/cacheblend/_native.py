@@ -49,6 +49,9 @@ SIGNATURES = {
     "cbk_silu_mul": (_i32, [_vp, _i64, _vp, _i64, _i64, _i32, _i32, _vp, _i64, _vp]),
     "cbk_scatter_rows": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _vp]),
     "cbk_gemv": (_i32, [_vp, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _vp]),
+    "cbk_decode_attn_workspace_bytes": (_sz, [_i64, _i32, _i32, _i32]),
+    "cbk_decode_attn": (_i32, [_vp, _vp, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _f32, _i32, _vp, _vp, _sz,
+                               _vp, _vp]),
 }
 
 

@@ -7,7 +7,7 @@ the fused row kernel, the projections as one-row GEMV kernels (q/k/v and
 gate/up over the stacked weights, SiLU * up formed inside the down
 projection's GEMV, lm_head), RoPE of the token's Q and K with its K/V written
 into cache row p (``rope_scatter`` with one index), and attention of the one
-query row over rows [0, p] (``partial_attn``).  Token 1 is the argmax of
+query row over rows [0, p] (``decode_attn``: split over the keys, HBM-bound).  Token 1 is the argmax of
 the last prefill row, as in the reference; decoding stops after
 ``max_new_tokens`` tokens or at ``eos_token_id``.
 """
@@ -37,7 +37,11 @@ class _DecodeState:
         self.token = first.view(1, 1).clone()
         self.pos = torch.full((1,), pre.S, dtype=torch.int64, device=device)
         self.base = pre.S - 1               # token t of the output was chosen at position base + t
-        self.ws = ops.attn_workspace(1, cap, geo.n_q, geo.n_kv, geo.head_dim, device)
+        # one-token attention kernel where it applies (head_dim 64/128, up to 8 q heads per
+        # KV head), else the selective-attention kernel with a one-row selection
+        self.one_row = geo.head_dim in (64, 128) and geo.n_q // geo.n_kv <= 8
+        self.ws = (ops.decode_workspace(cap, geo.n_q, geo.n_kv, geo.head_dim, device) if self.one_row
+                   else ops.attn_workspace(1, cap, geo.n_q, geo.n_kv, geo.head_dim, device))
 
 
 def _gemv_ok(w: torch.Tensor, x: torch.Tensor) -> bool:
@@ -91,9 +95,13 @@ def _decode_step(lw, pre, st: _DecodeState, status):
                                  pre.fused_k[li], pre.fused_v[li], status=status)
         # the whole capacity with the position as the causal bound: rows past pos are
         # invisible (and zero), so the call does not change from step to step
-        # the plan depends on the position only: made by the first layer, reused by the rest
-        a = ops.partial_attn(q_rot, pre.fused_k[li], pre.fused_v[li], st.pos, geo.n_q, geo.n_kv, geo.head_dim,
-                             geo.scaling, status=status, workspace=st.ws, reuse_plan=li > 0)
+        if st.one_row:
+            a = ops.decode_attn(q_rot, pre.fused_k[li], pre.fused_v[li], st.pos, geo.n_q, geo.n_kv, geo.head_dim,
+                                geo.scaling, st.ws, status=status)
+        else:
+            # the plan depends on the position only: made by the first layer, reused by the rest
+            a = ops.partial_attn(q_rot, pre.fused_k[li], pre.fused_v[li], st.pos, geo.n_q, geo.n_kv,
+                                 geo.head_dim, geo.scaling, status=status, workspace=st.ws, reuse_plan=li > 0)
         o = _lin1(attn.o_proj, a.unsqueeze(0))
         m = _mlp1(layer, _norm(layer.post_attention_layernorm, h, delta=o, sum_out=h, status=status), w_gu)
     row = _lin1(lw.model.lm_head, _norm(inner.norm, h, delta=m, status=status))[0, -1]

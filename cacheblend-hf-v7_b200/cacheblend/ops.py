@@ -414,6 +414,38 @@ def gemv(weight: torch.Tensor, x: torch.Tensor | None = None, gate: torch.Tensor
     return out
 
 
+def decode_workspace(cap: int, n_q_heads: int, n_kv_heads: int, head_dim: int, device) -> torch.Tensor:
+    """Zeroed workspace of decode_attn for a cache of `cap` rows (reusable across calls)."""
+    n = N.LIB.cbk_decode_attn_workspace_bytes(int(cap), n_q_heads, n_kv_heads, head_dim)
+    if n == 0:
+        raise ValueError("decode_workspace: bad geometry")
+    return torch.zeros((n,), dtype=torch.uint8, device=device)
+
+
+def decode_attn(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor,
+                n_q_heads: int, n_kv_heads: int, head_dim: int, scale: float, workspace: torch.Tensor,
+                out: torch.Tensor | None = None, status=None) -> torch.Tensor:
+    """Attention of one query token (q: [n_q_heads * head_dim], rotated) at the
+    device position pos (int64, one element) over cache rows 0..pos of
+    k_cache / v_cache ([cap][n_kv_heads * head_dim]); returns [1][n_q_heads * head_dim]."""
+    dev = require_cuda(q, k_cache, v_cache, pos, workspace)
+    if pos.dtype != torch.int64 or pos.numel() != 1:
+        raise ValueError("decode_attn: pos must be one int64 on the device")
+    if k_cache.shape != v_cache.shape or k_cache.stride() != v_cache.stride() or k_cache.stride(-1) != 1:
+        raise ValueError("decode_attn: k_cache and v_cache must have the same row layout")
+    qc = q.reshape(-1)
+    if not qc.is_contiguous():
+        qc = qc.contiguous()
+    if out is None:
+        out = torch.empty((1, n_q_heads * head_dim), dtype=q.dtype, device=dev)
+    with TIMES.span("decode_attn", dev):
+        N.check(N.LIB.cbk_decode_attn(_vp(qc), _vp(k_cache), _vp(v_cache), k_cache.stride(0), _vp(pos),
+                                      k_cache.shape[0], n_q_heads, n_kv_heads, head_dim, float(scale),
+                                      dtype_code(q.dtype), _vp(out), _vp(workspace), workspace.numel(),
+                                      _vp(status), _stream(dev)), "cbk_decode_attn")
+    return out
+
+
 def scatter_rows(src: torch.Tensor, idx: torch.Tensor, n_rows: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """Dense [n_rows][...] rows: out[idx[j]] = src[j], zeros elsewhere (idx ascending,
     distinct), every output byte written once."""

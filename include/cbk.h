@@ -216,6 +216,22 @@ int cbk_silu_mul(const void* gate, int64_t gate_stride, const void* up, int64_t 
 int cbk_gemv(const void* w, int64_t w_row_stride, const void* x, const void* gate, const void* up,
              int64_t n, int k, int dtype, void* y, void* stream);
 
+/* Attention of one query token at position *pos over cache rows 0..*pos (a
+ * greedy decode step, runners.py:106-152 through the HF attention with
+ * past_key_values): out[hq] = softmax(scale * q[hq] . K[j]) V[j] over j <= *pos
+ * for each q head hq (G = n_q_heads / n_kv_heads <= 8 heads per KV head).
+ * q, out: [n_q_heads][head_dim]; k_cache, v_cache: cap rows of kv_row_stride
+ * elements (>= n_kv_heads * head_dim, multiple of 8), head h at h * head_dim.
+ * *pos is read on the device (a captured graph stays valid as it advances); a
+ * *pos outside [0, cap) sets CBK_STATUS_BAD_INDEX and leaves out untouched.
+ * fp32 throughout, one rounding of the output.  head_dim 64 or 128.  The
+ * workspace (cbk_decode_attn_workspace_bytes) must be zeroed once before first
+ * use; the kernel leaves it reusable. */
+size_t cbk_decode_attn_workspace_bytes(int64_t cap, int n_q_heads, int n_kv_heads, int head_dim);
+int cbk_decode_attn(const void* q, const void* k_cache, const void* v_cache, int64_t kv_row_stride,
+                    const int64_t* pos, int64_t cap, int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                    int dtype, void* out, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Dense logits of the selected rows (fusor.py:483-491, the (1, S, vocab) zeros
  * plus index_copy_): dst[r] = src[j] for idx[j] == r, zero rows elsewhere, each
  * output byte written once.  idx: k int64 ascending distinct positions in

@@ -78,6 +78,13 @@ def test_abi_version_and_pure_helpers():
     ("cbk_gemv(16, 60, 16, None, None, 4, 64, 0, 16, None)", -1),
     ("cbk_gemv(16, 32768, 16, None, None, 4, 32768, 0, 16, None)", -1),
     ("cbk_gemv(16, 64, 16, None, None, 0, 64, 0, 16, None)", 0),
+    ("cbk_decode_attn(16, 16, 16, 1024, 16, 100, 32, 8, 128, 0.1, 2, 16, 16, 1 << 20, None, None)", -2),
+    ("cbk_decode_attn(16, 16, 16, 1024, 16, 100, 32, 8, 96, 0.1, 0, 16, 16, 1 << 20, None, None)", -2),
+    ("cbk_decode_attn(16, 16, 16, 1024, 16, 100, 32, 2, 128, 0.1, 0, 16, 16, 1 << 20, None, None)", -2),
+    ("cbk_decode_attn(16, 16, 16, 1000, 16, 100, 32, 8, 128, 0.1, 0, 16, 16, 1 << 20, None, None)", -1),
+    ("cbk_decode_attn(16, 16, 16, 1024, None, 100, 32, 8, 128, 0.1, 0, 16, 16, 1 << 20, None, None)", -1),
+    ("cbk_decode_attn(16, 24, 16, 1024, 16, 100, 32, 8, 128, 0.1, 0, 16, 16, 1 << 20, None, None)", -1),
+    ("cbk_decode_attn(16, 16, 16, 1024, 16, 100, 32, 8, 128, 0.1, 0, 16, 16, 64, None, None)", -4),
     ("cbk_scatter_rows(16, 64, 16, 2, None, 64, 4, 64, None)", -1),
     ("cbk_scatter_rows(16, 64, 16, 5, 16, 64, 4, 64, None)", -1),
     ("cbk_scatter_rows(16, 64, 16, 2, 16, 64, 4, 60, None)", -1),

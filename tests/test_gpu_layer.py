@@ -202,3 +202,47 @@ def test_gemv_with_silu_mul_input(dtype):
     fused = ops.gemv(w, gate=gu[..., :inter], up=gu[..., inter:])
     plain = ops.gemv(w, ops.silu_mul(gu[..., :inter], gu[..., inter:]))
     assert torch.equal(fused, plain)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hq,hkv,d,cap,p", [(32, 8, 128, 6240, 6208), (32, 8, 128, 6240, 0), (32, 8, 128, 6240, 255),
+                                           (32, 8, 128, 6240, 6239), (8, 8, 64, 700, 333), (16, 2, 128, 300, 299),
+                                           (12, 4, 64, 40000, 39001)])
+def test_decode_attn_one_token(dtype, hq, hkv, d, cap, p):
+    """decode_attn against an fp64 softmax attention of the same 16-bit inputs
+    over rows 0..p (rows past p hold garbage that must stay invisible)."""
+    from cacheblend import ops
+    g = torch.Generator(device=DEV).manual_seed(cap + p)
+    q = torch.randn((hq * d,), generator=g, device=DEV).to(dtype)
+    kc = torch.randn((cap, hkv * d), generator=g, device=DEV).to(dtype)
+    vc = torch.randn((cap, hkv * d), generator=g, device=DEV).to(dtype)
+    pos = torch.tensor([p], dtype=torch.int64, device=DEV)
+    ws = ops.decode_workspace(cap, hq, hkv, d, DEV)
+    scale = d ** -0.5
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for _ in range(2):                       # the workspace is reusable
+        out = ops.decode_attn(q, kc, vc, pos, hq, hkv, d, scale, ws, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    G = hq // hkv
+    qh = q.double().view(hq, d)
+    k = kc[: p + 1].double().view(p + 1, hkv, d)
+    v = vc[: p + 1].double().view(p + 1, hkv, d)
+    kk = k[:, torch.arange(hq, device=DEV) // G]          # (p+1, hq, d)
+    vv = v[:, torch.arange(hq, device=DEV) // G]
+    w = torch.softmax(torch.einsum("hd,jhd->hj", qh, kk) * scale, dim=-1)
+    ref = torch.einsum("hj,jhd->hd", w, vv).reshape(1, -1)
+    err = (out.double() - ref).abs()
+    assert err.max().item() < 2e-2 and err.mean().item() < 2e-3, (err.max().item(), err.mean().item())
+
+
+def test_decode_attn_bad_position_reported():
+    from cacheblend import _native as N, ops
+    q = torch.randn((32 * 128,), device=DEV).to(torch.bfloat16)
+    kc = torch.randn((100, 8 * 128), device=DEV).to(torch.bfloat16)
+    ws = ops.decode_workspace(100, 32, 8, 128, DEV)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = torch.zeros((1, 32 * 128), device=DEV, dtype=torch.bfloat16)
+    ops.decode_attn(q, kc, kc, torch.tensor([100], device=DEV), 32, 8, 128, 0.1, ws, out=out, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) & N.CBK_STATUS_BAD_INDEX and torch.all(out == 0)
