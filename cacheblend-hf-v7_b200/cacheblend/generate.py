@@ -37,9 +37,9 @@ class _DecodeState:
         self.token = first.view(1, 1).clone()
         self.pos = torch.full((1,), pre.S, dtype=torch.int64, device=device)
         self.base = pre.S - 1               # token t of the output was chosen at position base + t
-        # one-token attention kernel where it applies (head_dim 64/128, up to 8 q heads per
-        # KV head), else the selective-attention kernel with a one-row selection
-        self.one_row = geo.head_dim in (64, 128) and geo.n_q // geo.n_kv <= 8
+        # one-token attention kernel where it applies (head_dim 64/128, 1, 2, 4 or 8 q heads
+        # per KV head), else the selective-attention kernel with a one-row selection
+        self.one_row = geo.head_dim in (64, 128) and geo.n_q // geo.n_kv in (1, 2, 4, 8)
         self.ws = (ops.decode_workspace(cap, geo.n_q, geo.n_kv, geo.head_dim, device) if self.one_row
                    else ops.attn_workspace(1, cap, geo.n_q, geo.n_kv, geo.head_dim, device))
 

@@ -219,7 +219,7 @@ int cbk_gemv(const void* w, int64_t w_row_stride, const void* x, const void* gat
 /* Attention of one query token at position *pos over cache rows 0..*pos (a
  * greedy decode step, runners.py:106-152 through the HF attention with
  * past_key_values): out[hq] = softmax(scale * q[hq] . K[j]) V[j] over j <= *pos
- * for each q head hq (G = n_q_heads / n_kv_heads <= 8 heads per KV head).
+ * for each q head hq (G = n_q_heads / n_kv_heads in {1, 2, 4, 8} heads per KV head).
  * q, out: [n_q_heads][head_dim]; k_cache, v_cache: cap rows of kv_row_stride
  * elements (>= n_kv_heads * head_dim, multiple of 8), head h at h * head_dim.
  * *pos is read on the device (a captured graph stays valid as it advances); a

@@ -207,7 +207,8 @@ def test_gemv_with_silu_mul_input(dtype):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("hq,hkv,d,cap,p", [(32, 8, 128, 6240, 6208), (32, 8, 128, 6240, 0), (32, 8, 128, 6240, 255),
                                            (32, 8, 128, 6240, 6239), (8, 8, 64, 700, 333), (16, 2, 128, 300, 299),
-                                           (12, 4, 64, 40000, 39001)])
+                                           (16, 4, 64, 40000, 39001), (8, 4, 128, 5000, 4097),
+                                           (32, 4, 128, 131328, 131071)])
 def test_decode_attn_one_token(dtype, hq, hkv, d, cap, p):
     """decode_attn against an fp64 softmax attention of the same 16-bit inputs
     over rows 0..p (rows past p hold garbage that must stay invisible)."""
@@ -225,13 +226,11 @@ def test_decode_attn_one_token(dtype, hq, hkv, d, cap, p):
     torch.cuda.synchronize()
     assert int(st.item()) == 0
     G = hq // hkv
-    qh = q.double().view(hq, d)
+    qh = q.double().view(hkv, G, d)                       # q head hq = kv head hq // G
     k = kc[: p + 1].double().view(p + 1, hkv, d)
     v = vc[: p + 1].double().view(p + 1, hkv, d)
-    kk = k[:, torch.arange(hq, device=DEV) // G]          # (p+1, hq, d)
-    vv = v[:, torch.arange(hq, device=DEV) // G]
-    w = torch.softmax(torch.einsum("hd,jhd->hj", qh, kk) * scale, dim=-1)
-    ref = torch.einsum("hj,jhd->hd", w, vv).reshape(1, -1)
+    w = torch.softmax(torch.einsum("kgd,jkd->kgj", qh, k) * scale, dim=-1)
+    ref = torch.einsum("kgj,jkd->kgd", w, v).reshape(1, -1)
     err = (out.double() - ref).abs()
     assert err.max().item() < 2e-2 and err.mean().item() < 2e-3, (err.max().item(), err.mean().item())
 
