@@ -415,7 +415,8 @@ def gemv(weight: torch.Tensor, x: torch.Tensor | None = None, gate: torch.Tensor
 
 
 def decode_workspace(cap: int, n_q_heads: int, n_kv_heads: int, head_dim: int, device) -> torch.Tensor:
-    """Zeroed workspace of decode_attn for a cache of `cap` rows (reusable across calls)."""
+    """Workspace of decode_attn for a cache of `cap` rows (per-split partial
+    results; reusable by calls that do not overlap on the GPU)."""
     n = N.LIB.cbk_decode_attn_workspace_bytes(int(cap), n_q_heads, n_kv_heads, head_dim)
     if n == 0:
         raise ValueError("decode_workspace: bad geometry")

@@ -4,19 +4,21 @@
 // head, keys 0..p of the cache rows, p read from device memory so that a
 // captured decode step stays valid as the position advances.
 //
-// HBM-bound: every visible K/V byte is read once.  Grid (split, KV head); a CTA
-// of eight warps takes a contiguous split of the keys (256, one 32-key pass per
-// warp, while there are at most 64 splits) for the G q heads of its KV head.
-// A pass: scores with one key per lane (the key row loaded in two halves; the G
-// query rows, pre-scaled by scale * log2 e, sit in shared memory and are read
-// as broadcasts), the first V rows issued, an online softmax per head across
-// the warp, then P V with HD/32 head dimensions per lane and each key's weight
-// broadcast by a shuffle (all 32 V rows issued before the softmax).  The warps
-// merge through shared memory; the CTAs of a KV head merge without waiting:
-// each stores its partial (running max, row sum, O) and counts, and the CTA
-// that counts last merges them all (weights for every split staged in shared
-// memory, then each output summed over the splits in increasing order, 16
-// splits' loads in flight) and resets the counter.  fp32 throughout, output
+// HBM-bound: every visible K/V byte is read once.  Grid (split, KV head),
+// about two CTAs per SM; a CTA of four warps takes a contiguous split of the
+// keys for the G q heads of its KV head, each warp 32 keys per pass.  A pass
+// copies its 32 K rows and 32 V rows into shared memory with cp.async, 16
+// lanes per row and every copy in flight at once; scores are computed one key
+// per lane (K rows padded by 16 bytes so these reads do not conflict; the G
+// query rows, pre-scaled by scale * log2 e, are read as broadcasts), then an
+// online softmax per head across the warp and P V with HD/32 head dimensions
+// per lane, each key's weight broadcast by a shuffle.  The warps merge through
+// shared memory into the split's partial (running max, row sum, O), and a
+// second small kernel merges the splits (one CTA per q head, one thread per
+// head dimension, every split's load in flight): a merge inside the first
+// kernel by its last CTA measured slower (22.3 us against 17.9 us for the two
+// kernels at 32 q / 8 KV heads and 6209 keys), as a handful of CTAs then
+// finished the launch alone.  fp32 throughout, output
 // rounded once.
 #include <algorithm>
 #include <type_traits>
@@ -25,54 +27,72 @@
 
 namespace cbk {
 
-constexpr int kDecThreads = 256;
+int sm_count_layer();   // cbk_layer.cu
+int ensure_smem_attr(const void* func, int bytes);   // cbk_api.cu
+
+constexpr int kDecThreads = 128;
 constexpr int kDecWarps = kDecThreads / 32;
-constexpr int kDecMaxG = 8;
 constexpr int kDecMaxSplits = 64;
-constexpr int kDecSplit = kDecWarps * 32;   // keys per CTA pass: one 32-key pass per warp
+constexpr int kDecPass = 32;                 // keys per warp pass
+constexpr int kDecCtaKeys = kDecWarps * kDecPass;
 
 struct DecLayout {
   int n_splits, split_len;
-  size_t off_ml, off_o, off_cnt, bytes;
+  size_t off_ml, off_o, bytes;
 };
 
 static size_t dec_align(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-// splits of kDecSplit keys (one pass per warp) while they number <= kDecMaxSplits,
-// longer splits (several passes per warp) beyond
-static DecLayout dec_layout(int64_t cap, int n_kv_heads, int G, int head_dim) {
+// Workspace sized for kDecMaxSplits splits (independent of the device); the
+// split count fills one wave of two CTAs per SM: about 2 * SMs / n_kv_heads
+// splits (fewer when the cache is short), each a multiple of 32 keys.
+static DecLayout dec_layout(int64_t cap, int n_kv_heads, int G, int head_dim, int sms) {
   DecLayout d;
-  const int64_t want = (cap + kDecSplit - 1) / kDecSplit;
-  d.n_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, kDecMaxSplits)));
+  const int64_t by_keys = (cap + kDecCtaKeys - 1) / kDecCtaKeys;
+  const int64_t by_sms = std::max<int64_t>(1, 2LL * sms / n_kv_heads);
+  d.n_splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({by_keys, by_sms, kDecMaxSplits})));
   const int64_t per = (cap + d.n_splits - 1) / d.n_splits;
-  d.split_len = static_cast<int>((per + kDecSplit - 1) / kDecSplit * kDecSplit);
-  const size_t parts = static_cast<size_t>(n_kv_heads) * d.n_splits * G;
+  d.split_len = static_cast<int>((per + kDecPass - 1) / kDecPass * kDecPass);
+  const size_t parts = static_cast<size_t>(n_kv_heads) * kDecMaxSplits * G;
   d.off_ml = 0;
   d.off_o = dec_align(parts * sizeof(float2));
-  d.off_cnt = d.off_o + dec_align(parts * head_dim * sizeof(float));
-  d.bytes = d.off_cnt + dec_align(static_cast<size_t>(n_kv_heads) * sizeof(int));
+  d.bytes = d.off_o + dec_align(parts * head_dim * sizeof(float));
   return d;
+}
+
+// dynamic shared memory: per warp a K tile (32 rows, pitch HD + 8 elements so
+// that one key per lane reads without bank conflicts) and a V tile (32 rows)
+template <int HD>
+struct DecSmem {
+  static constexpr int kKPitch = HD + 8;
+  static constexpr int kKTile = kDecPass * kKPitch;     // elements
+  static constexpr int kVTile = kDecPass * HD;
+  static constexpr int kBytes = kDecWarps * (kKTile + kVTile) * 2;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 template <int DT, int HD, int G>
 __global__ void __launch_bounds__(kDecThreads, 2)
 decode_attn_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
                    const uint16_t* __restrict__ vc, int64_t kv_stride, const int64_t* __restrict__ pos,
-                   int64_t cap, float scale_log2, int split_len, float2* part_ml, float* part_o, int* cnt,
-                   uint16_t* __restrict__ out, int32_t* status) {
+                   int64_t cap, float scale_log2, int split_len, float2* part_ml, float* part_o,
+                   int32_t* status) {
   using E = Elem<DT>;
+  using SM = DecSmem<HD>;
   constexpr int kDimLane = HD / 32;                  // head dimensions per lane in P V
-  constexpr int kKPart = 4;                          // 16-byte vectors of the key row per load batch
-  constexpr int kKParts = HD / 8 / kKPart;
+  constexpr int kVecRow = HD / 8;                    // 16-byte pieces of a row
   using VRaw = typename std::conditional<kDimLane == 4, uint2, uint32_t>::type;
+  extern __shared__ __align__(16) uint16_t s_kv[];
   __shared__ __align__(16) float s_q[G][HD];
   __shared__ float s_m[kDecWarps][G], s_l[kDecWarps][G];
   __shared__ __align__(16) float s_o[kDecWarps][G][HD];
-  __shared__ float2 s_ml[kDecMaxSplits][G];
-  __shared__ float s_w[kDecMaxSplits][G];
-  __shared__ float s_L[G];
-  __shared__ int s_last;
-  const int h = blockIdx.y, split = blockIdx.x, n_splits = gridDim.x;
+  const int h = blockIdx.y, split = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t p = *pos;
   if (p < 0 || p >= cap) {                           // nothing visible: reported, output left alone
@@ -84,6 +104,8 @@ decode_attn_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ 
     s_q[i / HD][i % HD] = E::to_f(q[(static_cast<int64_t>(h) * G + i / HD) * HD + i % HD]) * scale_log2;
   __syncthreads();
 
+  uint16_t* sk = s_kv + warp * SM::kKTile;
+  uint16_t* sv = s_kv + kDecWarps * SM::kKTile + warp * SM::kVTile;
   float m[G], l[G], o[G][kDimLane];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -95,50 +117,52 @@ decode_attn_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ 
   const int64_t k0 = static_cast<int64_t>(split) * split_len;
   const int64_t k1 = std::min<int64_t>(k0 + split_len, n_keys);
   const uint16_t* kh = kc + static_cast<int64_t>(h) * HD;
-  const uint16_t* vh = vc + static_cast<int64_t>(h) * HD + lane * kDimLane;
-  for (int64_t c = k0 + warp * 32; c < k1; c += kDecWarps * 32) {
-    // scores, one key per lane, the key row in parts of kKPart vectors
-    const int64_t key = c + lane;
-    const bool valid = key < k1;
+  const uint16_t* vh = vc + static_cast<int64_t>(h) * HD;
+  for (int64_t c = k0 + warp * kDecPass; c < k1; c += kDecWarps * kDecPass) {
+    const int nk = static_cast<int>(std::min<int64_t>(kDecPass, k1 - c));
+    // the pass's K and V rows into shared memory, every copy in flight at once
+    // (16 lanes per row: coalesced)
+    __syncwarp();                                    // the previous pass is done with the tiles
+#pragma unroll
+    for (int i = 0; i < kDecPass * kVecRow / 32; ++i) {
+      const int idx = lane + 32 * i;
+      const int r = idx / kVecRow, v = idx % kVecRow;
+      if (r < nk) {
+        cp_async16(sk + r * SM::kKPitch + v * 8, kh + (c + r) * kv_stride + v * 8);
+        cp_async16(sv + r * HD + v * 8, vh + (c + r) * kv_stride + v * 8);
+      }
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    // scores, one key per lane
+    const bool valid = lane < nk;
     float s[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) s[g] = 0.f;
     if (valid) {
-      const uint16_t* kr = kh + key * kv_stride;
+      const uint16_t* kr = sk + lane * SM::kKPitch;
+#pragma unroll 4
+      for (int v = 0; v < kVecRow; ++v) {
+        const uint4 kv4 = *reinterpret_cast<const uint4*>(kr + v * 8);
+        const uint16_t* hk = reinterpret_cast<const uint16_t*>(&kv4);
+        float kf[8];
 #pragma unroll
-      for (int part = 0; part < kKParts; ++part) {
-        uint4 kv4[kKPart];
+        for (int e = 0; e < 8; ++e) kf[e] = E::to_f(hk[e]);
 #pragma unroll
-        for (int v = 0; v < kKPart; ++v) kv4[v] = ld_vec(kr + (part * kKPart + v) * 8);
-#pragma unroll
-        for (int v = 0; v < kKPart; ++v) {
-          const int e0 = (part * kKPart + v) * 8;
-          const uint16_t* hk = reinterpret_cast<const uint16_t*>(&kv4[v]);
-          float kf[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) kf[e] = E::to_f(hk[e]);
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const float4 qa = *reinterpret_cast<const float4*>(&s_q[g][e0]);
-            const float4 qb = *reinterpret_cast<const float4*>(&s_q[g][e0 + 4]);
-            s[g] = fmaf(qa.x, kf[0], s[g]);
-            s[g] = fmaf(qa.y, kf[1], s[g]);
-            s[g] = fmaf(qa.z, kf[2], s[g]);
-            s[g] = fmaf(qa.w, kf[3], s[g]);
-            s[g] = fmaf(qb.x, kf[4], s[g]);
-            s[g] = fmaf(qb.y, kf[5], s[g]);
-            s[g] = fmaf(qb.z, kf[6], s[g]);
-            s[g] = fmaf(qb.w, kf[7], s[g]);
-          }
+        for (int g = 0; g < G; ++g) {
+          const float4 qa = *reinterpret_cast<const float4*>(&s_q[g][v * 8]);
+          const float4 qb = *reinterpret_cast<const float4*>(&s_q[g][v * 8 + 4]);
+          s[g] = fmaf(qa.x, kf[0], s[g]);
+          s[g] = fmaf(qa.y, kf[1], s[g]);
+          s[g] = fmaf(qa.z, kf[2], s[g]);
+          s[g] = fmaf(qa.w, kf[3], s[g]);
+          s[g] = fmaf(qb.x, kf[4], s[g]);
+          s[g] = fmaf(qb.y, kf[5], s[g]);
+          s[g] = fmaf(qb.z, kf[6], s[g]);
+          s[g] = fmaf(qb.w, kf[7], s[g]);
         }
       }
     }
-    const int nk = static_cast<int>(std::min<int64_t>(32, k1 - c));
-    constexpr int kVBatch = 8;
-    VRaw raw[kVBatch];
-#pragma unroll
-    for (int jj = 0; jj < kVBatch; ++jj)
-      if (jj < nk) raw[jj] = *reinterpret_cast<const VRaw*>(vh + (c + jj) * kv_stride);
     // online softmax per head (lane 0's key is valid, so every max is finite)
     float pw[G];
 #pragma unroll
@@ -157,31 +181,19 @@ decode_attn_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ 
 #pragma unroll
       for (int d = 0; d < kDimLane; ++d) o[g][d] *= alpha;
     }
+    // P V, keys in order, kDimLane dimensions per lane from the V tile
+#pragma unroll 8
+    for (int j = 0; j < nk; ++j) {
+      const VRaw raw = *reinterpret_cast<const VRaw*>(sv + j * HD + lane * kDimLane);
+      const uint16_t* hv = reinterpret_cast<const uint16_t*>(&raw);
+      float vf[kDimLane];
 #pragma unroll
-    for (int j0 = 0; j0 < 32; j0 += kVBatch) {
-      if (j0 >= nk) break;
-      VRaw cur[kVBatch];
+      for (int d = 0; d < kDimLane; ++d) vf[d] = E::to_f(hv[d]);
 #pragma unroll
-      for (int jj = 0; jj < kVBatch; ++jj) cur[jj] = raw[jj];
-      if (j0 + kVBatch < 32) {
+      for (int g = 0; g < G; ++g) {
+        const float pj = __shfl_sync(0xffffffffu, pw[g], j);
 #pragma unroll
-        for (int jj = 0; jj < kVBatch; ++jj)
-          if (j0 + kVBatch + jj < nk)
-            raw[jj] = *reinterpret_cast<const VRaw*>(vh + (c + j0 + kVBatch + jj) * kv_stride);
-      }
-#pragma unroll
-      for (int jj = 0; jj < kVBatch; ++jj) {
-        if (j0 + jj >= nk) break;
-        const uint16_t* hv = reinterpret_cast<const uint16_t*>(&cur[jj]);
-        float vf[kDimLane];
-#pragma unroll
-        for (int d = 0; d < kDimLane; ++d) vf[d] = E::to_f(hv[d]);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float pj = __shfl_sync(0xffffffffu, pw[g], j0 + jj);
-#pragma unroll
-          for (int d = 0; d < kDimLane; ++d) o[g][d] = fmaf(pj, vf[d], o[g][d]);
-        }
+        for (int d = 0; d < kDimLane; ++d) o[g][d] = fmaf(pj, vf[d], o[g][d]);
       }
     }
   }
@@ -209,53 +221,57 @@ decode_attn_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ 
       L += wt * s_l[w][g];
       acc += wt * s_o[w][g][d];
     }
-    const int64_t part = (static_cast<int64_t>(h) * n_splits + split) * G + g;
+    const int64_t part = (static_cast<int64_t>(h) * kDecMaxSplits + split) * G + g;
     part_o[part * HD + d] = acc;                     // O un-normalised, relative to M
     if (d == 0) part_ml[part] = make_float2(M, L);
   }
-  // the CTA that counts last for this KV head merges every split
-  __threadfence();
+}
+
+// Merge of the splits, one CTA per (KV head, q head of its group), one thread
+// per head dimension: O = sum_s w_s O_s / sum_s w_s l_s, w_s = 2^(m_s - M)
+// over splits with visible keys, every split's load in flight at once, sums
+// in increasing split order.
+template <int DT, int HD>
+__global__ void __launch_bounds__(HD)
+decode_merge_kernel(const float2* __restrict__ part_ml, const float* __restrict__ part_o, int G, int n_splits,
+                    const int64_t* __restrict__ pos, int64_t cap, uint16_t* __restrict__ out) {
+  using E = Elem<DT>;
+  __shared__ float s_w[kDecMaxSplits], s_l[kDecMaxSplits];
+  __shared__ float s_M, s_L;
+  const int h = blockIdx.x / G, g = blockIdx.x % G, d = threadIdx.x;
+  const int64_t p = *pos;
+  if (p < 0 || p >= cap) return;                     // reported by the attention kernel
+  const int64_t base = (static_cast<int64_t>(h) * kDecMaxSplits) * G + g;   // split s at base + s * G
+  float x[kDecMaxSplits];
+#pragma unroll
+  for (int sp = 0; sp < kDecMaxSplits; ++sp)
+    x[sp] = sp < n_splits ? part_o[(base + static_cast<int64_t>(sp) * G) * HD + d] : 0.f;
+  if (d < n_splits) {
+    const float2 ml = part_ml[base + static_cast<int64_t>(d) * G];
+    s_w[d] = ml.x;
+    s_l[d] = ml.y;
+  }
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&cnt[h], 1) == n_splits - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  if (tid == 0) cnt[h] = 0;                          // ready for the next call
-  const int64_t base = static_cast<int64_t>(h) * n_splits * G;
-  for (int i = tid; i < n_splits * G; i += kDecThreads) s_ml[i / G][i % G] = __ldcg(&part_ml[base + i]);
-  __syncthreads();
-  if (tid < G) {
-    const int g = tid;
+  if (d == 0) {
     float M = -INFINITY;
     for (int sp = 0; sp < n_splits; ++sp)
-      if (s_ml[sp][g].y > 0.f) M = fmaxf(M, s_ml[sp][g].x);
-    float L = 0.f;
-    for (int sp = 0; sp < n_splits; ++sp) {
-      const float wt = s_ml[sp][g].y > 0.f ? ex2(s_ml[sp][g].x - M) : 0.f;
-      s_w[sp][g] = wt;
-      L += wt * s_ml[sp][g].y;
-    }
-    s_L[g] = L;
+      if (s_l[sp] > 0.f) M = fmaxf(M, s_w[sp]);
+    s_M = M;
   }
   __syncthreads();
-  // each output summed over the splits, kSpBatch splits' loads in flight
-  constexpr int kSpBatch = 16;
-#pragma unroll 1
-  for (int i = tid; i < G * HD; i += kDecThreads) {
-    const int g = i / HD, d = i % HD;
-    const float* po = part_o + (base + g) * HD + d;  // split sp at po[sp * G * HD]
-    float acc = 0.f;
-    for (int sp0 = 0; sp0 < n_splits; sp0 += kSpBatch) {
-      float x[kSpBatch];
-#pragma unroll
-      for (int u = 0; u < kSpBatch; ++u)
-        x[u] = sp0 + u < n_splits ? __ldcg(po + static_cast<int64_t>(sp0 + u) * G * HD) : 0.f;
-#pragma unroll
-      for (int u = 0; u < kSpBatch; ++u)
-        if (sp0 + u < n_splits) acc = fmaf(s_w[sp0 + u][g], x[u], acc);
-    }
-    out[(static_cast<int64_t>(h) * G + g) * HD + d] = E::from_f(acc / s_L[g]);
+  if (d < n_splits) s_w[d] = s_l[d] > 0.f ? ex2(s_w[d] - s_M) : 0.f;
+  __syncthreads();
+  if (d == 0) {
+    float L = 0.f;
+    for (int sp = 0; sp < n_splits; ++sp) L += s_w[sp] * s_l[sp];
+    s_L = L;
   }
+  __syncthreads();
+  float acc = 0.f;
+#pragma unroll
+  for (int sp = 0; sp < kDecMaxSplits; ++sp)
+    if (sp < n_splits) acc = fmaf(s_w[sp], x[sp], acc);
+  out[(static_cast<int64_t>(h) * G + g) * HD + d] = E::from_f(acc / s_L);
 }
 
 }  // namespace cbk
@@ -264,7 +280,7 @@ using namespace cbk;
 
 extern "C" size_t cbk_decode_attn_workspace_bytes(int64_t cap, int n_q_heads, int n_kv_heads, int head_dim) {
   if (cap <= 0 || n_kv_heads <= 0 || n_q_heads <= 0 || n_q_heads % n_kv_heads != 0) return 0;
-  return dec_layout(cap, n_kv_heads, n_q_heads / n_kv_heads, head_dim).bytes;
+  return dec_layout(cap, n_kv_heads, n_q_heads / n_kv_heads, head_dim, sm_count_layer()).bytes;
 }
 
 extern "C" int cbk_decode_attn(const void* q, const void* k_cache, const void* v_cache, int64_t kv_row_stride,
@@ -291,13 +307,12 @@ extern "C" int cbk_decode_attn(const void* q, const void* k_cache, const void* v
        reinterpret_cast<uintptr_t>(workspace)) & 15u)
     return set_error(CBK_ERR_INVALID, "cbk_decode_attn: caches and workspace must be 16-byte aligned");
   const int G = n_q_heads / n_kv_heads;
-  const DecLayout lay = dec_layout(cap, n_kv_heads, G, head_dim);
+  const DecLayout lay = dec_layout(cap, n_kv_heads, G, head_dim, sm_count_layer());
   if (workspace_bytes < lay.bytes)
     return set_error(CBK_ERR_WORKSPACE, "cbk_decode_attn: workspace %zu < %zu bytes", workspace_bytes, lay.bytes);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   auto ml = reinterpret_cast<float2*>(ws + lay.off_ml);
   auto po = reinterpret_cast<float*>(ws + lay.off_o);
-  auto cnt = reinterpret_cast<int*>(ws + lay.off_cnt);
   const dim3 grid(lay.n_splits, n_kv_heads);
   auto st = static_cast<cudaStream_t>(stream);
   const float sl2 = scale * 1.4426950408889634f;
@@ -306,8 +321,13 @@ extern "C" int cbk_decode_attn(const void* q, const void* k_cache, const void* v
   auto vp = static_cast<const uint16_t*>(v_cache);
   auto op = static_cast<uint16_t*>(out);
 #define CBK_DEC3(DT, HD, GG)                                                                            \
-  decode_attn_kernel<DT, HD, GG><<<grid, kDecThreads, 0, st>>>(qp, kp, vp, kv_row_stride, pos, cap, sl2,   \
-                                                              lay.split_len, ml, po, cnt, op, status)
+  do {                                                                                                  \
+    auto kern = decode_attn_kernel<DT, HD, GG>;                                                         \
+    if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), DecSmem<HD>::kBytes)) return rc; \
+    kern<<<grid, kDecThreads, DecSmem<HD>::kBytes, st>>>(qp, kp, vp, kv_row_stride, pos, cap, sl2,       \
+                                                        lay.split_len, ml, po, status);                 \
+    decode_merge_kernel<DT, HD><<<n_kv_heads * GG, HD, 0, st>>>(ml, po, GG, lay.n_splits, pos, cap, op);  \
+  } while (0)
 #define CBK_DEC(DT, HD)                                                                                 \
   switch (G) {                                                                                          \
     case 1: CBK_DEC3(DT, HD, 1); break;                                                                 \

@@ -225,8 +225,9 @@ int cbk_gemv(const void* w, int64_t w_row_stride, const void* x, const void* gat
  * *pos is read on the device (a captured graph stays valid as it advances); a
  * *pos outside [0, cap) sets CBK_STATUS_BAD_INDEX and leaves out untouched.
  * fp32 throughout, one rounding of the output.  head_dim 64 or 128.  The
- * workspace (cbk_decode_attn_workspace_bytes) must be zeroed once before first
- * use; the kernel leaves it reusable. */
+ * workspace (cbk_decode_attn_workspace_bytes) holds the per-split partial
+ * results between the two kernels of a call; it needs no initialisation, and
+ * calls that overlap on the GPU must not share it. */
 size_t cbk_decode_attn_workspace_bytes(int64_t cap, int n_q_heads, int n_kv_heads, int head_dim);
 int cbk_decode_attn(const void* q, const void* k_cache, const void* v_cache, int64_t kv_row_stride,
                     const int64_t* pos, int64_t cap, int n_q_heads, int n_kv_heads, int head_dim, float scale,
