@@ -130,9 +130,9 @@ __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, int64_t g_stride
 
 // One-row projection (a decode step): y[n] = round16(sum_k W[n][k] x[k]) in
 // fp32, W row-major [N][K].  HBM-bound, every weight byte read once: a warp
-// owns one output row at a time and each lane keeps kGemvVecs 16-byte weight
-// loads in flight (issued before any arithmetic); x is staged once per CTA in
-// shared memory.  With gate/up given, x[k] = round16(round16(silu(gate[k])) *
+// owns one output row at a time, each lane with kGemvVecs 16-byte weight loads
+// of the next step in flight while it sums the current one (the first ones
+// issued before x is staged); x is staged once per CTA in shared memory.  With gate/up given, x[k] = round16(round16(silu(gate[k])) *
 // up[k]) is formed while staging (silu_mul's arithmetic), so the MLP's down
 // projection needs no separate activation launch.
 constexpr int kGemvThreads = 256;
@@ -140,13 +140,29 @@ constexpr int kGemvVecs = 8;
 constexpr int kGemvMaxK = 16384;      // x in shared memory: K * 2 bytes <= 32 KB
 
 template <int DT>
-__global__ void __launch_bounds__(kGemvThreads)
+__global__ void __launch_bounds__(kGemvThreads, 2)
 gemv_kernel(const uint16_t* __restrict__ w, int64_t w_stride, const uint16_t* __restrict__ x,
             const uint16_t* __restrict__ gate, const uint16_t* __restrict__ up, int K, int64_t N,
             uint16_t* __restrict__ y) {
   using E = Elem<DT>;
   __shared__ uint4 s_x[kGemvMaxK / 8];
   const int kv = K / 8;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kGemvThreads / 32);
+  const int batches = (kv + 32 * kGemvVecs - 1) / (32 * kGemvVecs);    // weight batches per row
+  // a warp's steps are (row, batch) pairs, rows grid-strided; the next step's
+  // weights are loaded while the current step is summed
+  auto load = [&](uint4 (&wv)[kGemvVecs], int64_t row, int bt) {
+    const uint16_t* wr = w + row * w_stride;
+    const int v0 = bt * 32 * kGemvVecs + lane;
+#pragma unroll
+    for (int u = 0; u < kGemvVecs; ++u)
+      if (v0 + 32 * u < kv) wv[u] = ld_stream(wr + (v0 + 32 * u) * 8);
+  };
+  int64_t n = static_cast<int64_t>(blockIdx.x) * (kGemvThreads / 32) + (threadIdx.x >> 5);
+  int bt = 0;
+  uint4 cur[kGemvVecs];
+  if (n < N) load(cur, n, 0);                      // in flight while x is staged
   for (int i = threadIdx.x; i < kv; i += kGemvThreads) {
     if (gate) {
       const uint4 a = ld_vec(gate + i * 8), b = ld_vec(up + i * 8);
@@ -166,34 +182,40 @@ gemv_kernel(const uint16_t* __restrict__ w, int64_t w_stride, const uint16_t* __
     }
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kGemvThreads / 32);
-  for (int64_t n = static_cast<int64_t>(blockIdx.x) * (kGemvThreads / 32) + (threadIdx.x >> 5); n < N;
-       n += warps) {
-    const uint16_t* wr = w + n * w_stride;
-    float acc0 = 0.f, acc1 = 0.f;
-    for (int v0 = lane; v0 < kv; v0 += 32 * kGemvVecs) {
-      uint4 wv[kGemvVecs];
+  float acc0 = 0.f, acc1 = 0.f;
+  while (n < N) {
+    int64_t n2 = n;
+    int bt2 = bt + 1;
+    if (bt2 == batches) {
+      bt2 = 0;
+      n2 = n + warps;
+    }
+    uint4 nxt[kGemvVecs];
+    if (n2 < N) load(nxt, n2, bt2);
+    const int v0 = bt * 32 * kGemvVecs + lane;
 #pragma unroll
-      for (int u = 0; u < kGemvVecs; ++u)
-        if (v0 + 32 * u < kv) wv[u] = ld_stream(wr + (v0 + 32 * u) * 8);
+    for (int u = 0; u < kGemvVecs; ++u) {
+      if (v0 + 32 * u >= kv) break;
+      const uint4 xv = s_x[v0 + 32 * u];
+      const uint16_t* hw = reinterpret_cast<const uint16_t*>(&cur[u]);
+      const uint16_t* hx = reinterpret_cast<const uint16_t*>(&xv);
 #pragma unroll
-      for (int u = 0; u < kGemvVecs; ++u) {
-        if (v0 + 32 * u >= kv) break;
-        const uint4 xv = s_x[v0 + 32 * u];
-        const uint16_t* hw = reinterpret_cast<const uint16_t*>(&wv[u]);
-        const uint16_t* hx = reinterpret_cast<const uint16_t*>(&xv);
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          acc0 = fmaf(E::to_f(hw[e]), E::to_f(hx[e]), acc0);
-          acc1 = fmaf(E::to_f(hw[e + 1]), E::to_f(hx[e + 1]), acc1);
-        }
+      for (int e = 0; e < 8; e += 2) {
+        acc0 = fmaf(E::to_f(hw[e]), E::to_f(hx[e]), acc0);
+        acc1 = fmaf(E::to_f(hw[e + 1]), E::to_f(hx[e + 1]), acc1);
       }
     }
-    float acc = acc0 + acc1;
+    if (bt2 == 0) {                                // row n complete
+      float acc = acc0 + acc1;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) y[n] = E::from_f(acc);
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) y[n] = E::from_f(acc);
+      acc0 = acc1 = 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kGemvVecs; ++u) cur[u] = nxt[u];
+    n = n2;
+    bt = bt2;
   }
 }
 
@@ -350,7 +372,9 @@ extern "C" int cbk_gemv(const void* w, int64_t w_row_stride, const void* x, cons
   if (n == 0) return CBK_OK;
   auto st = static_cast<cudaStream_t>(stream);
   const int64_t want = (n + kGemvThreads / 32 - 1) / (kGemvThreads / 32);
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(want, 16LL * sm_count_layer()));
+  // two CTAs per SM (one where every CTA stages SiLU * up over all of k): each
+  // warp then walks several rows with its next weights always in flight
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(want, (gate ? 1LL : 2LL) * sm_count_layer()));
   auto wp = static_cast<const uint16_t*>(w);
   auto xp = static_cast<const uint16_t*>(x);
   auto gp = static_cast<const uint16_t*>(gate);
