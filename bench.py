@@ -659,6 +659,103 @@ def run_kv_microbench(args):
         "kernels": out, "hbm_peak_gbs": hbm, "hbm_peak_kind": src, "clocks": clk}), flush=True)
 
 
+def run_decode_kernels(args):
+    """One decode step's kernels at Mistral-7B shapes (7K blended cache), each
+    timed as a CUDA-graph replay of a batch of launches over distinct buffers
+    larger than L2: decode_attn over 32 layer caches of 6240 rows at position
+    6208, and the one-row GEMVs of a layer (stacked q/k/v, o, stacked gate/up,
+    down with the SiLU * up input) over 4 layers' weights, plus lm_head."""
+    import torch
+    from cacheblend import ops
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    H, I, Hq, Hkv, D, V = 4096, 14336, 32, 8, 128, 32000
+    L, cap, p, NL = 32, 6240, 6208, 4
+    bf = torch.bfloat16
+    g = torch.Generator(device=device).manual_seed(0)
+
+    def rnd(shape, scale=1.0):
+        return (torch.randn(shape, generator=g, device=device) * scale).to(bf)
+
+    kc = torch.stack([rnd((cap, Hkv * D)) for _ in range(L)])
+    vc = torch.stack([rnd((cap, Hkv * D)) for _ in range(L)])
+    q = rnd((Hq * D,))
+    pos = torch.tensor([p], dtype=torch.int64, device=device)
+    ws = ops.decode_workspace(cap, Hq, Hkv, D, device)
+    ao = torch.empty((L, 1, Hq * D), dtype=bf, device=device)
+    w_qkv = torch.stack([rnd((H + 2 * Hkv * D, H), 0.02) for _ in range(NL)])
+    w_o = torch.stack([rnd((H, H), 0.02) for _ in range(NL)])
+    w_gu = torch.stack([rnd((2 * I, H), 0.02) for _ in range(NL)])
+    w_down = torch.stack([rnd((H, I), 0.02) for _ in range(NL)])
+    w_lm = rnd((V, H), 0.02)
+    x = rnd((1, 1, H))
+    gu = rnd((1, 1, 2 * I), 3.0)
+    stream = torch.cuda.current_stream(device)
+
+    def graph_ms(fn, n_calls, reps):
+        fn()
+        side = torch.cuda.Stream(device=device)
+        side.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            fn()
+            side.synchronize()
+            with torch.cuda.graph(graph, stream=side):
+                fn()
+        stream.wait_stream(side)
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del graph
+        return e0.elapsed_time(e1) / reps / n_calls
+
+    kernels = {
+        "decode_attn": (lambda: [ops.decode_attn(q, kc[l], vc[l], pos, Hq, Hkv, D, D ** -0.5, ws, out=ao[l])
+                                 for l in range(L)], L, 2 * (p + 1) * Hkv * D * 2),
+        "gemv_qkv": (lambda: [ops.gemv(w_qkv[l], x) for l in range(NL)], NL, w_qkv[0].numel() * 2),
+        "gemv_o": (lambda: [ops.gemv(w_o[l], x) for l in range(NL)], NL, w_o[0].numel() * 2),
+        "gemv_gate_up": (lambda: [ops.gemv(w_gu[l], x) for l in range(NL)], NL, w_gu[0].numel() * 2),
+        # the GEMV forming SiLU * up while it stages its input (cbk_gemv's gate/up form)
+        "gemv_down_silu": (lambda: [ops.gemv(w_down[l], gate=gu[..., :I], up=gu[..., I:]) for l in range(NL)],
+                           NL, w_down[0].numel() * 2),
+        "gemv_lm_head": (lambda: [ops.gemv(w_lm, x)], 1, w_lm.numel() * 2),
+        # the decode step's down projection: one silu_mul launch, then the plain GEMV
+        "silu_mul_then_gemv_down": (lambda: [ops.gemv(w_down[l], ops.silu_mul(gu[..., :I], gu[..., I:]))
+                                             for l in range(NL)], NL, w_down[0].numel() * 2),
+    }
+    clocks = Clocks(0)
+    clocks.start()
+    time.sleep(0.3)
+    hbm = load_peaks()[0]
+    out, per_token_ms, per_token_bytes = {}, 0.0, 0
+    for name, (fn, n, nbytes) in kernels.items():
+        ms = graph_ms(fn, n, args.steps)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us_per_call": round(ms * 1e3, 2), "bytes_per_call": nbytes, "GB/s": round(gbs, 1),
+                     "frac_hbm": round(gbs / hbm, 3)}
+        if name == "gemv_down_silu":               # the alternative the decode step does not use
+            continue
+        calls = 1 if name == "gemv_lm_head" else 32
+        per_token_ms += ms * calls
+        per_token_bytes += nbytes * calls
+    clk = clocks.stop()
+    print(json.dumps({
+        "metric": "decode-step kernels HBM GB/s (Mistral-7B, 7K blended cache)",
+        "value": round(per_token_bytes / (per_token_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_token_kernels": round(per_token_ms, 3),
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "decode-kernels", "cache_rows": cap, "position": p, "layers_timed": {"attention": L,
+                   "gemv": NL}, "per_token": "32 x (attention + 4 GEMV) + lm_head",
+                   "l2": "distinct buffers per launch in a batch (K/V 0.8 GB, weights 1.7 GB); lm_head 262 MB alone"},
+        "kernels": out, "hbm_peak_gbs": hbm, "clocks": clk}), flush=True)
+
+
 LLAMA3_8B = dict(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
                  num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=5e5,
                  rms_norm_eps=1e-5, max_position_embeddings=131072)
@@ -1106,7 +1203,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=30.0)
     ap.add_argument("--workload", default="mistral7b-7k-blend",
                     choices=["mistral7b-7k-blend", "kv-microbench", "attn-layers", "llama70b-128k-sharded",
-                             "llama3-8b-32k-x64", "mistral7b-7k-decode"])
+                             "llama3-8b-32k-x64", "mistral7b-7k-decode", "decode-kernels"])
     ap.add_argument("--attn-layers", type=int, default=31)
     ap.add_argument("--attn-k", type=int, default=931, help="selected rows (6208 = dense causal)")
     ap.add_argument("--attn-dist", default="uniform", choices=["uniform", "tail"])
@@ -1130,6 +1227,8 @@ def main():
         run_llama8b_32k(args)
     elif args.workload == "mistral7b-7k-decode":
         run_decode(args)
+    elif args.workload == "decode-kernels":
+        run_decode_kernels(args)
     else:
         run_ours(args)
 

@@ -4,8 +4,8 @@ runners, ``runners.py:106-152``) on the libcbk kernels.
 The selective prefill keeps its fused cache with spare rows; each decode step
 then runs the decoder for one token at position p: residual add + RMSNorm as
 the fused row kernel, the projections as one-row GEMV kernels (q/k/v and
-gate/up over the stacked weights, SiLU * up formed inside the down
-projection's GEMV, lm_head), RoPE of the token's Q and K with its K/V written
+gate/up over the stacked weights, o, down and lm_head; SiLU * up by
+``silu_mul``), RoPE of the token's Q and K with its K/V written
 into cache row p (``rope_scatter`` with one index), and attention of the one
 query row over rows [0, p] (``decode_attn``: split over the keys, HBM-bound).  Token 1 is the argmax of
 the last prefill row, as in the reference; decoding stops after
@@ -65,8 +65,7 @@ def _qkv1(attn, hn, w_qkv):
 
 
 def _mlp1(layer, hn, w_gu):
-    """MLP at one decode row: the stacked gate/up GEMV, then the down GEMV with
-    silu(gate) * up formed as it stages its input."""
+    """MLP at one decode row: the stacked gate/up GEMV, SiLU * up, then the down GEMV."""
     mlp = layer.mlp
     down = getattr(mlp, "down_proj", None)
     if (w_gu is None or type(mlp).__name__ not in _MLPS or type(mlp.act_fn).__name__ not in _SILUS
@@ -75,7 +74,9 @@ def _mlp1(layer, hn, w_gu):
         return _mlp(layer, hn, w_gu)
     gu = ops.gemv(w_gu, hn)
     inter = mlp.gate_proj.weight.shape[0]
-    return ops.gemv(down.weight, gate=gu[..., :inter], up=gu[..., inter:])
+    # one silu_mul launch, then the plain GEMV: 24.8 vs 26.3 us at 4096 x 14336 for
+    # the GEMV forming SiLU * up itself (each of its CTAs stages the activation)
+    return ops.gemv(down.weight, ops.silu_mul(gu[..., :inter], gu[..., inter:]))
 
 
 def _decode_step(lw, pre, st: _DecodeState, status):
