@@ -1029,7 +1029,13 @@ static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int 
   a.tok_per_tile = kBM / G;
   a.n_tiles = static_cast<int>((n_sel + a.tok_per_tile - 1) / a.tok_per_tile);
   a.n_pairs = (a.n_tiles + 1) / 2;
-  a.target = 2 * sm_count();
+  // items per SM: 1 measured 703 / 838 TFLOP/s (uniform / tail 15 % selection at
+  // S = 6208) against 634 / 807 at 2, 589 / 828 at 3, 557 / 778 at 4, dense causal
+  // unchanged (1128 vs 1125): fewer splits leave less for the combine
+#ifndef CBK_ATTN_ITEMS_PER_SM
+#define CBK_ATTN_ITEMS_PER_SM 1
+#endif
+  a.target = CBK_ATTN_ITEMS_PER_SM * sm_count();
   a.min_chunk = 4;
   // items <= total / C + pairs <= target + pairs (C >= total / target)
   a.max_items = a.target + n_kv_heads * a.n_pairs;
