@@ -37,6 +37,11 @@ def test_abi_version_and_pure_helpers():
             assert N.LIB.cbk_topk_count(S, r) == max(1, min(S, int(S * r)))
     assert N.LIB.cbk_hkvd_workspace_bytes(6208) >= 6208 * 4
     assert N.LIB.cbk_hkvd_workspace_bytes(6208) % 256 == 0
+    # decode attention: per-split partials sized for the split maximum, whatever the cache length
+    dec = N.LIB.cbk_decode_attn_workspace_bytes(6240, 32, 8, 128)
+    assert dec >= 8 * 64 * 4 * 128 * 4 and dec == N.LIB.cbk_decode_attn_workspace_bytes(131328, 32, 8, 128)
+    assert N.LIB.cbk_decode_attn_workspace_bytes(0, 32, 8, 128) == 0
+    assert N.LIB.cbk_decode_attn_workspace_bytes(100, 32, 3, 128) == 0
 
 
 @pytest.mark.parametrize("call,code", [
