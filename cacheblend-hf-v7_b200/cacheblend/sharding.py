@@ -7,11 +7,17 @@ By KV head (long contexts that one GPU cannot hold): rank r of N keeps KV heads
 [r*Hkv/N, (r+1)*Hkv/N) and the q heads of their groups.  Concat + RoPE shift,
 the fresh-row scatter and partial attention are head-local.  HKVD needs the
 per-token deviation summed over all heads: every rank computes its partial
-over its own heads, the partials are all-gathered (S fp32 per rank) and summed
-in rank order on every rank, so every rank selects the identical index set
-without a broadcast.  The sum is a deterministic function of N (a different
-rounding order than the single-GPU kernel, so the single-GPU selection can
-differ only where two deviations tie to fp32 rounding).
+over its own heads, the partials are all-gathered (S fp32 per rank) and
+combined on every rank, so every rank selects the identical index set without
+a broadcast.
+
+The deviation kernel sums a row as a complete binary tree of pairwise fp32
+adds over its 8-element vectors.  A rank's heads are an aligned run of
+Hkv*D/(8N) vectors; when that count is a power of two (N a power of two
+dividing Hkv, head_dim/8 a power of two) the rank's partial is a node of the
+single-GPU tree, and combining the N partials with the same pairwise tree
+(``combine_partials``) gives the single-GPU deviations bit for bit: the
+selection does not depend on N.
 """
 from __future__ import annotations
 
@@ -28,16 +34,23 @@ def head_shard(n_kv_heads: int, world: int, rank: int) -> tuple[int, int]:
 
 
 def combine_partials(parts) -> torch.Tensor:
-    """Sum per-rank deviation partials in rank order (elementwise fp32 adds)."""
-    total = parts[0].clone()
-    for p in parts[1:]:
-        total = total + p
-    return total
+    """Combine per-rank deviation partials (rank order = head order) with the
+    pairwise tree of the deviation kernel: level by level, node = left + right,
+    an odd count padded with zeros (adding zero leaves a node unchanged)."""
+    level = list(parts)
+    if not level:
+        raise ValueError("combine_partials: no partials")
+    while len(level) > 1:
+        nxt = [level[i] + level[i + 1] for i in range(0, len(level) - 1, 2)]
+        if len(level) % 2:
+            nxt.append(level[-1])
+        level = nxt
+    return level[0].clone() if level[0] is parts[0] else level[0]
 
 
 def exchange_deviation(partial: torch.Tensor, group=None) -> torch.Tensor:
-    """All-gather per-rank deviation partials (S,) fp32 and sum them in rank
-    order; every rank returns the same tensor.  Without a process group (one
+    """All-gather per-rank deviation partials (S,) fp32 and combine them with
+    the kernel's pairwise tree; every rank returns the same tensor.  Without a process group (one
     GPU) the partial is the total."""
     if not (dist.is_available() and dist.is_initialized()):
         return partial

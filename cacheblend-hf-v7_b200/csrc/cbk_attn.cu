@@ -92,7 +92,9 @@ struct AttnParams {
   const int4* items;      // (kv head, tile pair, chunk, length) longest first
   const int* tile_base;   // [Hkv][n_tiles]: first partial slot of a split tile, -1 if not split
   const int4* split_desc; // [n_split]: (kvh * n_tiles + tile, first slot, chunks, 0) per split tile
-  __half* part_o;         // [slot][128][HD] O / l of the chunk (fp16, bounded by |V|)
+  uint16_t* part_o;       // [slot][128][HD] O / l of the chunk, in the inputs' 16-bit type
+                          // (a convex combination of V rows: bounded by max |V|, so it
+                          // cannot overflow the type V itself is stored in)
   float2* part_ml;        // [slot][128] (running max in log2 units, row sum)
   int64_t n_sel;
   int n_q_heads;
@@ -651,9 +653,9 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       tc_fence_after();
       const int slot0 = prm.tile_base[ig.kvh * prm.n_tiles + (t ? ig.tile[1] : ig.tile[0])];
       if (slot0 >= 0) {
-        // split tile: this chunk's O / l (fp16), running max and row sum
+        // split tile: this chunk's O / l (16-bit, the inputs' type), running max and row sum
         const int64_t slot = slot0 + ig.chunk;
-        __half* po = prm.part_o + (slot * kBM + row) * HD;
+        uint16_t* po = prm.part_o + (slot * kBM + row) * HD;
         const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;   // no visible key: O = 0
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
@@ -666,8 +668,8 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             uint32_t* w = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
             for (int e = 0; e < 4; ++e)
-              w[e] = pack2<CBK_F16>(__uint_as_float(o[q * 8 + 2 * e]) * inv_l,
-                                    __uint_as_float(o[q * 8 + 2 * e + 1]) * inv_l);
+              w[e] = pack2<DT>(__uint_as_float(o[q * 8 + 2 * e]) * inv_l,
+                               __uint_as_float(o[q * 8 + 2 * e + 1]) * inv_l);
             st_vec(po + c * 32 + q * 8, v);
           }
         }
@@ -941,13 +943,9 @@ attn_combine_kernel(const AttnParams prm) {
             const float2 ml = *ml_ptr(c0 + q, i);
             const float w = ml.y > 0.f ? ml.y * ex2(ml.x - M[i]) : 0.f;
             sum[i] += w;
-            const __half2* h = reinterpret_cast<const __half2*>(&raw[q][i]);
+            const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw[q][i]);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = __half22float2(h[e]);
-              acc[i][2 * e] = fmaf(w, f.x, acc[i][2 * e]);
-              acc[i][2 * e + 1] = fmaf(w, f.y, acc[i][2 * e + 1]);
-            }
+            for (int e = 0; e < 8; ++e) acc[i][e] = fmaf(w, Elem<DT>::to_f(h[e]), acc[i][e]);
           }
         }
     }
@@ -1046,7 +1044,7 @@ static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int 
   a.off_split = a.off_tile_base + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int));
   a.off_ml = a.off_split + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int4));
   a.off_o = a.off_ml + align256(static_cast<size_t>(a.max_slots) * kBM * sizeof(float2));
-  a.bytes = a.off_o + static_cast<size_t>(a.max_slots) * kBM * head_dim * sizeof(__half);
+  a.bytes = a.off_o + static_cast<size_t>(a.max_slots) * kBM * head_dim * sizeof(uint16_t);
   return a;
 }
 
@@ -1071,7 +1069,7 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   prm.tile_base = reinterpret_cast<const int*>(ws + lay.off_tile_base);
   prm.split_desc = reinterpret_cast<const int4*>(ws + lay.off_split);
   prm.part_ml = reinterpret_cast<float2*>(ws + lay.off_ml);
-  prm.part_o = reinterpret_cast<__half*>(ws + lay.off_o);
+  prm.part_o = reinterpret_cast<uint16_t*>(ws + lay.off_o);
   prm.n_sel = n_sel;
   prm.n_q_heads = n_q_heads;
   prm.group = G;

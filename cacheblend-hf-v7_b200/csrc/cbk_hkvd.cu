@@ -1,11 +1,21 @@
 // HKVD: per-token K deviation and top-K selection with the force-include rule.
 //
 // Deviation order (reproduced bit-for-bit by the oracle):
-//   one warp per token; lane l owns the 16-byte vectors v = l, l+32, l+64, ...
-//   of the row (8 elements each).  acc_l = 0; for each owned vector in
-//   increasing v, for e = 0..7: acc_l = acc_l + (d_e * d_e), d_e = new - old,
-//   every operation a separately rounded fp32 op (no FMA).  Then a butterfly
-//   acc_l += acc_(l xor o) for o = 16, 8, 4, 2, 1; lane 0 writes the result.
+//   the row's features are cut into 16-byte vectors of 8 elements; each
+//   vector's sum of squared differences is taken in element order,
+//   s = d_0*d_0, s = s + d_e*d_e (separately rounded fp32 ops, no FMA,
+//   d_e = new - old); the row total is the complete binary tree of pairwise
+//   fp32 adds over the vector sums, padded with zeros to a power of two
+//   (node = left + right, adjacent nodes paired level by level).
+//   Any aligned power-of-two run of vectors is a subtree, so the deviation of
+//   a slice of heads (one rank's KV heads when the heads are sharded over
+//   ranks) is a node of the full tree, and combining the slices' values with
+//   the same pairwise tree reproduces the single-GPU bits.
+//   In the kernel: one warp per token; lane l holds vectors l, l+32, l+64,
+//   l+96 of each 128-vector group; an xor butterfly over the lanes (1, 2, 4, 8,
+//   16) forms the 32-vector nodes, two more adds the 128-vector node, and
+//   successive groups are merged by a binary counter (which equals the
+//   zero-padded complete tree).
 //
 // Top-K: one CTA.  Order keys are the fp32 bit patterns mapped to a monotone
 // unsigned order; four 8-bit radix passes find the k-th largest key T and how
@@ -19,6 +29,21 @@ namespace cbk {
 
 constexpr int kDevThreads = 256;
 constexpr int kDevBatch = 4;     // 16-byte vectors per lane per batch
+constexpr int kDevLevels = 16;   // counter levels: rows of up to 2^16 groups of 128 vectors
+constexpr int64_t kDevMaxFeat = (int64_t{1} << kDevLevels) * 32 * kDevBatch * 8;
+
+template <int DT>
+__device__ __forceinline__ float vec_sq_sum(const uint4& x, const uint4& y) {
+  const uint16_t* xs = reinterpret_cast<const uint16_t*>(&x);
+  const uint16_t* ys = reinterpret_cast<const uint16_t*>(&y);
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float d = __fsub_rn(Elem<DT>::to_f(xs[e]), Elem<DT>::to_f(ys[e]));
+    s = e ? __fadd_rn(s, __fmul_rn(d, d)) : __fmul_rn(d, d);
+  }
+  return s;
+}
 
 template <int DT>
 __global__ void __launch_bounds__(kDevThreads)
@@ -28,9 +53,8 @@ deviation_kernel(const uint16_t* __restrict__ k_new, int64_t new_stride,
   const int lane = threadIdx.x & 31;
   const int64_t t = (static_cast<int64_t>(blockIdx.x) * kDevThreads + threadIdx.x) >> 5;
   if (t >= S) return;
-  // A lane's vectors go kDevBatch at a time with all their loads issued first;
-  // the fresh row's first batch is requested before the chunk search.  The
-  // accumulation order above is unchanged.
+  // A lane's vectors of a 128-vector group are loaded together (the fresh
+  // row's first group before the chunk search), then summed.
   const uint16_t* a = k_new + t * new_stride;
   const int nvec = static_cast<int>(feat >> 3);
   uint4 x[kDevBatch], y[kDevBatch];
@@ -43,31 +67,49 @@ deviation_kernel(const uint16_t* __restrict__ k_new, int64_t new_stride,
     if (chunk_start[mid] <= t) lo = mid; else hi = mid - 1;
   }
   const uint16_t* b = static_cast<const uint16_t*>(old_srcs[lo].k) + (t - chunk_start[lo]) * feat;
-  float acc = 0.f;
-  for (int v0 = lane; v0 < nvec; v0 += 32 * kDevBatch) {
-    if (v0 != lane) {
+  // binary counter over 128-vector group nodes: stack[i] holds a node of 2^i
+  // groups (constant indices after unrolling, so the stack stays in registers)
+  float stack[kDevLevels];
+  int groups = 0;
+  for (int v0 = 0; v0 < nvec; v0 += 32 * kDevBatch) {
+    if (v0) {
 #pragma unroll
       for (int q = 0; q < kDevBatch; ++q)
-        if (v0 + q * 32 < nvec) x[q] = ld_vec(a + (v0 + q * 32) * 8);
+        if (v0 + lane + q * 32 < nvec) x[q] = ld_vec(a + (v0 + lane + q * 32) * 8);
     }
 #pragma unroll
     for (int q = 0; q < kDevBatch; ++q)
-      if (v0 + q * 32 < nvec) y[q] = ld_stream(b + (v0 + q * 32) * 8);
+      if (v0 + lane + q * 32 < nvec) y[q] = ld_stream(b + (v0 + lane + q * 32) * 8);
+    float n32[kDevBatch];
 #pragma unroll
     for (int q = 0; q < kDevBatch; ++q) {
-      if (v0 + q * 32 < nvec) {
-        const uint16_t* xs = reinterpret_cast<const uint16_t*>(&x[q]);
-        const uint16_t* ys = reinterpret_cast<const uint16_t*>(&y[q]);
+      float s = (v0 + lane + q * 32 < nvec) ? vec_sq_sum<DT>(x[q], y[q]) : 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float d = __fsub_rn(Elem<DT>::to_f(xs[e]), Elem<DT>::to_f(ys[e]));
-          acc = __fadd_rn(acc, __fmul_rn(d, d));
-        }
+      for (int o = 1; o <= 16; o <<= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+      n32[q] = s;                                           // vectors [v0 + 32q, +32)
+    }
+    float node = __fadd_rn(__fadd_rn(n32[0], n32[1]), __fadd_rn(n32[2], n32[3]));   // 128 vectors
+#pragma unroll
+    for (int lvl = 0; lvl < kDevLevels; ++lvl) {
+      if (!((groups >> lvl) & 1)) {
+        stack[lvl] = node;
+        break;
       }
+      node = __fadd_rn(stack[lvl], node);
+    }
+    ++groups;
+  }
+  // fold what the counter holds, from the smallest node up (the zero padding
+  // of the complete tree leaves the smaller node as the right operand)
+  float acc = 0.f;
+  bool have = false;
+#pragma unroll
+  for (int lvl = 0; lvl < kDevLevels; ++lvl) {
+    if ((groups >> lvl) & 1) {
+      acc = have ? __fadd_rn(stack[lvl], acc) : stack[lvl];
+      have = true;
     }
   }
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
   if (lane == 0) dev[t] = acc;
 }
 
@@ -220,7 +262,8 @@ static int check_dev_args(const char* fn, const void* k_new, int64_t new_stride,
     return set_error(CBK_ERR_UNSUPPORTED, "%s: dtype %d not supported (bf16/fp16 only)", fn, dtype);
   if (!k_new || !old_srcs || !chunk_start)
     return set_error(CBK_ERR_INVALID, "%s: null pointer argument", fn);
-  if (S <= 0 || n_chunks <= 0 || feat <= 0 || feat % 8 != 0 || new_stride < feat || new_stride % 8)
+  if (S <= 0 || n_chunks <= 0 || feat <= 0 || feat % 8 != 0 || feat >= kDevMaxFeat || new_stride < feat ||
+      new_stride % 8)
     return set_error(CBK_ERR_INVALID, "%s: bad sizes (S %lld, chunks %d, feat %lld, stride %lld)",
                      fn, (long long)S, n_chunks, (long long)feat, (long long)new_stride);
   if (reinterpret_cast<uintptr_t>(k_new) & 15u)

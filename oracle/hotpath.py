@@ -112,9 +112,11 @@ def kv_deviation(k_new, k_old, order="kernel"):
     """dev[t] = sum_f (K_new - K_old)^2 in fp32 (hkvd.py:42-51).
 
     order="kernel": the fixed order of the CUDA kernel, reproduced exactly:
-      lane l (0..31) owns 8-element vectors v = l, l+32, ...; it accumulates
-      acc = acc + d*d element by element (separately rounded fp32 ops); the
-      32 lane sums are combined by a butterfly (xor 16, 8, 4, 2, 1).
+      each 8-element vector's squares are summed in element order
+      (s = d0*d0, then s = s + de*de, separately rounded fp32 ops); the row
+      total is the complete binary tree of pairwise adds over the vector
+      sums, zero-padded to a power of two.  An aligned power-of-two slice of
+      the features (a shard's KV heads) is a subtree of it.
     order="f64": float64 sum rounded to fp32 (an order-free yardstick)."""
     a = np.asarray(k_new, np.float32)
     b = np.asarray(k_old, np.float32)
@@ -132,17 +134,25 @@ def kv_deviation(k_new, k_old, order="kernel"):
     S, F = d.shape
     assert F % 8 == 0
     sq = (d * d).astype(np.float32).reshape(S, F // 8, 8)
-    nvec = F // 8
-    acc = np.zeros((S, 32), np.float32)
-    for m in range(0, nvec, 32):
-        blk = sq[:, m:m + 32, :]                 # vectors m .. m+31 -> lanes 0..31
-        w = blk.shape[1]
-        for e in range(8):
-            acc[:, :w] = (acc[:, :w] + blk[:, :, e]).astype(np.float32)
-    lanes = np.arange(32)
-    for o in (16, 8, 4, 2, 1):
-        acc = (acc + acc[:, lanes ^ o]).astype(np.float32)
-    return acc[:, 0].copy()
+    vec = sq[:, :, 0].copy()
+    for e in range(1, 8):
+        vec = (vec + sq[:, :, e]).astype(np.float32)
+    return tree_sum(vec)
+
+
+def tree_sum(x):
+    """Complete binary tree of pairwise fp32 adds along the last axis (zero-padded
+    to a power of two; adjacent nodes paired level by level)."""
+    x = np.asarray(x, np.float32)
+    n = x.shape[-1]
+    p = 1
+    while p < n:
+        p *= 2
+    if p != n:
+        x = np.concatenate([x, np.zeros(x.shape[:-1] + (p - n,), np.float32)], axis=-1)
+    while x.shape[-1] > 1:
+        x = (x[..., 0::2] + x[..., 1::2]).astype(np.float32)
+    return x[..., 0].copy()
 
 
 def topk_count(S: int, ratio: float) -> int:
@@ -198,12 +208,18 @@ def scatter_rows(cache, idx, fresh):
     return out
 
 
-def partial_attention(q, k, v, pos, scale, dtype=np.float64):
+def partial_attention(q, k, v, pos, scale, dtype=np.float64, with_abs=False, heads=None):
     """softmax(scale * Q_sel K^T + causal(pos)) V with GQA (n_rep = Hq / Hkv).
 
     q: (n, Hq, D); k, v: (S, Hkv, D); pos: (n,) ascending.  Returns (n, Hq*D).
     Keys t > pos[j] are excluded, like the -inf rows of the reference mask
-    (fusor.py:301-307, 385)."""
+    (fusor.py:301-307, 385).
+
+    with_abs=True also returns the same softmax weights applied to |V|
+    (sum_t p_t |v_t| / sum_t p_t), the scale that 16-bit rounding of P and of
+    the output acts on: an error bound for a 16-bit kernel is a fraction of
+    it.  ``heads`` restricts the computation to those q heads (the other
+    columns are left zero)."""
     q = np.asarray(q, dtype)
     k = np.asarray(k, dtype)
     v = np.asarray(v, dtype)
@@ -211,15 +227,21 @@ def partial_attention(q, k, v, pos, scale, dtype=np.float64):
     S, Hkv, _ = k.shape
     G = Hq // Hkv
     out = np.zeros((n, Hq, D), dtype)
+    absm = np.zeros((n, Hq, D), dtype) if with_abs else None
     pos = np.asarray(pos, np.int64)
     t = np.arange(S)
-    for h in range(Hq):
+    for h in (range(Hq) if heads is None else heads):
         kh, vh = k[:, h // G, :], v[:, h // G, :]
         s = (q[:, h, :] @ kh.T) * scale                       # (n, S)
         s = np.where(t[None, :] <= pos[:, None], s, -np.inf)
         m = s.max(axis=1, keepdims=True)
         p = np.exp(s - m)
-        out[:, h, :] = (p @ vh) / p.sum(axis=1, keepdims=True)
+        l = p.sum(axis=1, keepdims=True)
+        out[:, h, :] = (p @ vh) / l
+        if with_abs:
+            absm[:, h, :] = (p @ np.abs(vh)) / l
+    if with_abs:
+        return out.reshape(n, Hq * D), absm.reshape(n, Hq * D)
     return out.reshape(n, Hq * D)
 
 

@@ -1,0 +1,41 @@
+"""The partial-attention bound can fail: mistakes planted in a CPU restatement
+of the attention (never in a GPU kernel) violate it on the peaked GPU cases,
+while the exact result rounded to the output type stays inside it.
+
+Runs on the CPU over the q heads of the first KV head of each case (the bound
+is element by element, so a violation there is a violation of the whole case)."""
+import numpy as np
+import pytest
+
+import attn_check as ac
+
+MISTAKES = ["causal_plus_one", "causal_minus_one", "drop_split_chunk", "merge_without_max"]
+PEAKED = ["mistral7k_peaked", "g8_peaked", "long_split_peaked"]
+
+
+@pytest.fixture(scope="module", params=PEAKED)
+def case_data(request):
+    case = ac.CASE[request.param]
+    q, k, v, pos = ac.make_inputs(case)
+    G = case[3] // case[4]
+    heads = list(range(G))
+    exp, absm = ac.oracle(case, q, k, v, pos, heads=heads)
+    cols = np.concatenate([np.arange(h * case[5], (h + 1) * case[5]) for h in heads])
+    return case, (q, k, v, pos), heads, cols, exp, absm
+
+
+def test_rounded_exact_result_is_inside(case_data):
+    case, _, _, cols, exp, absm = case_data
+    n_bad, worst = ac.violations(ac.round_to(exp, case[6]), exp, absm, case[6], cols)
+    assert n_bad == 0 and worst < ac.TOL[case[6]] / 2, worst
+
+
+@pytest.mark.parametrize("mistake", MISTAKES)
+def test_planted_mistake_is_caught(case_data, mistake):
+    case, inputs, heads, cols, exp, absm = case_data
+    C, row_tile, key_tiles = ac.plan(inputs[3].numpy(), case[2], case[3] // case[4], case[4])
+    if mistake in ("drop_split_chunk", "merge_without_max"):
+        assert (key_tiles > C).any(), "the case must have split tiles"
+    bad = ac.round_to(ac.planted(case, *inputs, mistake, heads), case[6])
+    n_bad, worst = ac.violations(bad, exp, absm, case[6], cols)
+    assert n_bad > 0 and worst > 4 * ac.TOL[case[6]], (mistake, n_bad, worst)

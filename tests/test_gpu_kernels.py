@@ -1,12 +1,13 @@
 """Kernel-level parity of the sm_100a path against the oracle (and, through the
 golden fixtures, against the reference).  Integer / byte work is bit-exact;
 RoPE is bit-exact given the device's cos/sin table; attention is compared with
-an exact fp64 oracle within the bf16 tolerance atol 2e-2 (mean error bound
-1e-3)."""
+an exact fp64 oracle element by element, within a bound that scales with the
+output (``attn_check``)."""
 import numpy as np
 import pytest
 import torch
 
+import attn_check as ac
 from helpers import from_bits, golden, to_bits, ulp_diff_bf16
 from oracle import hotpath as hp
 from oracle.bf16 import bf16_to_f32, f32_to_bf16, f16_to_f32, f32_to_f16
@@ -286,44 +287,24 @@ def test_hkvd_select_fused(ops):
 # ---------------------------------------------------------------------------
 # (e) partial attention
 # ---------------------------------------------------------------------------
-ATTN_CASES = [
-    # name, S, n_sel, Hq, Hkv, D, dtype
-    ("mistral7k", 6208, 931, 32, 8, 128, "bf16"),
-    ("mock", 544, 81, 4, 2, 64, "bf16"),
-    ("dense_causal", 300, 300, 8, 2, 128, "bf16"),
-    ("g1", 1000, 150, 8, 8, 128, "bf16"),
-    ("g8", 2048, 200, 64, 8, 128, "bf16"),
-    ("g16", 700, 33, 16, 1, 64, "f16"),
-    ("short", 100, 15, 4, 1, 128, "bf16"),
-    ("one_row", 2000, 1, 8, 2, 128, "bf16"),
-    ("f16_128", 1500, 225, 32, 8, 128, "f16"),
-    ("long_split", 20000, 2000, 32, 8, 128, "bf16"),
-]
-
-
-@pytest.mark.parametrize("name,S,n_sel,Hq,Hkv,D,dtype", ATTN_CASES)
-def test_partial_attention(ops, name, S, n_sel, Hq, Hkv, D, dtype):
-    g = torch.Generator().manual_seed(S + n_sel)
-    if n_sel == S:
-        pos = torch.arange(S)
-    else:
-        pos = torch.sort(torch.randperm(S - 1, generator=g)[: n_sel - 1]).values
-        pos = torch.cat([pos, torch.tensor([S - 1])])
-    q = rand16((n_sel, Hq * D), dtype, g)
-    k = rand16((S, Hkv * D), dtype, g)
-    v = rand16((S, Hkv * D), dtype, g)
+@pytest.mark.parametrize("case", ac.CASES, ids=[c[0] for c in ac.CASES])
+def test_partial_attention(ops, case):
+    """Element by element within tol * (|exp| + A) of the fp64 oracle (A: the
+    softmax weights applied to |V|; tol 2^-7 bf16, 2^-9 fp16), and max |err|
+    within 2e-2 of max |exp|.  Peaked cases (q scaled) make outputs O(1) and
+    single keys decisive; big-V cases put |V| near 1e5 (bf16) and 3e4 (fp16)
+    through split tiles.  tests/test_attn_bound.py shows that an off-by-one
+    causal bound, a dropped split chunk or a wrong merge weight violate this
+    bound on the peaked cases."""
+    name, S, n_sel, Hq, Hkv, D, dtype, _, _ = case
+    q, k, v, pos = ac.make_inputs(case)
     st = status_word()
     out = ops.partial_attn(q.to(DEV), k.to(DEV), v.to(DEV), pos.to(DEV), Hq, Hkv, D, D ** -0.5,
                            status=st)
     assert_status_clean(st)
     got = DEC[dtype](to_bits(out))
-    exp = hp.partial_attention(DEC[dtype](to_bits(q)).reshape(n_sel, Hq, D),
-                               DEC[dtype](to_bits(k)).reshape(S, Hkv, D),
-                               DEC[dtype](to_bits(v)).reshape(S, Hkv, D), pos.numpy(), D ** -0.5)
-    err = np.abs(got - exp)
-    assert np.isfinite(got).all()
-    assert err.max() < 2e-2, err.max()
-    assert err.mean() < 1e-3, err.mean()
+    exp, absm = ac.oracle(case, q, k, v, pos)
+    ac.check(got, exp, absm, dtype)
 
 
 def test_partial_attention_vs_reference_golden(ops):

@@ -1,9 +1,10 @@
 """KV-head sharding of HKVD on one GPU: each shard's partial deviation comes
-from the deviation kernel over its head columns, the partials are summed in
-rank order (the exchange's combine step), and top-K runs on the total.  The
-oracle does the same per-shard fp32 sums: the totals and the selected index
-sets must be bit-identical.  The NCCL exchange itself is exercised by the
-sharded bench workload on 2+ GPUs and by the gloo tests on CPU."""
+from the deviation kernel over its head columns, the partials are combined
+with the kernel's pairwise tree (the exchange's combine step), and top-K runs
+on the total.  The totals must equal the unsharded kernel's deviations bit for
+bit, and the selection the unsharded selection, at 2, 4 and 8 shards.  The
+NCCL exchange itself is exercised by the sharded bench workload on 2+ GPUs and
+by the gloo tests on CPU."""
 import numpy as np
 import pytest
 import torch
@@ -40,8 +41,16 @@ def test_sharded_partials_sum_and_select_like_oracle(world):
         exp_parts.append(hp.kv_deviation(bf16_to_f32(to_bits(new[:, cols])), bf16_to_f32(to_bits(old[:, cols]))))
     total = combine_partials(parts)
     idx = ops.topk_select(total, k, force_last=True)
-    exp_total = exp_parts[0].astype(np.float32)
-    for p in exp_parts[1:]:
-        exp_total = (exp_total + p).astype(np.float32)
+    # unsharded: the deviation kernel over all heads, then the same top-K
+    entries = [{"K": [old_d[a:b].contiguous().unsqueeze(0)], "V": [old_d[a:b].contiguous().unsqueeze(0)]}
+               for a, b in zip(starts, starts[1:])]
+    single = ops.kv_deviation_rows(new_d, ops.ChunkTable(entries, [0], DEV), 0)
+    idx1 = ops.topk_select(single, k, force_last=True)
+    np.testing.assert_array_equal(total.cpu().numpy().view(np.uint32), single.cpu().numpy().view(np.uint32))
+    np.testing.assert_array_equal(idx.cpu().numpy(), idx1.cpu().numpy())
+    # and both equal the oracle's restatement
+    exp_total = hp.tree_sum(np.stack(exp_parts, axis=-1))
     np.testing.assert_array_equal(total.cpu().numpy(), exp_total)
-    np.testing.assert_array_equal(idx.cpu().numpy(), hp.topk_select(exp_total, k, force_last=True))
+    exp_single = hp.kv_deviation(bf16_to_f32(to_bits(new)), bf16_to_f32(to_bits(old)))
+    np.testing.assert_array_equal(exp_total, exp_single)
+    np.testing.assert_array_equal(idx.cpu().numpy(), hp.topk_select(exp_single, k, force_last=True))
