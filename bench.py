@@ -169,13 +169,15 @@ def run_ours(args):
     dev_ids = [torch.tensor([t for c in chunks for t in c.token_ids], dtype=torch.int64, device=device)
                for chunks in reqs]
 
-    def step(i):
+    use_graph = not args.no_cuda_graph
+
+    def step(i, graph=use_graph):
         chunks = reqs[i % len(reqs)]
         logits = cb.fuse_selective(lw, chunks, store, recompute_ratio=RATIO, check_layer=CHECK_LAYER,
-                                   input_ids=dev_ids[i % len(reqs)])
+                                   input_ids=dev_ids[i % len(reqs)], cuda_graph=None if graph else False)
         return logits[0, -1].argmax()
 
-    for i in range(args.warmup):
+    for i in range(args.warmup):          # (the first call of the geometry captures its CUDA graph)
         step(i)
     torch.cuda.synchronize()
 
@@ -190,29 +192,27 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # --- device-timed region --------------------------------------------------
+    def device_timed(fn):
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for i in range(args.steps):
+            fn(i)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(t0.elapsed_time(t1))
+
+    # --- device-timed region: the public API call (a replayed CUDA graph) -----
     clocks = Clocks(local)
-    barrier()
-    torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
-    TIMES.reset()
-    TIMES.active = True
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed")
-    t0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    t1.record(stream)
+    ms = device_timed(step)
     torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    TIMES.active = False
-    barrier()
     clk = clocks.stop()
-    ms = max_over_ranks(t0.elapsed_time(t1))
-    kern = TIMES.summary()
-    launch_counts = dict(TIMES.launches)
 
     # --- end to end through the public API (host ids in, first token out) -----
     pinned = [torch.tensor([t for c in chunks for t in c.token_ids], dtype=torch.int64).pin_memory()
@@ -224,39 +224,29 @@ def run_ours(args):
         chunks = reqs[i % len(reqs)]
         a = time.perf_counter()
         logits = cb.fuse_selective(lw, chunks, store, recompute_ratio=RATIO, check_layer=CHECK_LAYER,
-                                   input_ids=pinned[i % len(reqs)])         # H2D of this step's ids
+                                   input_ids=pinned[i % len(reqs)],          # H2D of this step's ids
+                                   cuda_graph=None if use_graph else False)
         int(logits[0, -1].argmax().item())                                   # first token to host
         e2e_ms.append((time.perf_counter() - a) * 1e3)
     barrier()
     e2e_step = max_over_ranks(sum(e2e_ms) / len(e2e_ms))
 
-    # --- the same steps replayed from one captured CUDA graph (BlendGraph) ------
-    graph_res = None
-    if not args.no_cuda_graph:
-        bg = cb.BlendGraph(lw, reqs[0], store, recompute_ratio=RATIO, check_layer=CHECK_LAYER)
-        for i in range(args.warmup):
-            bg(reqs[i % len(reqs)], store, input_ids=dev_ids[i % len(reqs)])
-        barrier()
-        torch.cuda.synchronize()
-        g0 = torch.cuda.Event(enable_timing=True)
-        g1 = torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        for i in range(args.steps):
-            bg(reqs[i % len(reqs)], store, input_ids=dev_ids[i % len(reqs)])[0, -1].argmax()
-        g1.record(stream)
-        torch.cuda.synchronize()
-        g_ms = max_over_ranks(g0.elapsed_time(g1)) / args.steps
-        ge = []
-        for i in range(args.steps):
-            a = time.perf_counter()
-            int(bg(reqs[i % len(reqs)], store, input_ids=pinned[i % len(reqs)])[0, -1].argmax().item())
-            ge.append((time.perf_counter() - a) * 1e3)
-        ge_ms = max_over_ranks(sum(ge) / len(ge))
-        graph_res = {"ms_per_step": round(g_ms, 3), "tokens_per_s": round(world * S / (g_ms * 1e-3), 1),
-                     "e2e_ttft_ms": round(ge_ms, 3),
-                     "how": "BlendGraph: fuse_selective captured once per request geometry; each step refreshes "
-                            "the chunk pointer table and ids, then replays (identical results, tested bit for bit)"}
-        del bg
+    # --- the same steps launched kernel by kernel: per-kernel CUDA events -------
+    # (the kernels a replayed graph runs, timed on their launch streams; the
+    # roofline below comes from this region)
+    for i in range(args.warmup):
+        step(i, graph=False)
+    torch.cuda.synchronize()
+    TIMES.reset()
+    TIMES.active = True
+    eager_ms = device_timed(lambda i: step(i, graph=False))
+    TIMES.active = False
+    kern = TIMES.summary()
+    launch_counts = dict(TIMES.launches)
+    eager_res = {"ms_per_step": round(eager_ms / args.steps, 3),
+                 "tokens_per_s": round(world * S * args.steps / (eager_ms * 1e-3), 1),
+                 "how": "fuse_selective(cuda_graph=False): every kernel launched from Python, each wrapped in "
+                        "CUDA events (the per-kernel figures and the roofline come from this region)"}
 
     # --- kernel accounting -----------------------------------------------------
     _, idx = cb.fuse_selective(lw, reqs[0], store, recompute_ratio=RATIO, check_layer=CHECK_LAYER,
@@ -285,7 +275,15 @@ def run_ours(args):
     hk_bytes = 2 * S * kv_dim * 2 + S * 4
     n_sc, sc_ms = kern.get("rope_scatter", (0, 0.0))
     k_sel = len(idx_l)
-    sc_bytes_sparse = k_sel * (cfg.hidden_size + 2 * kv_dim) * 2 * 2
+    sc_bytes_sparse = k_sel * (cfg.hidden_size + 2 * kv_dim) * 2 * 2      # read + write Q, K, V rows
+    sc_bytes_dense = S * (cfg.hidden_size + 2 * kv_dim) * 2 * 2
+    sc_bytes_step = CHECK_LAYER * sc_bytes_dense + (L - CHECK_LAYER) * sc_bytes_sparse
+
+    def gbs(nbytes, calls, total_ms):
+        if not calls:
+            return None, None
+        r = nbytes / (total_ms / calls * 1e-3) / 1e9
+        return round(r, 1), round(r / hbm_peak, 3)
     traffic = None
     prof = os.path.join(ROOT, "profiles", "partial_attn_kernel_mistral7b_7k_blend_traffic.json")
     if os.path.exists(prof):
@@ -325,16 +323,22 @@ def run_ours(args):
                      "frac": round(achieved_tf / tf_sust, 4) if achieved_tf else None,
                      "peak_kind": f"{peak_src} bf16 sustained (kernel timed inside a long step)",
                      "flops_per_launch": per_launch_flops, "calls": n_attn,
-                     "avg_launch_ms": round(attn_avg_ms, 5), "traffic": traffic},
+                     "avg_launch_ms": round(attn_avg_ms, 5), "traffic": traffic,
+                     "traffic_src": ("dram bytes per launch read from the committed ncu summary "
+                                     "profiles/partial_attn_kernel_mistral7b_7k_blend_traffic.json, not measured "
+                                     "in this run") if traffic else None,
+                     "timed_in": "the kernel-by-kernel region (eager_launches)"},
         "kernels": {
             "assemble_kv": {"calls": n_asm, "avg_ms": round(asm_ms / max(n_asm, 1), 4),
                             "bytes": asm_bytes,
                             "GB/s": round(asm_bytes / (asm_ms / max(n_asm, 1) * 1e-3) / 1e9, 1) if n_asm else None,
                             "frac_hbm": round(asm_bytes / (asm_ms / max(n_asm, 1) * 1e-3) / 1e9 / hbm_peak, 3) if n_asm else None},
             "hkvd_select": {"calls": n_hk, "avg_ms": round(hk_ms / max(n_hk, 1), 4), "bytes": hk_bytes,
-                            "GB/s": round(hk_bytes / (hk_ms / max(n_hk, 1) * 1e-3) / 1e9, 1) if n_hk else None},
+                            "GB/s": gbs(hk_bytes, n_hk, hk_ms)[0], "frac_hbm": gbs(hk_bytes, n_hk, hk_ms)[1]},
             "rope_scatter": {"calls": n_sc, "avg_ms": round(sc_ms / max(n_sc, 1), 4),
-                             "bytes_sparse_layer": sc_bytes_sparse},
+                             "bytes_sparse_layer": sc_bytes_sparse, "bytes_per_step": sc_bytes_step,
+                             "GB/s": gbs(sc_bytes_step * n_sc / max(L, 1), n_sc, sc_ms)[0],
+                             "frac_hbm": gbs(sc_bytes_step * n_sc / max(L, 1), n_sc, sc_ms)[1]},
             "partial_attn_sparse": {"calls": n_sp, "avg_ms": round(ms_sp / max(n_sp, 1), 4),
                                     "flops_per_call": fl_sp,
                                     "TFLOP/s": round(tf_sp, 1) if tf_sp else None},
@@ -344,11 +348,15 @@ def run_ours(args):
             "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_src,
         },
         "gpu_launches": launches,
+        "gpu_launches_note": "libcbk launches counted in the kernel-by-kernel region over the same number of "
+                             "steps; the replayed graph of the timed region holds the same launches",
         "clocks": clk,
-        "cuda_graph": graph_res,
+        "eager_launches": eager_res,
+        "timed_path": ("fuse_selective default: a CUDA graph of the request geometry, captured on the first "
+                       "call, replayed per step" if use_graph else "fuse_selective(cuda_graph=False)"),
     }
     if world == 1 and not args.no_cpu_baseline:       # host-core baseline: rank 0 at N=1 only
-        res["cpu_baseline"] = cpu_baseline(model, lw, store, reqs[0], budget_s=args.cpu_budget)
+        res["cpu_baseline"] = cpu_baseline()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
@@ -359,59 +367,114 @@ def run_ours(args):
 # ---------------------------------------------------------------------------
 # CPU baseline / reference arm: the oracle restatement of fuse_selective
 # ---------------------------------------------------------------------------
-class OracleTTFT:
-    """CPU TTFT of the reference's algorithm (the oracle, numpy fp32) on a layer
-    sample: the fixed part (concat, layers < check layer, check layer with HKVD,
-    final norm + lm_head) is timed once; each sample() times one sparse layer;
-    TTFT = fixed + sparse * (n_layers - check_layer - 1)."""
+class OracleBlend:
+    """One blended prefill of the reference's algorithm on the host cores (the
+    oracle restatement, numpy fp32, every core), as a list of units run in
+    order: concat + the full layers before the check layer; the check layer
+    (HKVD, top-K, force-include); one unit per sparse layer; the final norm +
+    lm_head + dense logits.  Running every unit once is one whole prefill, and
+    each unit's time is measured as it runs (nothing is extrapolated)."""
 
-    def __init__(self, W, ids, ck_k, ck_v, n_layers_full):
+    def __init__(self, W, ids, ck_k, ck_v, n_layers):
         from oracle import model as om
-        self.om, self.W, self.full = om, W, n_layers_full
-        t = time.perf_counter()
-        self.state = om.selective_begin(ids, ck_k, ck_v, W, RATIO, CHECK_LAYER, n_layers=CHECK_LAYER + 2)
-        hs = self.state.hs
-        om.selective_end(self.state, W)
-        self.t_fixed = time.perf_counter() - t
-        self.hs0 = hs
+        self.om, self.W, self.ids, self.ck_k, self.ck_v, self.L = om, W, ids, ck_k, ck_v, n_layers
+        self.prep = self.state = self.result = None
 
-    def sample(self):
-        self.state.hs = self.hs0
-        t = time.perf_counter()
-        self.om.selective_layer(self.state, CHECK_LAYER + 1, self.W, keep_cache=False)
-        t_sparse = time.perf_counter() - t
-        return self.t_fixed + t_sparse * (self.full - CHECK_LAYER - 1), t_sparse
+    def units(self):
+        om, W = self.om, self.W
 
+        def prep():
+            self.prep = om.selective_prepare(self.ids, self.ck_k, self.ck_v, W, CHECK_LAYER, self.L)
 
-def _oracle_weights_from_model(model, n_layers):
-    from oracle import model as om
-    cfg = om.Config.from_hf(model.config)
-    sd = {}
-    for n, t in model.state_dict().items():
-        if n.startswith("model.layers."):
-            if int(n.split(".")[2]) >= n_layers:
-                continue
-        sd[n] = t.float().cpu().numpy()
-    cfg.num_hidden_layers = n_layers
-    return om.Weights(sd, cfg, model.model.rotary_emb.inv_freq.float().cpu().numpy())
+        def check():
+            self.state = om.selective_check(self.prep, W, RATIO)
+            self.prep = None
+
+        def end():
+            self.result = om.selective_end(self.state, W)
+            self.state = None
+
+        sparse = [lambda l=l: om.selective_layer(self.state, l, W, keep_cache=False)
+                  for l in range(CHECK_LAYER + 1, self.L)]
+        return [prep, check] + sparse + [end]
 
 
-def cpu_baseline(model, lw, store, chunks, budget_s=30.0):
+def _mem_available_gb():
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) / 2 ** 20
+    except OSError:
+        pass
+    return 0.0
+
+
+def _synthetic_oracle_inputs(seed=0):
+    """Random-init Mistral-7B-shape weights (N(0, 0.02), unit norm weights) as
+    oracle fp32 arrays, the 7-chunk request's ids and per-layer chunk K / V
+    ~ N(0, 1).  With enough host memory every layer has its own weights (29
+    GB); otherwise the sparse layers 2..31 share one weight set and one chunk
+    K / V set (same shapes, so the same work per layer; a layer's weights are
+    0.87 GB, far larger than the host caches, so sharing them does not make a
+    layer faster).  Returns (W, ids, ck_k, ck_v, distinct)."""
     import numpy as np
-    nl = CHECK_LAYER + 2
-    W = _oracle_weights_from_model(model, nl)
-    ids = [np.asarray(c.token_ids) for c in chunks]
-    ents = [store.get(c.chunk_id) for c in chunks]
-    ck_k = [[e["K"][l][0].float().cpu().numpy() for l in range(nl)] for e in ents]
-    ck_v = [[e["V"][l][0].float().cpu().numpy() for l in range(nl)] for e in ents]
+    from oracle import model as om, threads
+    c = MISTRAL_7B
+    L = c["num_hidden_layers"]
+    H, I, kvd = c["hidden_size"], c["intermediate_size"], c["num_key_value_heads"] * c["head_dim"]
+    distinct = _mem_available_gb() >= 96
+    n_sets = L if distinct else CHECK_LAYER + 2
+    cfg = om.Config(c["vocab_size"], H, I, L, c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"],
+                    c["rope_theta"], c["rms_norm_eps"])
+
+    def w(seed_, *shape):
+        r = np.random.default_rng(seed_)
+        return r.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+
+    def layer(l):
+        b = 1000 * (l + 1) + seed
+        return {"q": w(b, H, H), "k": w(b + 1, kvd, H), "v": w(b + 2, kvd, H), "o": w(b + 3, H, H),
+                "gate": w(b + 4, I, H), "up": w(b + 5, I, H), "down": w(b + 6, H, I),
+                "ln1": np.ones(H, np.float32), "ln2": np.ones(H, np.float32)}
+
+    sets = threads.run([lambda l=l: layer(l) for l in range(n_sets)])
+    W = om.Weights.__new__(om.Weights)
+    W.cfg = cfg
+    W.embed, W.lm_head = threads.run([lambda: w(seed + 1, c["vocab_size"], H), lambda: w(seed + 2, c["vocab_size"], H)])
+    W.norm = np.ones(H, np.float32)
+    W.layers = [sets[min(l, n_sets - 1)] for l in range(L)]
+    W.inv_freq = __import__("oracle").hotpath.inv_freq(c["rope_theta"], c["head_dim"])
+    rng = np.random.default_rng(seed + 3)
+    lens = [CHUNK_LEN] * N_CHUNKS + [QUERY_LEN]
+    ids = [rng.integers(0, c["vocab_size"], n) for n in lens]
+    kv_sets = [[(rng.standard_normal((n, kvd), dtype=np.float32), rng.standard_normal((n, kvd), dtype=np.float32))
+                for n in lens] for _ in range(n_sets)]
+    ck_k = [[kv_sets[min(l, n_sets - 1)][i][0] for l in range(L)] for i in range(len(lens))]
+    ck_v = [[kv_sets[min(l, n_sets - 1)][i][1] for l in range(L)] for i in range(len(lens))]
+    return W, ids, ck_k, ck_v, distinct
+
+
+def _oracle_sample_text(distinct, cores):
+    return (f"the reference's fuse_selective restated by the oracle (numpy fp32, {cores} host threads) on the "
+            f"Mistral-7B 7K workload (S = 6208, ratio 0.15, 32 layers, random-init weights"
+            f"{'' if distinct else '; sparse layers 2..31 share one weight set'}); every unit of each "
+            f"prefill (concat + layer 0, check layer + HKVD, 30 sparse layers, lm_head) timed, none extrapolated")
+
+
+def cpu_baseline():
+    """Host-core baseline for the N=1 line: one whole blended prefill of the
+    reference's algorithm (oracle, every core), measured unit by unit."""
+    W, ids, ck_k, ck_v, distinct = _synthetic_oracle_inputs()
+    ob = OracleBlend(W, ids, ck_k, ck_v, MISTRAL_7B["num_hidden_layers"])
+    t = time.perf_counter()
+    for u in ob.units():
+        u()
+    ttft = time.perf_counter() - t
     S = sum(len(x) for x in ids)
-    o = OracleTTFT(W, ids, ck_k, ck_v, model.config.num_hidden_layers)
-    ttft, t_sparse = o.sample()
-    return {"value": round(S / ttft, 2), "unit": "tokens/s", "ttft_s": round(ttft, 3),
-            "cores": _blas_threads(), "kind": "port",
-            "sample": (f"oracle fuse_selective (numpy fp32) on the same request: fixed part (concat, "
-                       f"layer 0, check layer + HKVD, lm_head) {o.t_fixed:.2f} s once, one sparse "
-                       f"layer {t_sparse:.2f} s, TTFT extrapolated to {model.config.num_hidden_layers} layers")}
+    cores = _blas_threads()
+    return {"value": round(S / ttft, 2), "unit": "tokens/s", "ttft_s": round(ttft, 3), "cores": cores,
+            "kind": "port", "sample": "one prefill: " + _oracle_sample_text(distinct, cores)}
 
 
 def _blas_threads():
@@ -425,16 +488,15 @@ def _blas_threads():
 
 def run_reference(args):
     """Reference arm: the reference's algorithm (oracle restatement, numpy on the
-    host cores) on the same workload; each step is one layer-sampled blended
-    prefill with the TTFT extrapolated to 32 layers."""
-    import numpy as np
+    host cores) on the same workload."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
     # torchrun sets OMP_NUM_THREADS=1 for every rank; the reference arm runs on
     # rank 0 alone and may use every host core
     try:
         from threadpoolctl import threadpool_limits
-        limiter = threadpool_limits(limits=os.cpu_count() or 1)
+        from oracle import threads
+        limiter = threadpool_limits(limits=threads.n_threads())
     except Exception:
         limiter = None
     try:
@@ -445,50 +507,48 @@ def run_reference(args):
 
 
 def _run_reference(args):
-    import numpy as np
-    from oracle import model as om
-    rng = np.random.default_rng(0)
-    c = MISTRAL_7B
-    nl = CHECK_LAYER + 2
-    cfg = om.Config(c["vocab_size"], c["hidden_size"], c["intermediate_size"], nl,
-                    c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"], c["rope_theta"],
-                    c["rms_norm_eps"])
-    H, I, kvd = c["hidden_size"], c["intermediate_size"], c["num_key_value_heads"] * c["head_dim"]
-
-    def w(*shape):
-        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02))
-    sd = {"model.embed_tokens.weight": w(c["vocab_size"], H), "lm_head.weight": w(c["vocab_size"], H),
-          "model.norm.weight": np.ones(H, np.float32)}
-    for l in range(nl):
-        p = f"model.layers.{l}."
-        sd.update({p + "self_attn.q_proj.weight": w(H, H), p + "self_attn.k_proj.weight": w(kvd, H),
-                   p + "self_attn.v_proj.weight": w(kvd, H), p + "self_attn.o_proj.weight": w(H, H),
-                   p + "mlp.gate_proj.weight": w(I, H), p + "mlp.up_proj.weight": w(I, H),
-                   p + "mlp.down_proj.weight": w(H, I), p + "input_layernorm.weight": np.ones(H, np.float32),
-                   p + "post_attention_layernorm.weight": np.ones(H, np.float32)})
-    W = om.Weights(sd, cfg)
-    lens = [CHUNK_LEN] * N_CHUNKS + [QUERY_LEN]
-    ids = [rng.integers(0, c["vocab_size"], n) for n in lens]
-    ck_k = [[rng.standard_normal((n, kvd), dtype=np.float32) for _ in range(nl)] for n in lens]
-    ck_v = [[rng.standard_normal((n, kvd), dtype=np.float32) for _ in range(nl)] for n in lens]
-    S = sum(lens)
-    o = OracleTTFT(W, ids, ck_k, ck_v, c["num_hidden_layers"])
-    for _ in range(args.warmup):
-        o.sample()
-    ttfts = [o.sample()[0] for _ in range(args.steps)]
-    ttft = sum(ttfts) / len(ttfts)
-    value = round(S / ttft, 2)
+    """The K timed steps cover R = ceil(K / U) whole blended prefills of U units
+    each, split into K consecutive runs of units (step i runs units
+    [i*R*U/K, (i+1)*R*U/K) of the sequence), so every layer of every reported
+    prefill is timed; value = R * S / (time of the K steps).  The W warm-up
+    steps run one sparse-layer unit each on a separate prefill."""
+    W, ids, ck_k, ck_v, distinct = _synthetic_oracle_inputs()
+    L = MISTRAL_7B["num_hidden_layers"]
+    S = sum(len(x) for x in ids)
+    warm = OracleBlend(W, ids, ck_k, ck_v, L)
+    wu = warm.units()
+    wu[0]()
+    wu[1]()
+    for i in range(args.warmup):
+        wu[2 + i % (L - CHECK_LAYER - 1)]()
+    del warm, wu
+    U = L + 2
+    R = -(-args.steps // U)
+    seq = []
+    for _ in range(R):
+        seq += OracleBlend(W, ids, ck_k, ck_v, L).units()
+    bounds = [i * R * U // args.steps for i in range(args.steps + 1)]
+    step_s = []
+    t_all = time.perf_counter()
+    for i in range(args.steps):
+        t = time.perf_counter()
+        for u in seq[bounds[i]:bounds[i + 1]]:
+            u()
+        step_s.append(time.perf_counter() - t)
+    total = time.perf_counter() - t_all
+    value = round(R * S / total, 2)
     cores = _blas_threads()
-    sample = (f"oracle fuse_selective (numpy fp32, BLAS {cores} threads): fixed part (concat, layer 0, "
-              f"check layer + HKVD, lm_head) timed once ({o.t_fixed:.2f} s); each step times one sparse "
-              f"layer; TTFT = fixed + 30 x sparse")
+    sample = (f"{R} whole prefill(s) over the {args.steps} timed steps (each step runs the next "
+              f"{R * U / args.steps:.2f} of the {U} units in order): " + _oracle_sample_text(distinct, cores))
     print(json.dumps({
         "metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s",
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ttft * 1e3, 1), "ttft_ms": round(ttft * 1e3, 1), "higher_is_better": True,
+        "ms_per_step": round(total * 1e3 / args.steps, 1), "ttft_ms": round(total * 1e3 / R, 1),
+        "step_ms": [round(x * 1e3, 1) for x in step_s], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "mistral7b-7k-blend", "S": S, "recompute_ratio": RATIO,
-                   "check_layer": CHECK_LAYER, "parallelism": "host CPU"},
+                   "check_layer": CHECK_LAYER, "parallelism": "host CPU", "host_mem_available_gb":
+                   round(_mem_available_gb(), 1)},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -811,9 +871,12 @@ def run_llama8b_32k(args):
     pinned = [t.pin_memory() for t in ids]
     stream = torch.cuda.current_stream(device)
 
-    def one(i, src):
+    def one(i, src, graph=True):
+        # only the first token is needed: lm_head on the last position (the dense
+        # (1, S, vocab) logits would be 8.4 GB per request)
         logits = cb.fuse_selective(lw, reqs[i % n_distinct], store, recompute_ratio=L8_RATIO,
-                                   check_layer=CHECK_LAYER, input_ids=src[i % n_distinct])
+                                   check_layer=CHECK_LAYER, input_ids=src[i % n_distinct], logits_rows="last",
+                                   cuda_graph=None if graph else False)
         return logits[0, -1].argmax()
 
     def barrier():
@@ -836,8 +899,6 @@ def run_llama8b_32k(args):
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
-    TIMES.reset()
-    TIMES.active = True
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -846,12 +907,9 @@ def run_llama8b_32k(args):
             one(i, dev_ids)
     t1.record(stream)
     torch.cuda.synchronize()
-    TIMES.active = False
     barrier()
     clk = clocks.stop()
     ms = max_over_ranks(t0.elapsed_time(t1)) / args.steps
-    kern = TIMES.summary()
-    launches = sum(TIMES.launches.values())
     # end to end: host ids in (pinned), first token out, per request
     barrier()
     torch.cuda.synchronize()
@@ -859,6 +917,17 @@ def run_llama8b_32k(args):
     for i in range(per_rank):
         int(one(i, pinned).item())
     e2e_ms = max_over_ranks((time.perf_counter() - a) * 1e3)
+    # per-kernel CUDA events: one step's requests launched kernel by kernel
+    for i in range(min(per_rank, 2)):
+        one(i, dev_ids, graph=False)
+    torch.cuda.synchronize()
+    TIMES.reset()
+    TIMES.active = True
+    for i in range(per_rank):
+        one(i, dev_ids, graph=False)
+    TIMES.active = False
+    kern = TIMES.summary()
+    launches = sum(TIMES.launches.values()) * args.steps
     n_sp, ms_sp = kern.get("partial_attn", (0, 0.0))
     _, idx = cb.fuse_selective(lw, reqs[0], store, recompute_ratio=L8_RATIO, check_layer=CHECK_LAYER,
                                return_hkvd_indices=True)
@@ -877,7 +946,7 @@ def run_llama8b_32k(args):
                    "chunks": f"{L8_CHUNKS}x{L8_CHUNK_LEN}+{L8_QUERY_LEN}", "S": S, "recompute_ratio": L8_RATIO,
                    "k_selected": int(idx.numel()), "check_layer": CHECK_LAYER, "requests": L8_REQUESTS,
                    "requests_per_rank": per_rank, "distinct_requests_per_rank": n_distinct,
-                   "parallelism": f"by-request x{world}",
+                   "parallelism": f"by-request x{world}", "logits_rows": "last",
                    "l2": "inputs larger than L2 (16 GB weights, 4.3 GB fused KV per request)"},
         "e2e": {"value": round(L8_REQUESTS / (e2e_ms * 1e-3), 3), "unit": "requests/s",
                 "ms_per_step": round(e2e_ms, 1), "h2d_bytes_per_step": per_rank * S * 8,
@@ -1200,7 +1269,6 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--requests", type=int, default=1, help="distinct requests per rank (cycled)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-budget", type=float, default=30.0)
     ap.add_argument("--workload", default="mistral7b-7k-blend",
                     choices=["mistral7b-7k-blend", "kv-microbench", "attn-layers", "llama70b-128k-sharded",
                              "llama3-8b-32k-x64", "mistral7b-7k-decode", "decode-kernels"])
@@ -1211,7 +1279,8 @@ def main():
     ap.add_argument("--kv-layers", type=int, default=32, help="layers of the KV microbench")
     ap.add_argument("--kv-arena", action="store_true", help="chunk K/V in one KVArena device pool")
     ap.add_argument("--decode-tokens", type=int, default=32, help="tokens of the decode workload")
-    ap.add_argument("--no-cuda-graph", action="store_true", help="skip the BlendGraph replay measurement")
+    ap.add_argument("--no-cuda-graph", action="store_true",
+                    help="time fuse_selective(cuda_graph=False) (kernel by kernel) instead of the graph replay")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

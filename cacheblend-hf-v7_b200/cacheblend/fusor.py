@@ -193,11 +193,15 @@ def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_
     return attn.o_proj(a.unsqueeze(0)), k_pre
 
 
+_LOGITS_ROWS = ("all", "last")
+
+
 def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
                    recompute_ratio: float = 0.15, check_layer: int = 1,
                    return_layerwise_output: bool = False, return_hkvd_indices: bool = False,
                    rope_mode: str = "ref", status: torch.Tensor | None = None,
-                   input_ids: torch.Tensor | None = None):
+                   input_ids: torch.Tensor | None = None, logits_rows: str = "all",
+                   cuda_graph: bool | None = None):
     """CacheBlend selective recompute (reference fusor.py:193-497).
 
     Layers < check_layer: full forward.  Check layer: HKVD picks the
@@ -211,30 +215,135 @@ def fuse_selective(layerwise_model, chunks: list[Chunk], kv_store: KVStore,
     ``rope_mode`` "ref" reproduces HF's 16-bit RoPE rounding, "fp32" rotates in
     fp32 with one rounding.  ``status`` (int32 CUDA tensor) collects device-side
     error bits.  ``input_ids`` (1-D or (1, S) int64, host -- preferably pinned --
-    or device) replaces the ids gathered from ``chunks``."""
+    or device) replaces the ids gathered from ``chunks``.
+
+    ``logits_rows``: "all" (default) returns the reference's dense (1, S, vocab)
+    logits; "last" runs the final norm and lm_head on the last position only and
+    returns its logits as (1, 1, vocab) -- the only row a prefill's caller reads
+    (fusor.py:486-491 fills the other selected rows, runners decode from
+    [:, -1]); at 32K tokens and a 128K vocab the dense tensor is 8.4 GB.
+
+    ``cuda_graph``: None (default) or True replays a CUDA graph of the selective
+    path captured once per request geometry (chunk lengths, ratio, check layer,
+    RoPE mode, logits rows) and kept on the model (the two most recent
+    geometries); the first call of a geometry runs the path eagerly twice and
+    captures it.  Results are bit-identical to the eager path (False), and
+    every call returns new tensors.  After a replayed call the pre-RoPE K that
+    ``get_pre_rope_k`` returns lives in the graph's memory and is overwritten
+    by the next call of the same geometry."""
     if recompute_ratio == 0:
         return fuse_full_reuse(layerwise_model, chunks, kv_store, return_layerwise_output)
     if recompute_ratio >= 1:
         return fuse_full_recompute(layerwise_model, chunks, return_layerwise_output)
     if len(chunks) <= 1:
         return fuse_full_recompute(layerwise_model, chunks, return_layerwise_output)
-    pre = _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check_layer, rope_mode,
-                             status, input_ids, extra_tokens=0)
-    result = pre.logits
-    if return_layerwise_output:
-        result = LayerwiseOutput(logits=pre.logits, past_key_values=pre.dynamic_cache())
+    if logits_rows not in _LOGITS_ROWS:
+        raise ValueError(f"logits_rows must be one of {_LOGITS_ROWS}, got {logits_rows!r}")
+    if not 0 <= int(check_layer) < layerwise_model.num_layers:
+        raise IndexError(f"check_layer {check_layer} out of range for {layerwise_model.num_layers} layers")
+    graph = None
+    if cuda_graph is not False and _graphs_enabled(layerwise_model):
+        graph = _cached_graph(layerwise_model, chunks, kv_store, recompute_ratio, check_layer, rope_mode,
+                              logits_rows)
+    if graph is not None:
+        with torch.inference_mode():
+            pre = graph.replay(chunks, kv_store, input_ids)
+            layerwise_model._pre_rope_k = dict(graph.pre_rope_k)
+            if status is not None:
+                status.bitwise_or_(graph.status)
+            logits = _fresh_logits(pre, logits_rows)
+            idx = pre.idx.clone()
+            result = logits
+            if return_layerwise_output:
+                own = _Prefill(logits, pre.fused_k.clone(), pre.fused_v.clone(), idx, pre.geo, pre.S, pre.rope)
+                result = LayerwiseOutput(logits=logits, past_key_values=own.dynamic_cache())
+    else:
+        pre = _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check_layer, rope_mode,
+                                 status, input_ids, extra_tokens=0, logits_rows=logits_rows)
+        idx = pre.idx
+        result = pre.logits
+        if return_layerwise_output:
+            result = LayerwiseOutput(logits=pre.logits, past_key_values=pre.dynamic_cache())
     if return_hkvd_indices:
-        return result, pre.idx
+        return result, idx
     return result
+
+
+# CUDA graphs of the selective path, per model and request geometry
+GRAPH_CACHE_SIZE = 2
+
+
+def _graphs_enabled(lw) -> bool:
+    import os
+    if os.environ.get("CACHEBLEND_CUDA_GRAPH", "1") == "0":
+        return False
+    if getattr(lw, "device", torch.device("cpu")).type != "cuda":
+        return False
+    return not torch.cuda.is_current_stream_capturing()
+
+
+def _cached_graph(lw, chunks, kv_store, ratio, ck, rope_mode, logits_rows):
+    """The model's captured graph of this geometry (captured on first use), or
+    None when the path could not be captured (then the eager path runs)."""
+    from collections import OrderedDict
+    from cacheblend.graph import BlendGraph
+    cache = getattr(lw, "_cbk_graphs", None)
+    if cache is None:
+        cache = OrderedDict()
+        try:
+            lw._cbk_graphs = cache
+        except AttributeError:
+            return None
+    key = (tuple(c.length for c in chunks), float(ratio), int(ck), rope_mode, logits_rows, str(lw.device))
+    if key in cache:
+        cache.move_to_end(key)
+        return cache[key]
+    try:
+        g = BlendGraph(lw, chunks, kv_store, ratio, ck, rope_mode, logits_rows=logits_rows, dense_logits=False)
+    except (KeyError, ValueError, IndexError, NotImplementedError):
+        raise                              # the caller's error, as the eager path raises it
+    except RuntimeError:
+        g = None                           # not capturable here: eager from now on
+    cache[key] = g
+    while len(cache) > GRAPH_CACHE_SIZE:
+        cache.popitem(last=False)
+    return g
+
+
+def release_graphs(layerwise_model) -> None:
+    """Drop the CUDA graphs fuse_selective keeps on the model (and their memory)."""
+    cache = getattr(layerwise_model, "_cbk_graphs", None)
+    if cache is not None:
+        cache.clear()
+
+
+def _fresh_logits(pre, logits_rows):
+    """New logits tensor from a prefill's selected-row logits."""
+    ls = pre.logits_sparse
+    if logits_rows == "last":
+        return ls.clone()
+    return _dense_logits(ls, pre.idx, pre.S)
+
+
+def _dense_logits(logits_sparse, idx, S):
+    """(1, S, vocab) with the selected rows' logits and zeros elsewhere, one write
+    pass (rows whose byte length is not a multiple of 16 take torch's zeros +
+    index_copy_)."""
+    if (logits_sparse.shape[-1] * logits_sparse.element_size()) % 16 == 0:
+        return ops.scatter_rows(logits_sparse[0], idx, S).unsqueeze(0)
+    logits = torch.zeros((1, S, logits_sparse.shape[-1]), dtype=logits_sparse.dtype, device=logits_sparse.device)
+    logits[0].index_copy_(0, idx, logits_sparse[0])
+    return logits
 
 
 class _Prefill:
     """Result of a selective prefill: logits, the fused cache (capacity S + extra
     rows per layer, the first S filled) and the selection."""
 
-    def __init__(self, logits, fused_k, fused_v, idx, geo, S, rope):
+    def __init__(self, logits, fused_k, fused_v, idx, geo, S, rope, logits_sparse=None):
         self.logits, self.fused_k, self.fused_v, self.idx = logits, fused_k, fused_v, idx
         self.geo, self.S, self.rope = geo, S, rope
+        self.logits_sparse = logits_sparse      # (1, k or 1, vocab): the rows lm_head ran on
 
     def dynamic_cache(self):
         g, S = self.geo, self.S
@@ -245,10 +354,14 @@ class _Prefill:
 
 
 def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check_layer, rope_mode, status,
-                       input_ids, extra_tokens: int = 0, table=None) -> _Prefill:
+                       input_ids, extra_tokens: int = 0, table=None, logits_rows: str = "all",
+                       dense_logits: bool = True) -> _Prefill:
     """Body of fuse_selective's selective path; the fused cache gets extra_tokens
     spare rows per layer (room for decode).  ``table``: a prebuilt chunk table
-    of layers check_layer.. (a captured graph keeps one and refreshes it)."""
+    of layers check_layer.. (a captured graph keeps one and refreshes it).
+    ``logits_rows`` "last": lm_head on the last position only; with
+    ``dense_logits`` False the (1, S, vocab) tensor is not formed (the caller
+    forms it from ``logits_sparse``)."""
     lw = layerwise_model
     inner = lw._inner
     n_layers = lw.num_layers
@@ -357,15 +470,18 @@ def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check
                 m = _mlp(layer, _norm(layer.post_attention_layernorm, hs, delta=a, sum_out=hs, status=status),
                          w_gu)
 
-            logits_sparse = lw.model.lm_head(_norm(inner.norm, hs, delta=m, status=status))   # (1, k, vocab)
-            # dense (1, S, vocab) with zero rows outside the selection, one write pass
-            # (rows whose byte length is not a multiple of 16 take torch's zeros + index_copy_)
-            if (logits_sparse.shape[-1] * logits_sparse.element_size()) % 16 == 0:
-                logits = ops.scatter_rows(logits_sparse[0], idx, S).unsqueeze(0)
+            if logits_rows == "last":       # idx is ascending and holds S - 1: the last selected row
+                hs_out = _norm(inner.norm, hs[:, -1:], delta=m[:, -1:], status=status)
             else:
-                logits = torch.zeros((1, S, logits_sparse.shape[-1]), dtype=logits_sparse.dtype, device=device)
-                logits[0].index_copy_(0, idx, logits_sparse[0])
+                hs_out = _norm(inner.norm, hs, delta=m, status=status)
+            logits_sparse = lw.model.lm_head(hs_out)            # (1, k or 1, vocab)
+            if not dense_logits:
+                logits = None
+            elif logits_rows == "last":
+                logits = logits_sparse
+            else:
+                logits = _dense_logits(logits_sparse, idx, S)
         finally:
             cur.wait_event(assembled)
 
-    return _Prefill(logits, fused_k, fused_v, idx, geo, S, rope)
+    return _Prefill(logits, fused_k, fused_v, idx, geo, S, rope, logits_sparse)

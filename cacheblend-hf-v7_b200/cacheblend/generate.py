@@ -148,8 +148,9 @@ def generate_greedy(layerwise_model, chunks: list[Chunk], kv_store: KVStore, max
                 step = lw.model(input_ids=nxt.view(1, 1), past_key_values=cache, use_cache=True)
                 cache, row = step.past_key_values, step.logits[0, -1]
         else:
+            # only the last prefill row is read: lm_head on that row alone
             pre = _selective_prefill(lw, chunks, kv_store, recompute_ratio, check_layer, rope_mode, status,
-                                     None, extra_tokens=max_new_tokens)
+                                     None, extra_tokens=max_new_tokens, logits_rows="last")
             st = _DecodeState(lw, pre, max_new_tokens, pre.logits[0, -1], return_logits)
             n_steps = max_new_tokens - 1
             if n_steps >= 1:

@@ -179,6 +179,22 @@ class ChunkTable:
         return self.srcs.data_ptr() + li * self.n_chunks * 16
 
 
+def chunk_signature(entries: Sequence[dict], layers: Sequence[int]) -> tuple:
+    """Device addresses of the store entries' K/V tensors of `layers` (for
+    KVArena entries, their slab): equal signatures mean a ChunkTable built from
+    either set of entries holds the same pointers.  (A table keeps its tensors
+    alive, so a stored tensor that replaced one of them cannot have its address.)"""
+    sig = []
+    for e in entries:
+        slab = e.get("_slab")
+        if slab is not None:
+            sig.append(slab)
+        else:
+            K, V = e["K"], e["V"]
+            sig.append(tuple(K[l].data_ptr() for l in layers) + tuple(V[l].data_ptr() for l in layers))
+    return tuple(sig)
+
+
 def _chunk_rows(t: torch.Tensor, device) -> torch.Tensor:
     if t.device != device:
         raise RuntimeError(f"chunk tensor on {t.device}, model on {device}")

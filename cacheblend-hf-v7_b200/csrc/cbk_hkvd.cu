@@ -341,8 +341,10 @@ extern "C" int cbk_hkvd_select(const void* k_new, int64_t new_row_stride,
 //
 // The array's host-side name is only a stand-in for the device address, so the
 // address is looked up with cudaGetSymbolAddress once per device, on the first
-// call made with that device current; make that first call before any stream
-// capture.  All calls share the array and it keeps the previous call's
+// call made with that device current, and kept for the process; make that
+// first call before any stream capture.  A device reset (cudaDeviceReset or a
+// primary-context reset) reloads the module and may move the array, leaving
+// the kept address stale: the entry point is not for use after a reset.  All calls share the array and it keeps the previous call's
 // contents; nothing in it is read before this call writes it (positions
 // [0, S) are written by the deviation kernel before the top-K kernel reads
 // them), so nothing needs clearing.  Calls that overlap on the GPU (two streams,

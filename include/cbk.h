@@ -118,10 +118,14 @@ int cbk_rope_scatter(const void* q_src, int64_t q_row_stride, const void* k_src,
                      void* q_out, void* k_cache, void* v_cache, int32_t* status, void* stream);
 
 /* (c) HKVD deviation (hkvd.py:23-55, kv_deviation):
- *   dev[t] = sum_f (K_new[t][f] - K_old[t][f])^2 in fp32, fixed order
- * (see the kernel for the exact order).  K_new rows have stride new_row_stride
- * elements; K_old rows come from the chunk table (srcs[c].k, c < n_chunks,
- * rows chunk_start[c] .. chunk_start[c+1]). */
+ *   dev[t] = sum_f (K_new[t][f] - K_old[t][f])^2 in fp32, fixed order: each
+ * 8-element vector's squares summed in element order, then a complete binary
+ * tree of pairwise adds over the vectors (zero-padded to a power of two).  The
+ * deviation of an aligned power-of-two slice of the features (one rank's KV
+ * heads) is a node of that tree, so slices combined with the same tree give
+ * these bits exactly.  K_new rows have stride new_row_stride elements; K_old
+ * rows come from the chunk table (srcs[c].k, c < n_chunks, rows
+ * chunk_start[c] .. chunk_start[c+1]).  feat % 8 == 0, feat < 2^27. */
 int cbk_kv_deviation(const void* k_new, int64_t new_row_stride, const cbk_chunk_src* old_srcs,
                      const int64_t* chunk_start, int n_chunks, int64_t S, int64_t feat,
                      int dtype, float* dev, void* stream);
@@ -153,8 +157,11 @@ int cbk_hkvd_select(const void* k_new, int64_t new_row_stride, const cbk_chunk_s
  * synchronise the device).  No counterpart in the reference.  Same arguments
  * and results as cbk_hkvd_select without the workspace; S above the maximum is
  * rejected (CBK_ERR_INVALID).  The first call on a device looks up the array's
- * address (make it before any stream capture); calls that overlap on the GPU
- * share the array and race. */
+ * address (make it before any stream capture) and keeps it for the process; a
+ * device reset (cudaDeviceReset, or a reset of the primary context) reloads the
+ * module and invalidates that address, so do not call this entry point on a
+ * device after resetting it.  Calls that overlap on the GPU share the array and
+ * race. */
 int64_t cbk_hkvd_noalloc_max_tokens(void);
 int cbk_hkvd_select_noalloc(const void* k_new, int64_t new_row_stride, const cbk_chunk_src* old_srcs,
                             const int64_t* chunk_start, int n_chunks, int64_t S, int64_t feat,

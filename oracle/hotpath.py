@@ -245,6 +245,37 @@ def partial_attention(q, k, v, pos, scale, dtype=np.float64, with_abs=False, hea
     return out.reshape(n, Hq * D)
 
 
+def partial_attention_f32(q, k, v, pos, scale):
+    """fp32 partial_attention for the model replay: the same softmax attention,
+    computed per (q head, block of query rows) on all host cores; a block's
+    keys stop at its largest position (keys past it are masked for every row
+    of the block).  q: (n, Hq, D); k, v: (S, Hkv, D); pos ascending.  Returns
+    (n, Hq*D) fp32."""
+    from oracle import threads
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    v = np.asarray(v, np.float32)
+    n, Hq, D = q.shape
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    pos = np.asarray(pos, np.int64)
+    out = np.empty((n, Hq, D), np.float32)
+    kh = [np.ascontiguousarray(k[:, g, :]) for g in range(Hkv)]
+    vh = [np.ascontiguousarray(v[:, g, :]) for g in range(Hkv)]
+    rb = 256
+
+    def block(h, r0, r1):
+        pm = int(pos[r0:r1].max()) + 1
+        s = (q[r0:r1, h, :] @ kh[h // G][:pm].T) * np.float32(scale)
+        s[np.arange(pm)[None, :] > pos[r0:r1, None]] = -np.inf
+        s -= s.max(axis=1, keepdims=True)
+        np.exp(s, out=s)
+        out[r0:r1, h, :] = (s @ vh[h // G][:pm]) / s.sum(axis=1, keepdims=True)
+
+    threads.run([lambda h=h, r0=r0: block(h, r0, min(n, r0 + rb)) for h in range(Hq) for r0 in range(0, n, rb)])
+    return out.reshape(n, Hq * D)
+
+
 def encode(x, dtype):
     return ENCODE[dtype](x)
 

@@ -65,9 +65,18 @@ def rmsnorm(x, w, eps):
 
 
 def mlp(x, L):
+    """SiLU-gated MLP; the elementwise SiLU * up runs over row blocks on all
+    host cores."""
+    from oracle import threads
     g = x @ L["gate"].T
     u = x @ L["up"].T
-    a = (g / (1.0 + np.exp(-g))).astype(np.float32) * u
+    a = np.empty_like(g)
+
+    def silu_mul(r0, r1):
+        gg = g[r0:r1]
+        a[r0:r1] = (gg / (1.0 + np.exp(-gg))).astype(np.float32) * u[r0:r1]
+
+    threads.run([lambda r0=r0, r1=r1: silu_mul(r0, r1) for r0, r1 in threads.row_chunks(g.shape[0])])
     return (a @ L["down"].T).astype(np.float32)
 
 
@@ -76,14 +85,19 @@ def _heads(x, D):
 
 
 def rope(x, pos, W: Weights):
-    return hp.apply_rope(x, pos, W.inv_freq, W.cfg.head_dim, dtype="f32", mode="ref")
+    """RoPE in fp32 (the model replay's precision), over row blocks on all host cores."""
+    from oracle import threads
+    pos = np.asarray(pos)
+    parts = threads.run([lambda r0=r0, r1=r1: hp.apply_rope(x[r0:r1], pos[r0:r1], W.inv_freq, W.cfg.head_dim,
+                                                            dtype="f32", mode="ref")
+                         for r0, r1 in threads.row_chunks(x.shape[0], 256)])
+    return np.concatenate(parts, axis=0) if len(parts) > 1 else parts[0]
 
 
 def attention(q_post, k_post, v, pos_q, W: Weights):
-    """GQA causal attention of query rows (positions pos_q) over all keys."""
+    """GQA causal attention of query rows (positions pos_q, ascending) over all keys."""
     D = W.cfg.head_dim
-    o = hp.partial_attention(_heads(q_post, D), _heads(k_post, D), _heads(v, D), pos_q,
-                             D ** -0.5, dtype=np.float32)
+    o = hp.partial_attention_f32(_heads(q_post, D), _heads(k_post, D), _heads(v, D), pos_q, D ** -0.5)
     return o.astype(np.float32)
 
 
@@ -146,22 +160,38 @@ def selective_begin(chunk_ids, chunk_k, chunk_v, W: Weights, recompute_ratio=0.1
                     force_idx=None, n_layers=None) -> SelectiveState:
     """fusor.py:258-406: concat of the cached K/V, the dense layers before the
     check layer, HKVD + force-include, and the check layer itself."""
-    c = W.cfg
+    prep = selective_prepare(chunk_ids, chunk_k, chunk_v, W, check_layer, n_layers)
+    return selective_check(prep, W, recompute_ratio, force_idx)
+
+
+def selective_prepare(chunk_ids, chunk_k, chunk_v, W: Weights, check_layer=1, n_layers=None) -> dict:
+    """First part of selective_begin: the concat of every layer's cached K/V
+    (fusor.py:258-272), the embedding and the full layers before the check
+    layer (fusor.py:313-323)."""
     ck = check_layer
-    nl = c.num_hidden_layers if n_layers is None else n_layers
+    nl = W.cfg.num_hidden_layers if n_layers is None else n_layers
     ids = np.concatenate([np.asarray(x, np.int64) for x in chunk_ids])
     S = len(ids)
     pos_full = np.arange(S)
-    # (a) concat of every layer's cached K_pre / V (fusor.py:258-272)
     K_st = [hp.concat_chunks([chunk_k[i][l] for i in range(len(chunk_ids))]) for l in range(nl)]
     V_st = [hp.concat_chunks([chunk_v[i][l] for i in range(len(chunk_ids))]) for l in range(nl)]
     h = W.embed[ids]
     cache_k, cache_v = [], []
-    for l in range(ck):                                   # fusor.py:313-323
+    for l in range(ck):
         h, _, v, kpost = dense_layer(h, W.layers[l], pos_full, W)
         cache_k.append(kpost)
         cache_v.append(v)
-    # check layer (fusor.py:326-406)
+    return {"S": S, "ck": ck, "h": h, "K_st": K_st, "V_st": V_st, "cache_k": cache_k, "cache_v": cache_v}
+
+
+def selective_check(prep: dict, W: Weights, recompute_ratio=0.15, force_idx=None) -> SelectiveState:
+    """Second part of selective_begin: the check layer (fusor.py:326-406) --
+    HKVD on the pre-RoPE K, top-K with force-include, the mixed K/V, the
+    selected queries' attention and MLP."""
+    c = W.cfg
+    S, ck, h, K_st, V_st = prep["S"], prep["ck"], prep["h"], prep["K_st"], prep["V_st"]
+    cache_k, cache_v = prep["cache_k"], prep["cache_v"]
+    pos_full = np.arange(S)
     L = W.layers[ck]
     hn = rmsnorm(h, L["ln1"], c.rms_norm_eps)
     q, k_pre, v = hn @ L["q"].T, hn @ L["k"].T, hn @ L["v"].T

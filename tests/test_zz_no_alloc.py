@@ -63,9 +63,14 @@ def _select_noalloc(N, new, table, S, feat, k):
     return idx, st
 
 
-def test_noalloc_hkvd_matches_allocating_entry_point_twice():
+@pytest.mark.parametrize("cases", [
+    [([1024] * 6 + [64], 1024, 1), ([128] * 4 + [32], 256, 2)],          # 2nd call: shorter S
+    # above the top-K kernel's shared-memory key cache (40960 keys: the scores are
+    # read back from the scratch array itself), then the scratch array's full length
+    [([20481, 20481], 128, 4), ([65536] * 4, 128, 5)],
+])
+def test_noalloc_hkvd_matches_allocating_entry_point_twice(cases):
     from cacheblend import _native as N
-    cases = [([1024] * 6 + [64], 1024, 1), ([128] * 4 + [32], 256, 2)]   # 2nd call: shorter S
     for lengths, feat, seed in cases:
         new, table, S = _case(lengths, feat, seed)
         k = int(N.LIB.cbk_topk_count(S, 0.15))
@@ -75,6 +80,8 @@ def test_noalloc_hkvd_matches_allocating_entry_point_twice():
         assert int(sa.item()) == 0 and int(sb.item()) == 0
         np.testing.assert_array_equal(b.cpu().numpy(), a.cpu().numpy())
         assert int(b[-1]) == S - 1
+    if sum(cases[-1][0]) == 4 * 65536:
+        assert sum(cases[-1][0]) == int(N.LIB.cbk_hkvd_noalloc_max_tokens())
 
 
 def test_noalloc_rejects_sequences_beyond_its_scratch():
