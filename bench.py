@@ -231,22 +231,36 @@ def run_ours(args):
     barrier()
     e2e_step = max_over_ranks(sum(e2e_ms) / len(e2e_ms))
 
-    # --- the same steps launched kernel by kernel: per-kernel CUDA events -------
-    # (the kernels a replayed graph runs, timed on their launch streams; the
-    # roofline below comes from this region)
+    # --- the same steps launched kernel by kernel from Python (context) ----------
     for i in range(args.warmup):
         step(i, graph=False)
     torch.cuda.synchronize()
-    TIMES.reset()
-    TIMES.active = True
     eager_ms = device_timed(lambda i: step(i, graph=False))
-    TIMES.active = False
-    kern = TIMES.summary()
-    launch_counts = dict(TIMES.launches)
     eager_res = {"ms_per_step": round(eager_ms / args.steps, 3),
                  "tokens_per_s": round(world * S * args.steps / (eager_ms * 1e-3), 1),
-                 "how": "fuse_selective(cuda_graph=False): every kernel launched from Python, each wrapped in "
-                        "CUDA events (the per-kernel figures and the roofline come from this region)"}
+                 "how": "fuse_selective(cuda_graph=False): every kernel launched from Python"}
+
+    # --- per-kernel device times inside the graph --------------------------------
+    # A second capture of the same geometry with an external CUDA event around
+    # every libcbk launch (event-record nodes of the graph); each replay is
+    # followed by a synchronize and the events are read: each kernel's own
+    # duration as the graph runs it, on its launch stream, with no host gaps.
+    TIMES.reset()
+    TIMES.active = True
+    tg = cb.BlendGraph(lw, reqs[0], store, recompute_ratio=RATIO, check_layer=CHECK_LAYER, dense_logits=False)
+    TIMES.active = False
+    spans = list(TIMES.graph_spans)
+    TIMES.reset()
+    acc = {}
+    for i in range(args.steps):
+        tg.replay(reqs[i % len(reqs)], store, input_ids=dev_ids[i % len(reqs)])
+        torch.cuda.synchronize()
+        TIMES.read_graph_spans(spans, acc)
+    del tg
+    kern = {name: (v[0], v[1]) for name, v in acc.items()}
+    # the graph's launches plus the dense-logits scatter fuse_selective runs after the replay
+    launch_counts = {name: v[2] for name, v in acc.items()}
+    launch_counts["scatter_rows"] = launch_counts.get("scatter_rows", 0) + args.steps
 
     # --- kernel accounting -----------------------------------------------------
     _, idx = cb.fuse_selective(lw, reqs[0], store, recompute_ratio=RATIO, check_layer=CHECK_LAYER,
@@ -327,7 +341,8 @@ def run_ours(args):
                      "traffic_src": ("dram bytes per launch read from the committed ncu summary "
                                      "profiles/partial_attn_kernel_mistral7b_7k_blend_traffic.json, not measured "
                                      "in this run") if traffic else None,
-                     "timed_in": "the kernel-by-kernel region (eager_launches)"},
+                     "timed_in": ("CUDA events captured as graph nodes around each launch, read after each of "
+                                  f"{args.steps} replays of the step's graph")},
         "kernels": {
             "assemble_kv": {"calls": n_asm, "avg_ms": round(asm_ms / max(n_asm, 1), 4),
                             "bytes": asm_bytes,
@@ -337,8 +352,8 @@ def run_ours(args):
                             "GB/s": gbs(hk_bytes, n_hk, hk_ms)[0], "frac_hbm": gbs(hk_bytes, n_hk, hk_ms)[1]},
             "rope_scatter": {"calls": n_sc, "avg_ms": round(sc_ms / max(n_sc, 1), 4),
                              "bytes_sparse_layer": sc_bytes_sparse, "bytes_per_step": sc_bytes_step,
-                             "GB/s": gbs(sc_bytes_step * n_sc / max(L, 1), n_sc, sc_ms)[0],
-                             "frac_hbm": gbs(sc_bytes_step * n_sc / max(L, 1), n_sc, sc_ms)[1]},
+                             "GB/s": gbs(sc_bytes_step / L, n_sc, sc_ms)[0],
+                             "frac_hbm": gbs(sc_bytes_step / L, n_sc, sc_ms)[1]},
             "partial_attn_sparse": {"calls": n_sp, "avg_ms": round(ms_sp / max(n_sp, 1), 4),
                                     "flops_per_call": fl_sp,
                                     "TFLOP/s": round(tf_sp, 1) if tf_sp else None},
@@ -348,8 +363,8 @@ def run_ours(args):
             "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_src,
         },
         "gpu_launches": launches,
-        "gpu_launches_note": "libcbk launches counted in the kernel-by-kernel region over the same number of "
-                             "steps; the replayed graph of the timed region holds the same launches",
+        "gpu_launches_note": ("libcbk launches of the timed steps: the launches captured in the step's graph "
+                              "times the steps, plus the dense-logits scatter run after each replay"),
         "clocks": clk,
         "eager_launches": eager_res,
         "timed_path": ("fuse_selective default: a CUDA graph of the request geometry, captured on the first "
@@ -917,17 +932,24 @@ def run_llama8b_32k(args):
     for i in range(per_rank):
         int(one(i, pinned).item())
     e2e_ms = max_over_ranks((time.perf_counter() - a) * 1e3)
-    # per-kernel CUDA events: one step's requests launched kernel by kernel
-    for i in range(min(per_rank, 2)):
-        one(i, dev_ids, graph=False)
-    torch.cuda.synchronize()
+    # per-kernel device times inside the graph: a second capture of the request
+    # geometry with external CUDA events around every libcbk launch, read after
+    # each replay (one step's requests)
     TIMES.reset()
     TIMES.active = True
-    for i in range(per_rank):
-        one(i, dev_ids, graph=False)
+    tg = cb.BlendGraph(lw, reqs[0], store, recompute_ratio=L8_RATIO, check_layer=CHECK_LAYER,
+                       logits_rows="last", dense_logits=False)
     TIMES.active = False
-    kern = TIMES.summary()
-    launches = sum(TIMES.launches.values()) * args.steps
+    spans = list(TIMES.graph_spans)
+    TIMES.reset()
+    acc = {}
+    for i in range(per_rank):
+        tg.replay(reqs[i % n_distinct], store, input_ids=dev_ids[i % n_distinct])
+        torch.cuda.synchronize()
+        TIMES.read_graph_spans(spans, acc)
+    del tg
+    kern = {name: (v[0], v[1]) for name, v in acc.items()}
+    launches = sum(v[2] for v in acc.values()) * args.steps
     n_sp, ms_sp = kern.get("partial_attn", (0, 0.0))
     _, idx = cb.fuse_selective(lw, reqs[0], store, recompute_ratio=L8_RATIO, check_layer=CHECK_LAYER,
                                return_hkvd_indices=True)
@@ -1011,9 +1033,14 @@ def run_kv_sharded(args):
         g = torch.Generator(device=device).manual_seed(seed)
         return torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(bf)
 
+    def heads(seed_of, h_lo, h_hi):
+        """(S, (h_hi - h_lo) * D) bf16: KV head h's columns seeded by seed_of(h), so the
+        whole-model data (and the selection) is the same for every rank count"""
+        return torch.cat([randn((S, D), seed_of(h)) for h in range(h_lo, h_hi)], dim=1)
+
     # per-layer chunk K/V of this rank's heads (chunks are row ranges of one buffer)
-    ck_k = [randn((S, kvd), 10_000 * rank + 2 * l) for l in range(L)]
-    ck_v = [randn((S, kvd), 10_000 * rank + 2 * l + 1) for l in range(L)]
+    ck_k = [heads(lambda h, l=l: 1_000_000 * h + 2 * l, lo, hi) for l in range(L)]
+    ck_v = [heads(lambda h, l=l: 1_000_000 * h + 2 * l + 1, lo, hi) for l in range(L)]
     starts = [0]
     for n in lens:
         starts.append(starts[-1] + n)
@@ -1028,8 +1055,8 @@ def run_kv_sharded(args):
     # (the token mask is common to all ranks: the same tokens are recomputed)
     gm = torch.Generator(device=device).manual_seed(77)
     mask = (torch.rand((S, 1), generator=gm, device=device) < 0.2).float()
-    k_fresh = (ck_k[ck].float() + randn((S, kvd), 10_000 * rank + 9_999).float() * 0.05 * mask).to(bf)
-    del mask
+    noise_seed = lambda h: 1_000_000 * h + 999_999
+    k_fresh = (ck_k[ck].float() + heads(noise_seed, lo, hi).float() * 0.05 * mask).to(bf)
     q_all, k_all, v_all = randn((S, hq * D), 5 + rank), randn((S, kvd), 6 + rank), randn((S, kvd), 7 + rank)
     q_rows, k_rows, v_rows = q_all[:k_sel], k_all[:k_sel], v_all[:k_sel]
     pos_all = torch.arange(S, device=device, dtype=torch.int64)
@@ -1074,12 +1101,25 @@ def run_kv_sharded(args):
     for _ in range(args.warmup):
         idx = step(k_fresh)
     torch.cuda.synchronize()
-    # every rank must hold the identical selection
+    # every rank must hold the identical selection ...
     same = True
     if world > 1:
         allidx = torch.empty((world, k_sel), dtype=torch.int64, device=device)
         dist.all_gather_into_tensor(allidx, idx)
         same = bool((allidx == allidx[0:1]).all().item())
+    # ... and it must be the selection one GPU makes from all heads: rank 0 rebuilds
+    # the check layer's fresh and cached K of every head and runs the unsharded HKVD
+    single = None
+    if rank == 0:
+        k_old_all = heads(lambda h: 1_000_000 * h + 2 * ck, 0, Hkv)
+        k_new_all = (k_old_all.float() + heads(noise_seed, 0, Hkv).float() * 0.05 * mask).to(bf)
+        ent_all = [{"K": [k_old_all[a:b].unsqueeze(0)], "V": [k_old_all[a:b].unsqueeze(0)]}
+                   for a, b in zip(starts, starts[1:])]
+        dev_all = ops.kv_deviation_rows(k_new_all, ops.ChunkTable(ent_all, [0], device), 0)
+        single = bool(torch.equal(ops.topk_select(dev_all, k_sel, force_last=True), idx))
+        del k_old_all, k_new_all, ent_all, dev_all
+    del mask
+    sel_digest = int(torch.sum(idx * torch.arange(1, k_sel + 1, device=device)).item())
 
     clocks = Clocks(local)
     barrier()
@@ -1136,8 +1176,10 @@ def run_kv_sharded(args):
         "config": {"workload": "llama70b-128k-sharded", "layers": L, "S": S, "k_selected": k_sel,
                    "chunks": f"{SH_CHUNKS}x{SH_CHUNK_LEN}+{SH_QUERY_LEN}", "q_heads_per_rank": hq,
                    "kv_heads_per_rank": hkv, "head_dim": D, "check_layer": ck,
-                   "parallelism": f"kv-heads/{world}", "exchange": "NCCL all_gather of S fp32 partials",
-                   "selection_identical_on_all_ranks": same, "status": st,
+                   "parallelism": f"kv-heads/{world}",
+                   "exchange": "NCCL all_gather of S fp32 partials, combined by the deviation's pairwise tree",
+                   "selection_identical_on_all_ranks": same, "selection_equals_single_gpu": single,
+                   "selection_digest": sel_digest, "status": st,
                    "l2": "inputs larger than L2 (per-layer K/V buffers)"},
         "e2e": {"value": round(S / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": S * kvd * 2, "d2h_bytes_per_step": k_sel * 8},

@@ -17,6 +17,7 @@ CBK_ERR_CUDA = -3
 CBK_ERR_WORKSPACE = -4
 CBK_BF16, CBK_F16 = 0, 1
 CBK_ROPE_REF, CBK_ROPE_FP32 = 0, 1
+CBK_ROPE_TABLE_BY_ROW = 16
 CBK_STATUS_BAD_INDEX, CBK_STATUS_TIMEOUT, CBK_STATUS_COUNT = 1, 2, 4
 
 _vp, _i32, _i64, _f32, _f64, _sz = (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float,

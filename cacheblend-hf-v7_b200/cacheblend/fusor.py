@@ -180,14 +180,15 @@ def _qkv(attn, hn, w_qkv=None):
 
 
 def _attention_block(layer, geo, hn, pos, S, rope, kc, vc, gather, status, rope_mode, ws, reuse,
-                     tag="", w_qkv=None):
+                     tag="", w_qkv=None, rope_by_row=False):
     """q/k/v projections -> (b)+(d) RoPE + scatter into the fused cache ->
     (e) partial attention -> o_proj.  Returns the attention output rows and the
-    pre-RoPE K (which the k_proj hook records when k_proj runs on its own)."""
+    pre-RoPE K (which the k_proj hook records when k_proj runs on its own).
+    ``rope_by_row``: ``rope`` holds the cos/sin of pos[j] in row j."""
     attn = layer.self_attn
     q, k_pre, v = _qkv(attn, hn, w_qkv)
     q_rot = ops.rope_scatter(q[0], k_pre[0], v[0], pos, gather, S, geo.n_q, geo.n_kv, geo.head_dim,
-                             rope, kc, vc, mode=rope_mode, status=status)
+                             rope, kc, vc, mode=rope_mode, status=status, table_by_row=rope_by_row)
     a = ops.partial_attn(q_rot, kc, vc, pos, geo.n_q, geo.n_kv, geo.head_dim, geo.scaling,
                          status=status, workspace=ws, reuse_plan=reuse, timer_tag=tag)
     return attn.o_proj(a.unsqueeze(0)), k_pre
@@ -396,14 +397,19 @@ def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check
             fused_k[:, S:].zero_()
             fused_v[:, S:].zero_()
 
-        # (a)+(b): all cached layers in one launch, overlapped with layers < ck
+        # (a)+(b): all cached layers in one launch on a side stream.  It starts once the
+        # last full layer's attention has been issued (at once when check_layer is 0),
+        # so this HBM-bound copy overlaps that layer's MLP GEMMs and the check layer's
+        # projections, and the attention kernel has the SMs to itself.
         side = _side_stream(lw, device)
-        side.wait_stream(cur)
-        with torch.cuda.stream(side):
-            ops.assemble_kv(table, ck, n_layers, geo.n_kv, geo.head_dim, rope, fused_k, fused_v,
-                            mode=rope_mode, status=status)
         assembled = torch.cuda.Event()
-        assembled.record(side)
+
+        def launch_assemble():
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                ops.assemble_kv(table, ck, n_layers, geo.n_kv, geo.head_dim, rope, fused_k, fused_v,
+                                mode=rope_mode, status=status)
+            assembled.record(side)
         # No record_stream: the current stream waits for `assembled` below, before
         # anything can free these buffers, so their memory returns to the caching
         # allocator in stream order.  (record_stream would hold it until the side
@@ -412,7 +418,9 @@ def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check
 
         # the side stream writes fused_k / fused_v until `assembled`: whatever
         # happens below, the current stream is ordered after it before they can
-        # be freed
+        # be freed (waiting on an event that was never recorded is a no-op)
+        if ck == 0:
+            launch_assemble()
         try:
             if input_ids is None:
                 ids = fused_input_ids(chunks, device=device)
@@ -433,6 +441,8 @@ def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check
                 a, _ = _attention_block(layer, geo, hn, pos_all, S, rope,
                                         fk[li], fv[li], False, status, rope_mode, ws_dense, li > 0,
                                         tag="_dense")
+                if li == ck - 1:
+                    launch_assemble()
                 m = _mlp(layer, _norm(layer.post_attention_layernorm, h, delta=a, sum_out=h, status=status))
 
             # check layer: full-row K, HKVD, then sparse from here on
@@ -447,9 +457,12 @@ def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check
             q = attn.q_proj(hn_sel)
             v = attn.v_proj(hn_sel)
             k_rows = k_pre.index_select(1, idx)
+            # cos/sin of the selected positions, one row per selected token: every
+            # later rope_scatter reads them without waiting for the positions
+            rope_sel = rope.index_select(0, idx)
             cur.wait_event(assembled)
             q_rot = ops.rope_scatter(q[0], k_rows[0], v[0], idx, False, S, geo.n_q, geo.n_kv, geo.head_dim,
-                                     rope, fk[ck], fv[ck], mode=rope_mode, status=status)
+                                     rope_sel, fk[ck], fv[ck], mode=rope_mode, status=status, table_by_row=True)
             ws_sparse = ops.attn_workspace(k_sel, S, geo.n_q, geo.n_kv, geo.head_dim, device)
             a = ops.partial_attn(q_rot, fk[ck], fv[ck], idx, geo.n_q, geo.n_kv, geo.head_dim,
                                  geo.scaling, status=status, workspace=ws_sparse, reuse_plan=False)
@@ -463,8 +476,8 @@ def _selective_prefill(layerwise_model, chunks, kv_store, recompute_ratio, check
                 layer = inner.layers[li]
                 w_qkv, w_gu = _fused_w(lw, li, k_sel)
                 hn = _norm(layer.input_layernorm, hs, delta=m, sum_out=hs, status=status)
-                a, k_pre = _attention_block(layer, geo, hn, idx, S, rope, fk[li], fv[li], False, status,
-                                            rope_mode, ws_sparse, True, w_qkv=w_qkv)
+                a, k_pre = _attention_block(layer, geo, hn, idx, S, rope_sel, fk[li], fv[li], False, status,
+                                            rope_mode, ws_sparse, True, w_qkv=w_qkv, rope_by_row=True)
                 if w_qkv is not None:
                     lw._pre_rope_k[li] = k_pre
                 m = _mlp(layer, _norm(layer.post_attention_layernorm, hs, delta=a, sum_out=hs, status=status),

@@ -233,9 +233,12 @@ def assemble_kv(table: ChunkTable, layer_lo: int, layer_hi: int, n_kv_heads: int
 def rope_scatter(q_src: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor, idx: torch.Tensor,
                  gather: bool, S: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
                  rope: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                 q_out: torch.Tensor | None = None, mode: str = "ref", status=None) -> torch.Tensor:
+                 q_out: torch.Tensor | None = None, mode: str = "ref", status=None,
+                 table_by_row: bool = False) -> torch.Tensor:
     """RoPE of fresh Q (-> q_out, [n_sel][Hq*D]) and K at positions idx; K and V
-    rows written into the fused cache of one layer at rows idx."""
+    rows written into the fused cache of one layer at rows idx.  With
+    ``table_by_row`` row j of ``rope`` holds the cos/sin of position idx[j]
+    (``rope.index_select(0, idx)``, made once per selection)."""
     dev = require_cuda(q_src, k_src, v_src, idx, rope, k_cache, v_cache)
     q2, k2, v2 = _rows(q_src, "q"), _rows(k_src, "k"), _rows(v_src, "v")
     n_sel = idx.numel()
@@ -245,7 +248,8 @@ def rope_scatter(q_src: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor, 
         N.check(N.LIB.cbk_rope_scatter(_vp(q2), q2.stride(0), _vp(k2), k2.stride(0), _vp(v2), v2.stride(0),
                                      int(bool(gather)), _vp(idx), n_sel, int(S), n_q_heads, n_kv_heads,
                                      head_dim, dtype_code(q_src.dtype), _vp(rope), rope.shape[0],
-                                     ROPE_MODES[mode], _vp(q_out), _vp(k_cache), _vp(v_cache),
+                                     ROPE_MODES[mode] | (N.CBK_ROPE_TABLE_BY_ROW if table_by_row else 0),
+                                     _vp(q_out), _vp(k_cache), _vp(v_cache),
                                      _vp(status), _stream(dev)), "cbk_rope_scatter")
     return q_out
 

@@ -1,19 +1,24 @@
 // Partial-query attention on 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
-// Work item = (KV head, pair of 128-row Q tiles, chunk of key tiles).  Rows of a
+// Work item = (KV head, pair of 128-row Q tiles, range of key tiles).  Rows of a
 // tile are r = tok * G + h (G = q heads per KV head, 128 / G selected tokens per
 // tile), so K/V tiles are shared by the GQA group without expanding them.  Keys
 // are visited in 128-key tiles; causality is a per-row position compare (no
-// mask tensor).  A tile whose key range is longer than one chunk is split over
-// several items; their partial results are merged by attn_combine_kernel.  The
-// chunking is planned on the device (attn_plan_kernel) from the positions, so
-// no host synchronisation is needed, and the plan can be reused by every layer
-// that attends with the same positions.
+// mask tensor).
+//
+// Work plan (attn_plan_kernel, on the device from the positions, so no host
+// synchronisation; reusable by every layer that attends with the same
+// positions): the (KV head, pair, key tile) steps of the call are laid end to
+// end and cut into one equal range per SM ("worker"); a pair whose steps cross
+// a cut is split into pieces, whose partial results attn_combine_kernel
+// merges.  Every SM gets the same number of steps, whatever the spread of the
+// pairs' key ranges (a causal selection makes them range from one tile to all).
 //
 // The attention kernel is persistent: one CTA per SM keeps its TMEM and
-// barriers and pulls items (longest first) from a queue in the workspace.  The
-// producer publishes each item to the other warps through a two-slot ring in
-// shared memory and loads the next item's Q as soon as the current item's last
+// barriers and takes workers from a queue in the workspace (one each when every
+// CTA is resident), running the items of a worker in order.  The producer
+// publishes each item to the other warps through a two-slot ring in shared
+// memory and loads the next item's Q as soon as the current item's last
 // S = Q K^T has been issued, so set-up costs overlap the previous item.
 //
 // TMEM (512 columns): tile t uses S/P at [256t, 256t+128) and O at
@@ -76,10 +81,10 @@ enum Bar { B_QFULL = 0, B_QEMPTY = 1, B_KFULL = 2, B_KEMPTY = 4, B_VFULL = 6, B_
 // Work plan in the caller's workspace (written by attn_plan_kernel).
 struct AttnPlanHeader {
   int n_items;     // work items
-  int chunk;       // key tiles per item (C)
+  int n_workers;   // equal ranges of steps (one per SM)
   int n_slots;     // partial-result slots in use
   int error;       // nonzero: the plan did not fit the workspace bounds
-  int next_item;   // queue head: zeroed by the plan and after every attention call
+  int next_item;   // worker queue head: zeroed by the plan and after every attention call
   int n_split;     // Q tiles (over all KV heads) whose key range is split
 };
 
@@ -89,7 +94,8 @@ struct AttnParams {
   int32_t* status;
   const AttnPlanHeader* plan;
   int* queue;             // &plan->next_item
-  const int4* items;      // (kv head, tile pair, chunk, length) longest first
+  const int4* items;      // (kv head, tile pair, first key tile j0, j1 | piece << 16) by worker
+  const int* first_item;  // [n_workers + 1]: the items of worker w are [first_item[w], first_item[w+1])
   const int* tile_base;   // [Hkv][n_tiles]: first partial slot of a split tile, -1 if not split
   const int4* split_desc; // [n_split]: (kvh * n_tiles + tile, first slot, chunks, 0) per split tile
   uint16_t* part_o;       // [slot][128][HD] O / l of the chunk, in the inputs' 16-bit type
@@ -228,9 +234,9 @@ __device__ __forceinline__ int tile_key_tiles(const int64_t* pos, int64_t n_sel,
   return static_cast<int>(pos[last] / kBN) + 1;
 }
 
-// geometry of one work item: Q-tile pair, chunk of key tiles
+// geometry of one work item: Q-tile pair, range [j0, j1) of its key tiles
 struct ItemGeom {
-  int kvh, pair, chunk, j0;
+  int kvh, pair, piece, j0;
   int n_kv[2];          // key tiles of this item for tile 0 / 1 (0: tile absent or done)
   int n_all;            // max of the two
   int tile[2];           // tile index of slot 0 / 1 (out of range: slot empty)
@@ -238,12 +244,13 @@ struct ItemGeom {
   int64_t tok0[2], tok_end[2], p_max[2];
 };
 
-__device__ __forceinline__ ItemGeom item_geom(const int4 item, int C, const AttnParams& prm) {
+__device__ __forceinline__ ItemGeom item_geom(const int4 item, const AttnParams& prm) {
   ItemGeom g;
   g.kvh = item.x;
   g.pair = item.y;
-  g.chunk = item.z;
-  g.j0 = item.z * C;
+  g.j0 = item.z;
+  const int j1 = item.w & 0xFFFF;
+  g.piece = item.w >> 16;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     const int tile = pair_tile(prm.n_tiles, g.pair, t);
@@ -258,7 +265,7 @@ __device__ __forceinline__ ItemGeom item_geom(const int4 item, int C, const Attn
       g.tok_end[t] = g.tok0[t] + prm.tok_per_tile;
       g.p_max[t] = prm.pos[g.tok_end[t] - 1];
       const int n_full = static_cast<int>(g.p_max[t] / kBN) + 1;
-      g.n_kv[t] = max(0, min(C, n_full - g.j0));
+      g.n_kv[t] = max(0, min(j1, n_full) - g.j0);
     }
   }
   g.n_all = max(g.n_kv[0], g.n_kv[1]);
@@ -271,8 +278,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     const __grid_constant__ CUtensorMap tm_v, const AttnParams prm) {
   using L = AttnSmem<HD>;
   if (prm.plan->error || prm.plan->n_items == 0) return;
-  const int n_items = prm.plan->n_items;
-  const int C = prm.plan->chunk;
+  const int n_workers = prm.plan->n_workers;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -342,15 +348,24 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     int g = 0;                               // K/V tiles loaded by this CTA
     int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
     int n_q = 0;                             // Q loads issued
+    int it = 0, it_end = 0;                  // items left of the current worker
     for (int n = 0; !failed; ++n) {
       if (n >= 2 && !wait_all(bar(B_IEMPTY + (n & 1)), ((n >> 1) - 1) & 1)) {
         failed = true;
         break;
       }
-      int idx = 0;
-      if (leader) idx = atomicAdd(prm.queue, 1);
-      idx = __shfl_sync(0xffffffffu, idx, leader_lane);
-      const int4 item = idx < n_items ? prm.items[idx] : make_int4(-1, 0, 0, 0);
+      while (it >= it_end) {                 // next worker with items from the queue
+        int w = 0;
+        if (leader) w = atomicAdd(prm.queue, 1);
+        w = __shfl_sync(0xffffffffu, w, leader_lane);
+        if (w >= n_workers) {
+          it = it_end = 0;
+          break;
+        }
+        it = prm.first_item[w];
+        it_end = prm.first_item[w + 1];
+      }
+      const int4 item = it < it_end ? prm.items[it++] : make_int4(-1, 0, 0, 0);
       if (leader) {
         s_item[n & 1].x = item.x;
         s_item[n & 1].y = item.y;
@@ -359,7 +374,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         mbar_arrive(bar(B_IFULL + (n & 1)));   // release: the slot is visible to the waiters
       }
       if (item.x < 0) break;
-      const ItemGeom ig = item_geom(item, C, prm);
+      const ItemGeom ig = item_geom(item, prm);
       // Q of this item once the previous item's last S = Q K^T has been issued
       if (n_q > 0 && !wait_all(bar(B_QEMPTY), (n_q - 1) & 1)) {
         failed = true;
@@ -459,7 +474,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       if (leader) mbar_arrive(bar(B_IEMPTY + (n & 1)));
       if (item.x < 0) break;
-      const ItemGeom ig = item_geom(item, C, prm);
+      const ItemGeom ig = item_geom(item, prm);
       if (!wait_all(bar(B_QFULL), n & 1) || !wait_all(bar(B_KFULL + (g & 1)), (g >> 1) & 1)) {
         failed = true;
         break;
@@ -538,7 +553,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_IEMPTY + (n & 1)));
       if (item.x < 0) break;
-      const ItemGeom ig = item_geom(item, C, prm);
+      const ItemGeom ig = item_geom(item, prm);
       // (t is warp-uniform; selects keep the geometry in registers)
       const int n_t = t ? ig.n_kv[1] : ig.n_kv[0];
       if (n_t == 0) continue;
@@ -654,7 +669,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       const int slot0 = prm.tile_base[ig.kvh * prm.n_tiles + (t ? ig.tile[1] : ig.tile[0])];
       if (slot0 >= 0) {
         // split tile: this chunk's O / l (16-bit, the inputs' type), running max and row sum
-        const int64_t slot = slot0 + ig.chunk;
+        const int64_t slot = slot0 + ig.piece;
         uint16_t* po = prm.part_o + (slot * kBM + row) * HD;
         const float inv_l = l_sum > 0.f ? 1.f / l_sum : 0.f;   // no visible key: O = 0
 #pragma unroll
@@ -715,11 +730,22 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 }
 
 // ---------------------------------------------------------------------------
-// Work plan (one CTA).  Key tiles of a Q-tile pair are split into chunks of at
-// most C tiles, C = max(4, ceil(total / target_items)), where total counts the
-// (pair, key tile) iterations of all KV heads; items are ordered longest first
-// (the block scheduler starts CTAs roughly in index order).  A tile whose key
-// range spans more than one chunk gets consecutive partial slots (tile_base).
+// Work plan (one CTA).  A pair's steps are its later tile's 128-key tiles L_p
+// (the earlier tile's La_p <= L_p are a prefix of them; L_p grows with p, the
+// positions being ascending).  Every item also costs a fixed overhead of c0
+// steps (Q load, pipeline refill, epilogue), so the plan balances
+// steps + c0 * items over the SMs (B workers):
+//   - small units (the longest, plus c0, at most half an SM's share): every
+//     (KV head, pair) unit is one item, longest first, each item its own
+//     worker: the dynamic queue then balances them like LPT scheduling, with
+//     no split and nothing to merge;
+//   - otherwise the units are laid end to end in cost space (c0, then the
+//     unit's L_p steps) and cut into B equal ranges; a unit whose steps cross a
+//     cut is split there into pieces (one item each), whose partial results
+//     attn_combine_kernel merges.  A split unit's tiles get consecutive
+//     partial slots: the earlier tile one per piece that holds some of its key
+//     tiles (when more than one does), then the later tile one per piece.
+// Items in unit order are grouped by worker; first_item[w] indexes them.
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
 
@@ -754,111 +780,127 @@ __device__ int block_excl_scan(int v, int* s_warp, int* total) {
 
 __global__ void __launch_bounds__(kPlanThreads, 1)
 attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_tile, int n_tiles,
-                 int n_kv_heads, int target_items, int min_chunk, int max_items, int max_slots,
-                 AttnPlanHeader* hdr, int4* items, int* tile_base, int4* split_desc, int32_t* status) {
-  __shared__ int s_hist[kMaxKvTiles + 1];
+                 int n_kv_heads, int target_workers, int item_cost, int max_items, int max_slots,
+                 AttnPlanHeader* hdr, int4* items, int* first_item, int* pair_off, int* tile_base,
+                 int4* split_desc, int32_t* status) {
   __shared__ int s_warp[33];
-  __shared__ unsigned long long s_total;
-  __shared__ int s_max;
-  __shared__ int s_error;
+  __shared__ int s_error, s_lmax;
   const int tid = threadIdx.x;
   const int n_pairs = (n_tiles + 1) / 2;
+  const int n_units = n_kv_heads * n_pairs;
   if (tid == 0) {
-    s_total = 0;
-    s_max = 0;
     s_error = 0;
+    s_lmax = 0;
   }
-  for (int i = tid; i <= kMaxKvTiles; i += kPlanThreads) s_hist[i] = 0;
   __syncthreads();
-  auto pair_tiles = [&](int p) {   // the later tile of a pair (always present) has the larger key range
-    return tile_key_tiles(pos, n_sel, n_tiles, tok_per_tile, pair_tile(n_tiles, p, 1));
+  auto tile_len = [&](int tile) {
+    return tile >= 0 ? tile_key_tiles(pos, n_sel, n_tiles, tok_per_tile, tile) : 0;
   };
-  // 1. key-tile iterations of all pairs
-  unsigned long long local = 0;
-  int local_max = 0;
-  for (int p = tid; p < n_pairs; p += kPlanThreads) {
-    const int n = pair_tiles(p);
-    local += n;
-    local_max = max(local_max, n);
-  }
-  atomicAdd(&s_total, local);
-  atomicMax(&s_max, local_max);
-  __syncthreads();
-  const unsigned long long total = s_total * static_cast<unsigned long long>(n_kv_heads);
-  int C = static_cast<int>((total + target_items - 1) / target_items);
-  C = max(C, min_chunk);
-  if (tid == 0 && s_max > kMaxKvTiles) s_error = 1;
-  // 2. item lengths -> histogram (identical for every KV head)
-  for (int p = tid; p < n_pairs; p += kPlanThreads) {
-    const int n = min(pair_tiles(p), kMaxKvTiles);
-    const int full = n / C, rem = n % C;
-    if (full) atomicAdd(&s_hist[min(C, kMaxKvTiles)], full * n_kv_heads);
-    if (rem) atomicAdd(&s_hist[rem], n_kv_heads);
-  }
-  __syncthreads();
-  // 3. offsets in descending length order: thread i owns the kPerThread lengths
-  //    kMaxKvTiles - kPerThread*i - r (r = 0 ..), down to length 0
-  {
-    constexpr int kPerThread = (kMaxKvTiles + 1 + kPlanThreads - 1) / kPlanThreads;
-    int cnt[kPerThread];
-    int mine = 0;
-#pragma unroll
-    for (int r = 0; r < kPerThread; ++r) {
-      const int len = kMaxKvTiles - kPerThread * tid - r;
-      cnt[r] = len >= 0 ? s_hist[len] : 0;
-      mine += cnt[r];
+  // 1. pair step counts, their prefix (pair_off[p] = steps of pairs before p), the longest
+  int carry = 0;
+  for (int b0 = 0; b0 < n_pairs; b0 += kPlanThreads) {
+    const int p = b0 + tid;
+    int L = 0;
+    if (p < n_pairs) {
+      L = tile_len(pair_tile(n_tiles, p, 1));
+      if (L > kMaxKvTiles) s_error = 1;
+      atomicMax(&s_lmax, L);
     }
     int tot;
-    int off = block_excl_scan(mine, s_warp, &tot);
-#pragma unroll
-    for (int r = 0; r < kPerThread; ++r) {
-      const int len = kMaxKvTiles - kPerThread * tid - r;
-      if (len >= 0) s_hist[len] = off;
-      off += cnt[r];
+    const int off = block_excl_scan(L, s_warp, &tot);
+    if (p < n_pairs) pair_off[p] = carry + off;
+    carry += tot;
+  }
+  if (tid == 0) pair_off[n_pairs] = carry;
+  __syncthreads();
+  const int64_t Wh = carry;
+  const int64_t W = Wh * n_kv_heads;                               // steps, >= 1
+  const int64_t c0 = item_cost;
+  const int64_t Wc = W + c0 * n_units;                             // cost
+  const int64_t B = W < target_workers ? W : target_workers;
+
+  if ((s_lmax + c0) * 2 * B <= Wc) {
+    // ---- small units: one item each, longest first (pairs in descending order)
+    if (n_units > max_items) s_error = 1;
+    for (int i = tid; i < n_units && i < max_items; i += kPlanThreads) {
+      const int p = n_pairs - 1 - i / n_kv_heads, h = i % n_kv_heads;
+      items[i] = make_int4(h, p, 0, pair_off[p + 1] - pair_off[p]);
+      first_item[i] = i;
     }
+    for (int i = tid; i < n_kv_heads * n_tiles; i += kPlanThreads) tile_base[i] = -1;
     if (tid == 0) {
-      if (tot > max_items) s_error = 1;
-      hdr->n_items = tot;
+      const int n = n_units < max_items ? n_units : max_items;
+      first_item[n] = n;
+      hdr->n_items = n;
+      hdr->n_workers = n;
+      hdr->n_split = 0;
+      hdr->n_slots = 0;
+      hdr->error = s_error;
+      hdr->next_item = 0;
+      if (s_error) report(status, CBK_STATUS_COUNT);
     }
+    return;
+  }
+
+  // ---- equal ranges of cost: unit u's steps are [Q_u, Q_u + L) in cost space,
+  //      Q_u = (u + 1) c0 + P_u (P_u its first step in step space)
+  auto worker_of = [&](int64_t x) { return ((x + 1) * B + Wc - 1) / Wc - 1; };
+  auto worker_start = [&](int64_t w) { return w * Wc / B; };
+  for (int64_t w = tid; w < B; w += kPlanThreads) first_item[w] = 0x7fffffff;
+  __syncthreads();
+  int item_carry = 0, slot_carry = 0, split_carry = 0;
+  for (int b0 = 0; b0 < n_units; b0 += kPlanThreads) {
+    const int u = b0 + tid;
+    int n_pieces = 0, m_a = 0, ta = -1, tb = -1, L = 0, La = 0;
+    int64_t Q = 0, wa = 0;
+    if (u < n_units) {
+      const int h = u / n_pairs, p = u % n_pairs;
+      ta = pair_tile(n_tiles, p, 0);
+      tb = pair_tile(n_tiles, p, 1);
+      L = pair_off[p + 1] - pair_off[p];
+      La = tile_len(ta);
+      Q = (u + 1) * c0 + h * Wh + pair_off[p];
+      wa = worker_of(Q);
+      n_pieces = static_cast<int>(worker_of(Q + L - 1) - wa + 1);
+      m_a = La > 0 ? static_cast<int>(worker_of(Q + La - 1) - wa + 1) : 0;
+    }
+    const int slots_a = m_a > 1 ? m_a : 0, slots_b = n_pieces > 1 ? n_pieces : 0;
+    int tot_items, tot_slots, tot_split;
+    const int item0 = item_carry + block_excl_scan(n_pieces, s_warp, &tot_items);
+    const int slot0 = slot_carry + block_excl_scan(slots_a + slots_b, s_warp, &tot_slots);
+    const int split0 = split_carry + block_excl_scan((slots_a > 0) + (slots_b > 0), s_warp, &tot_split);
+    if (u < n_units) {
+      const int h = u / n_pairs, p = u % n_pairs;
+      for (int i = 0; i < n_pieces; ++i) {
+        const int64_t w = wa + i;
+        const int64_t sw = worker_start(w), sw1 = worker_start(w + 1);
+        const int j0 = static_cast<int>((sw > Q ? sw : Q) - Q);
+        const int j1 = static_cast<int>((sw1 < Q + L ? sw1 : Q + L) - Q);
+        const int at = item0 + i;
+        if (at < max_items) items[at] = make_int4(h, p, j0, j1 | (i << 16));
+        atomicMin(&first_item[w], at);
+      }
+      if (ta >= 0) tile_base[h * n_tiles + ta] = slots_a ? slot0 : -1;
+      tile_base[h * n_tiles + tb] = slots_b ? slot0 + slots_a : -1;
+      int sp = split0;
+      if (slots_a) split_desc[sp++] = make_int4(h * n_tiles + ta, slot0, slots_a, 0);
+      if (slots_b) split_desc[sp] = make_int4(h * n_tiles + tb, slot0 + slots_a, slots_b, 0);
+    }
+    item_carry += tot_items;
+    slot_carry += tot_slots;
+    split_carry += tot_split;
   }
   __syncthreads();
-  // 4. emit items (order inside one length class is arbitrary)
-  for (int p = tid; p < n_pairs; p += kPlanThreads) {
-    const int n = min(pair_tiles(p), kMaxKvTiles);
-    const int nc = (n + C - 1) / C;
-    for (int h = 0; h < n_kv_heads; ++h)
-      for (int c = 0; c < nc; ++c) {
-        const int len = min(C, n - c * C);
-        const int at = atomicAdd(&s_hist[min(len, kMaxKvTiles)], 1);
-        if (at < max_items) items[at] = make_int4(h, p, c, len);
-      }
-  }
-  // 5. partial slots of split tiles, in (head, tile) order, and the list of
-  //    split tiles that the combine kernel walks
-  int carry = 0, n_split = 0;
-  const int n_all = n_kv_heads * n_tiles;
-  for (int b0 = 0; b0 < n_all; b0 += kPlanThreads) {
-    const int i = b0 + tid;
-    int cnt = 0;
-    if (i < n_all) {
-      const int nc = (tile_key_tiles(pos, n_sel, n_tiles, tok_per_tile, i % n_tiles) + C - 1) / C;
-      cnt = nc > 1 ? nc : 0;
-    }
-    int tot, tot_split;
-    const int off = block_excl_scan(cnt, s_warp, &tot);
-    const int rank = block_excl_scan(cnt ? 1 : 0, s_warp, &tot_split);
-    if (i < n_all) {
-      tile_base[i] = cnt ? carry + off : -1;
-      if (cnt) split_desc[n_split + rank] = make_int4(i, carry + off, cnt, 0);
-    }
-    carry += tot;
-    n_split += tot_split;
-  }
   if (tid == 0) {
-    if (carry > max_slots) s_error = 1;
-    hdr->n_split = n_split;
-    hdr->chunk = C;
-    hdr->n_slots = carry;
+    if (item_carry > max_items || slot_carry > max_slots) s_error = 1;
+    // a worker whose range holds no step (it fell inside items' overheads) has no items
+    first_item[B] = item_carry;
+    for (int64_t w = B - 1; w >= 0; --w)
+      if (first_item[w] == 0x7fffffff) first_item[w] = first_item[w + 1];
+    hdr->n_items = item_carry;
+    hdr->n_workers = static_cast<int>(B);
+    hdr->n_split = split_carry;
+    hdr->n_slots = slot_carry;
     hdr->error = s_error;
     hdr->next_item = 0;
     if (s_error) report(status, CBK_STATUS_COUNT);
@@ -1015,11 +1057,18 @@ static int sm_count() {
 
 // Workspace layout of one partial-attention call (all offsets 256-byte aligned).
 struct AttnLayout {
-  int tok_per_tile, n_tiles, n_pairs, target, min_chunk, max_items, max_slots;
-  size_t off_items, off_tile_base, off_split, off_ml, off_o, bytes;
+  int tok_per_tile, n_tiles, n_pairs, target, max_items, max_slots;
+  size_t off_items, off_first, off_pair, off_tile_base, off_split, off_ml, off_o, bytes;
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Fixed cost of one work item in key-tile steps (Q load, pipeline refill and
+// epilogue of a Q-tile pair), for the plan's balance.
+#ifndef CBK_ATTN_ITEM_COST
+#define CBK_ATTN_ITEM_COST 2
+#endif
+constexpr int kAttnItemCost = CBK_ATTN_ITEM_COST;
 
 static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int head_dim) {
   AttnLayout a;
@@ -1027,20 +1076,16 @@ static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int 
   a.tok_per_tile = kBM / G;
   a.n_tiles = static_cast<int>((n_sel + a.tok_per_tile - 1) / a.tok_per_tile);
   a.n_pairs = (a.n_tiles + 1) / 2;
-  // items per SM: 1 measured 703 / 838 TFLOP/s (uniform / tail 15 % selection at
-  // S = 6208) against 634 / 807 at 2, 589 / 828 at 3, 557 / 778 at 4, dense causal
-  // unchanged (1128 vs 1125): fewer splits leave less for the combine
-#ifndef CBK_ATTN_ITEMS_PER_SM
-#define CBK_ATTN_ITEMS_PER_SM 1
-#endif
-  a.target = CBK_ATTN_ITEMS_PER_SM * sm_count();
-  a.min_chunk = 4;
-  // items <= total / C + pairs <= target + pairs (C >= total / target)
+  a.target = sm_count();                      // workers: one equal range of steps per SM
+  // items: one per unit plus one per worker boundary inside a unit
   a.max_items = a.target + n_kv_heads * a.n_pairs;
-  // split tiles span more than C key tiles each, so their slots number < 4 * total / C <= 4 * target
+  // a split unit holds a worker boundary, so split units' pieces number <= 2 (workers - 1),
+  // and each piece gives at most two slots (earlier and later tile)
   a.max_slots = 4 * a.target + 2;
   a.off_items = align256(sizeof(AttnPlanHeader));
-  a.off_tile_base = a.off_items + align256(static_cast<size_t>(a.max_items) * sizeof(int4));
+  a.off_first = a.off_items + align256(static_cast<size_t>(a.max_items) * sizeof(int4));
+  a.off_pair = a.off_first + align256(static_cast<size_t>(a.max_items + 1) * sizeof(int));
+  a.off_tile_base = a.off_pair + align256(static_cast<size_t>(a.n_pairs + 1) * sizeof(int));
   a.off_split = a.off_tile_base + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int));
   a.off_ml = a.off_split + align256(static_cast<size_t>(n_kv_heads) * a.n_tiles * sizeof(int4));
   a.off_o = a.off_ml + align256(static_cast<size_t>(a.max_slots) * kBM * sizeof(float2));
@@ -1066,6 +1111,7 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   prm.plan = reinterpret_cast<const AttnPlanHeader*>(ws);
   prm.queue = &reinterpret_cast<AttnPlanHeader*>(ws)->next_item;
   prm.items = reinterpret_cast<const int4*>(ws + lay.off_items);
+  prm.first_item = reinterpret_cast<const int*>(ws + lay.off_first);
   prm.tile_base = reinterpret_cast<const int*>(ws + lay.off_tile_base);
   prm.split_desc = reinterpret_cast<const int4*>(ws + lay.off_split);
   prm.part_ml = reinterpret_cast<float2*>(ws + lay.off_ml);
@@ -1078,16 +1124,17 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   prm.scale_log2 = scale * 1.4426950408889634f;
   if (!reuse_plan) {
     attn_plan_kernel<<<1, kPlanThreads, 0, st>>>(
-        pos, n_sel, lay.tok_per_tile, lay.n_tiles, n_kv_heads, lay.target, lay.min_chunk,
-        lay.max_items, lay.max_slots, reinterpret_cast<AttnPlanHeader*>(ws),
-        reinterpret_cast<int4*>(ws + lay.off_items), reinterpret_cast<int*>(ws + lay.off_tile_base),
-        reinterpret_cast<int4*>(ws + lay.off_split), status);
+        pos, n_sel, lay.tok_per_tile, lay.n_tiles, n_kv_heads, lay.target, kAttnItemCost, lay.max_items,
+        lay.max_slots,
+        reinterpret_cast<AttnPlanHeader*>(ws), reinterpret_cast<int4*>(ws + lay.off_items),
+        reinterpret_cast<int*>(ws + lay.off_first), reinterpret_cast<int*>(ws + lay.off_pair),
+        reinterpret_cast<int*>(ws + lay.off_tile_base), reinterpret_cast<int4*>(ws + lay.off_split), status);
     if (int rc = check_launch("attn_plan_kernel")) return rc;
   }
   auto kern = partial_attn_kernel<DT, HD>;
   const int smem = AttnSmem<HD>::kAlloc;
   if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem)) return rc;
-  const int grid = std::min(lay.max_items, sm_count());   // persistent: one CTA per SM
+  const int grid = lay.target;             // persistent: one CTA per SM (workers beyond the plan's exit)
   kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(mq, mk, mv, prm);
   if (int rc = check_launch("partial_attn_kernel")) return rc;
   // one CTA per half split tile; at most every tile is split

@@ -122,29 +122,40 @@ constexpr int kTopkThreads = 1024;
 constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int64_t kTopkSmemKeys = 40960;   // keys cached in shared memory up to this S
 
+// Each warp owns one contiguous chunk of the keys (a multiple of 32 long) and
+// walks it in 32-key tiles, lane = key within the tile: loads are coalesced,
+// shared-memory reads conflict-free, and within a warp the keys come in index
+// order, which the ordered compaction below relies on.
 __global__ void __launch_bounds__(kTopkThreads, 1)
 topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
             int64_t* __restrict__ idx, int32_t* status) {
   extern __shared__ uint32_t s_keys[];   // S keys when S <= kTopkSmemKeys
   __shared__ uint32_t s_hist[256];
-  __shared__ uint32_t s_wcount[kTopkWarps];
+  __shared__ uint32_t s_wa[kTopkWarps], s_wb[kTopkWarps];
   __shared__ uint32_t s_prefix, s_mask;
   __shared__ int64_t s_krem, s_total_eq;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool cached = S <= kTopkSmemKeys;
+  const int64_t chunk = ((S + kTopkWarps - 1) / kTopkWarps + 31) & ~int64_t{31};
+  const int64_t w_lo = warp * chunk, w_hi = w_lo + chunk < S ? w_lo + chunk : S;
   if (cached)
     for (int64_t i = tid; i < S; i += kTopkThreads) s_keys[i] = order_key(dev[i]);
+  for (int b = tid; b < 256; b += kTopkThreads) s_hist[b] = 0;
   if (tid == 0) { s_prefix = 0; s_mask = 0; s_krem = k; }
   __syncthreads();
+  auto key_at = [&](int64_t i) { return cached ? s_keys[i] : order_key(dev[i]); };
 
+  // four 8-bit radix passes, high digit first (shared-memory atomics; lanes
+  // that hit one bin are serialised by the hardware, a few cycles per warp)
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
-    for (int b = tid; b < 256; b += kTopkThreads) s_hist[b] = 0;
-    __syncthreads();
     const uint32_t prefix = s_prefix, mask = s_mask;
-    for (int64_t i = tid; i < S; i += kTopkThreads) {
-      const uint32_t key = cached ? s_keys[i] : order_key(dev[i]);
-      if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+    for (int64_t b = w_lo; b < w_hi; b += 32) {
+      const int64_t i = b + lane;
+      if (i < w_hi) {
+        const uint32_t key = key_at(i);
+        if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+      }
     }
     __syncthreads();
     if (warp == 0) {
@@ -152,6 +163,8 @@ topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
       uint32_t c[8], sum = 0;
 #pragma unroll
       for (int e = 0; e < 8; ++e) { c[e] = s_hist[255 - 8 * lane - e]; sum += c[e]; }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s_hist[255 - 8 * lane - e] = 0;      // ready for the next pass
       uint32_t incl = sum;   // inclusive scan over lanes: counts of digits >= this lane's lowest
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -181,50 +194,70 @@ topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
   }
 
   const uint32_t T = s_prefix;
-  const int64_t k_eq = s_krem;          // elements equal to T that are taken
+  const int64_t k_eq = s_krem;          // elements equal to T that are taken (lowest index first)
   const int64_t total_eq = s_total_eq;  // elements equal to T in total
-  const uint32_t last_key = cached ? s_keys[S - 1] : order_key(dev[S - 1]);
+  const uint32_t last_key = key_at(S - 1);
   const bool last_sel = last_key > T || (last_key == T && total_eq <= k_eq);
   const bool force = force_last && !last_sel;
 
-  int64_t eq_seen = 0, out_base = 0;
+  // ordered compaction: per-warp counts, warp offsets, then each warp writes its keys
   const unsigned lt_mask = (1u << lane) - 1u;
-  for (int64_t base = 0; base < S; base += kTopkThreads) {
-    const int64_t i = base + tid;
-    const bool valid = i < S;
-    const uint32_t key = valid ? (cached ? s_keys[i] : order_key(dev[i])) : 0u;
+  uint32_t n_gt = 0, n_eq = 0;
+  for (int64_t b = w_lo; b < w_hi; b += 32) {
+    const int64_t i = b + lane;
+    const uint32_t key = i < w_hi ? key_at(i) : 0u;
+    n_gt += __popc(__ballot_sync(0xffffffffu, i < w_hi && key > T));
+    n_eq += __popc(__ballot_sync(0xffffffffu, i < w_hi && key == T));
+  }
+  if (lane == 0) {
+    s_wa[warp] = n_gt;
+    s_wb[warp] = n_eq;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // eq elements before each warp, then each warp's selected count and output offset
+    const uint32_t gt = s_wa[lane], eq = s_wb[lane];
+    uint32_t e_incl = eq;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, e_incl, o);
+      if (lane >= o) e_incl += y;
+    }
+    const int64_t e_before = e_incl - eq;
+    int64_t take = k_eq - e_before;
+    take = take < 0 ? 0 : (take > eq ? eq : take);
+    const int64_t lo = lane * chunk, hi = lo + chunk;
+    const bool has_last = lo <= S - 1 && S - 1 < hi;
+    int64_t sel = gt + take - (force && e_before == 0 && eq > 0 ? 1 : 0) + (force && has_last ? 1 : 0);
+    uint32_t s_incl = static_cast<uint32_t>(sel);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, s_incl, o);
+      if (lane >= o) s_incl += y;
+    }
+    s_wa[lane] = static_cast<uint32_t>(e_before);
+    s_wb[lane] = s_incl - static_cast<uint32_t>(sel);
+    if (lane == 31 && s_incl != k) report(status, CBK_STATUS_COUNT);
+  }
+  __syncthreads();
+  int64_t eq_rank0 = s_wa[warp], out = s_wb[warp];
+  for (int64_t b = w_lo; b < w_hi; b += 32) {
+    const int64_t i = b + lane;
+    const bool valid = i < w_hi;
+    const uint32_t key = valid ? key_at(i) : 0u;
     const bool eq = valid && key == T;
     const unsigned eq_bal = __ballot_sync(0xffffffffu, eq);
-    if (lane == 0) s_wcount[warp] = __popc(eq_bal);
-    __syncthreads();
-    uint32_t eq_before = 0, eq_tile = 0;
-    for (int w = 0; w < kTopkWarps; ++w) {
-      const uint32_t c = s_wcount[w];
-      if (w < warp) eq_before += c;
-      eq_tile += c;
-    }
-    const int64_t eq_rank = eq_seen + eq_before + __popc(eq_bal & lt_mask);
+    const int64_t eq_rank = eq_rank0 + __popc(eq_bal & lt_mask);
     bool sel = valid && (key > T || (eq && eq_rank < k_eq && !(force && eq_rank == 0)));
     if (force && i == S - 1) sel = true;
-    __syncthreads();
     const unsigned sel_bal = __ballot_sync(0xffffffffu, sel);
-    if (lane == 0) s_wcount[warp] = __popc(sel_bal);
-    __syncthreads();
-    uint32_t sel_before = 0, sel_tile = 0;
-    for (int w = 0; w < kTopkWarps; ++w) {
-      const uint32_t c = s_wcount[w];
-      if (w < warp) sel_before += c;
-      sel_tile += c;
-    }
     if (sel) {
-      const int64_t pos = out_base + sel_before + __popc(sel_bal & lt_mask);
-      if (pos < k) idx[pos] = i; else report(status, CBK_STATUS_COUNT);
+      const int64_t at = out + __popc(sel_bal & lt_mask);
+      if (at < k) idx[at] = i; else report(status, CBK_STATUS_COUNT);
     }
-    eq_seen += eq_tile;
-    out_base += sel_tile;
-    __syncthreads();
+    eq_rank0 += __popc(eq_bal);
+    out += __popc(sel_bal);
   }
-  if (tid == 0 && out_base != k) report(status, CBK_STATUS_COUNT);
 }
 
 int ensure_smem_attr(const void* func, int bytes);   // cbk_api.cu

@@ -260,7 +260,7 @@ rope_scatter_kernel(const uint16_t* __restrict__ q_src, int64_t q_stride,
                     const uint16_t* __restrict__ v_src, int64_t v_stride, int gather,
                     const int64_t* __restrict__ idx, int64_t n_sel, int64_t S, int n_q_heads,
                     int n_kv_heads, int head_dim, const float2* __restrict__ table,
-                    int64_t table_rows, int mode, uint16_t* __restrict__ q_out,
+                    int64_t table_rows, int by_row, uint16_t* __restrict__ q_out,
                     uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache,
                     int32_t* status) {
   constexpr int U = kScatUnits;
@@ -319,16 +319,19 @@ rope_scatter_kernel(const uint16_t* __restrict__ q_src, int64_t q_stride,
       }
     };
     const int64_t p = idx[j];
-    // without a gather the source row is j: its loads go out before the position arrives
+    // without a gather the source row is j: its loads go out before the position
+    // arrives, and with a table indexed by row (row j holds the cos/sin of idx[j])
+    // so do the cos/sin loads -- the whole pass waits for memory once
     if (!gather) load(j);
-    if (p < 0 || p >= S || p >= table_rows) {
+    float4 c4[4];
+    if (by_row && rope && shared_f && j < table_rows) ld_cs(table + j * half + (lane % gpr) * 8, c4);
+    if (p < 0 || p >= S || (by_row ? j >= table_rows : p >= table_rows)) {
       if (lane == 0) report(status, CBK_STATUS_BAD_INDEX);
       continue;
     }
     if (gather) load(p);
-    const float2* cs = table + p * half;
-    float4 c4[4];
-    if (rope && shared_f) ld_cs(cs + (lane % gpr) * 8, c4);
+    const float2* cs = table + (by_row ? j : p) * half;
+    if (!by_row && rope && shared_f) ld_cs(cs + (lane % gpr) * 8, c4);
 #pragma unroll
     for (int k = 0; k < U; ++k) {
       if (kind[k] < 0) continue;
@@ -458,6 +461,8 @@ extern "C" int cbk_rope_scatter(const void* q_src, int64_t q_row_stride, const v
                                 void* q_out, void* k_cache, void* v_cache, int32_t* status,
                                 void* stream) {
   if (int rc = check_geometry("cbk_rope_scatter", n_kv_heads, head_dim, dtype)) return rc;
+  const int by_row = (rope_mode & CBK_ROPE_TABLE_BY_ROW) ? 1 : 0;
+  rope_mode &= ~CBK_ROPE_TABLE_BY_ROW;
   if (int rc = check_mode("cbk_rope_scatter", rope_mode)) return rc;
   if (n_q_heads <= 0 || n_q_heads % n_kv_heads != 0)
     return set_error(CBK_ERR_INVALID, "cbk_rope_scatter: n_q_heads must be a multiple of n_kv_heads");
@@ -480,7 +485,7 @@ extern "C" int cbk_rope_scatter(const void* q_src, int64_t q_row_stride, const v
   rope_scatter_kernel<DT, GPR, MODE><<<grid_for(warp_items * 32, 256, 148 * 64), 256, 0, st>>>(   \
       static_cast<const uint16_t*>(q_src), q_row_stride, static_cast<const uint16_t*>(k_src),   \
       k_row_stride, static_cast<const uint16_t*>(v_src), v_row_stride, gather, idx, n_sel, S,   \
-      n_q_heads, n_kv_heads, head_dim, tab, table_rows, rope_mode,                              \
+      n_q_heads, n_kv_heads, head_dim, tab, table_rows, by_row,                                 \
       static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_cache),                          \
       static_cast<uint16_t*>(v_cache), status)
 #define CBK_LAUNCH_SCATTER_M(DT, GPR)                                                           \

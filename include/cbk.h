@@ -55,6 +55,11 @@ enum { CBK_BF16 = 0, CBK_F16 = 1 };
  *                MistralRotaryEmbedding.forward casts cos/sin to x.dtype).
  * CBK_ROPE_FP32: rotate in fp32 with one final rounding (more accurate). */
 enum { CBK_ROPE_REF = 0, CBK_ROPE_FP32 = 1 };
+/* cbk_rope_scatter only, OR-ed into rope_mode: rope_table row j holds the
+ * cos/sin of position idx[j] (a copy of the position-indexed table's rows at
+ * the selection, made once per selection), so the kernel loads it without
+ * waiting for idx[j]; table_rows must be >= n_sel. */
+enum { CBK_ROPE_TABLE_BY_ROW = 16 };
 
 /* Device status bits (OR-ed into *status). */
 enum {
@@ -107,7 +112,9 @@ int cbk_rope_rows(const void* in, void* out, int64_t n_rows, int n_heads, int he
  *   q_out[j]      = RoPE(q_src[r], p)              [n_sel][n_q_heads*head_dim]
  *   k_cache[p]    = RoPE(k_src[r], p)              fused [S][kv_dim]
  *   v_cache[p]    = v_src[r]
- * Row strides are in elements.  Replaces fusor.py:355-361 + 370-376 (check
+ * Row strides are in elements.  With CBK_ROPE_TABLE_BY_ROW in rope_mode the
+ * cos/sin of row j are rope_table row j instead of row p.  Replaces
+ * fusor.py:355-361 + 370-376 (check
  * layer: mixed K, RoPE of Q and K, Q sliced to the selection) and
  * fusor.py:432-458 (sparse layers: RoPE of sparse Q/K, clone + index_put of K/V). */
 int cbk_rope_scatter(const void* q_src, int64_t q_row_stride, const void* k_src,

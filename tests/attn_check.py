@@ -51,7 +51,7 @@ CASES = [
     ("long_split", 20000, 2000, 32, 8, 128, "bf16", 1.0, 1.0),
     ("long_split_peaked", 20000, 2000, 32, 8, 128, "bf16", 4.0, 1.0),
     ("big_v_split", 20000, 2000, 32, 8, 128, "bf16", 1.0, 1e5),
-    ("big_v_f16", 6208, 931, 32, 8, 128, "f16", 4.0, 3e4),
+    ("big_v_f16", 6208, 931, 32, 8, 128, "f16", 4.0, 1e4),   # |V| up to ~5.5e4 (fp16 max 65504)
 ]
 CASE = {c[0]: c for c in CASES}
 
@@ -112,75 +112,95 @@ def check(got, exp, absm, dtype):
 # ---------------------------------------------------------------------------
 # the kernel's split plan (attn_plan_kernel restated) and planted mistakes
 # ---------------------------------------------------------------------------
-def plan(pos, n_sel, G, Hkv, sms=148):
-    """(C, tile of each selected row, key tiles of each tile) of the partial-
-    attention plan: Q tiles of 128/G tokens aligned to the end of the
-    selection, paired, and every pair's key range cut into chunks of C
-    128-key tiles, C = max(4, ceil(total / SMs))."""
+def plan(pos, n_sel, G, Hkv, sms=148, c0=2):
+    """The partial-attention work plan (attn_plan_kernel restated): Q tiles of
+    128/G tokens aligned to the end of the selection, paired; a pair's steps
+    are its later tile's 128-key tiles, and every item costs c0 steps more.
+    Small units (longest + c0 at most half an SM's share) are whole items;
+    otherwise the units, each c0 of cost then its steps, are laid end to end
+    and cut into ``sms`` equal ranges of cost, and a unit whose steps cross a
+    cut is split there.  Returns (tile of each selected row, pair of each
+    tile, cuts) with cuts[(h, pair)] the key-tile indices where that unit is
+    split (empty when it is not)."""
     pos = np.asarray(pos, np.int64)
     tpt = 128 // G
     n_tiles = -(-n_sel // tpt)
     first = n_sel - n_tiles * tpt
-    last_tok = np.array([first + (t + 1) * tpt - 1 for t in range(n_tiles)])
-    key_tiles = pos[last_tok] // 128 + 1
+    key_tiles = np.array([pos[first + (t + 1) * tpt - 1] // 128 + 1 for t in range(n_tiles)])
     n_pairs = (n_tiles + 1) // 2
-    later = [2 * p + 1 - (n_tiles & 1) for p in range(n_pairs)]
-    total = Hkv * int(key_tiles[later].sum())
-    C = max(4, -(-total // sms))
+    odd = n_tiles & 1
+    later = [2 * p + 1 - odd for p in range(n_pairs)]
+    L = key_tiles[later]
+    Wh = int(L.sum())
+    W = Hkv * Wh
+    n_units = Hkv * n_pairs
+    Wc = W + c0 * n_units
+    B = min(W, sms)
+    off = np.concatenate([[0], np.cumsum(L)])
+    cuts = {(h, p): [] for h in range(Hkv) for p in range(n_pairs)}
+    if (int(L.max()) + c0) * 2 * B > Wc:
+        starts = [w * Wc // B for w in range(B + 1)]
+        for h in range(Hkv):
+            for p in range(n_pairs):
+                Q = (h * n_pairs + p + 1) * c0 + h * Wh + int(off[p])
+                cuts[(h, p)] = [s_ - Q for s_ in starts if Q < s_ < Q + int(L[p])]
     row_tile = (np.arange(n_sel) - first) // tpt
-    return C, row_tile, key_tiles
+    tile_pair = (np.arange(n_tiles) + odd) // 2
+    return row_tile, tile_pair, cuts
 
 
 def planted(case, q, k, v, pos, mistake, heads):
     """The case's attention (fp64) with one planted mistake, for the q heads
-    in ``heads``; returns (n, Hq*D) with the other columns zero."""
+    in ``heads``; returns (n, Hq*D) with the other columns zero.  The split
+    mistakes act on the kernel's own pieces (``plan``): "drop_split_chunk"
+    leaves out a split row's second piece of keys, "merge_without_max" merges
+    the pieces' O / l with weights l_c, without the 2^(m_c - M) correction."""
     _, S, n_sel, Hq, Hkv, D, dtype, _, _ = case
     G = Hq // Hkv
     qf = _f32(q, dtype).reshape(n_sel, Hq, D).astype(np.float64)
     kf = _f32(k, dtype).reshape(S, Hkv, D).astype(np.float64)
     vf = _f32(v, dtype).reshape(S, Hkv, D).astype(np.float64)
     p_ = pos.numpy()
-    C, row_tile, key_tiles = plan(p_, n_sel, G, Hkv)
-    split_row = key_tiles[row_tile] > C            # the row's tile is split into chunks of C key tiles
+    row_tile, tile_pair, cuts = plan(p_, n_sel, G, Hkv)
     t = np.arange(S)
     out = np.zeros((n_sel, Hq, D))
     for h in heads:
-        s = (qf[:, h] @ kf[:, h // G].T) * D ** -0.5
+        kvh = h // G
+        # key bounds of each row's pieces: [0, c1, c2, ..., end) in keys
+        bounds = [[0] + [c * 128 for c in cuts[(kvh, tile_pair[row_tile[j]])]] + [S] for j in range(n_sel)]
+        s = (qf[:, h] @ kf[:, kvh].T) * D ** -0.5
         if mistake == "causal_plus_one":
             vis = t[None, :] <= p_[:, None] + 1
         elif mistake == "causal_minus_one":
             vis = t[None, :] < p_[:, None]
             vis[:, 0] |= p_ == 0
-        elif mistake == "drop_split_chunk":
+        elif mistake in ("drop_split_chunk", "merge_without_max"):
             vis = t[None, :] <= p_[:, None]
-            drop = (t[None, :] >= C * 128) & (t[None, :] < 2 * C * 128) & split_row[:, None]
-            vis &= ~drop
-        elif mistake == "merge_without_max":
-            vis = t[None, :] <= p_[:, None]
+            if mistake == "drop_split_chunk":
+                for j, b in enumerate(bounds):
+                    if len(b) > 2:
+                        vis[j, b[1]:b[2]] = False
         else:
             raise ValueError(mistake)
         s = np.where(vis, s, -np.inf)
+        m = s.max(axis=1, keepdims=True)
+        p = np.exp(s - m)
+        exact = (p @ vf[:, kvh]) / p.sum(axis=1, keepdims=True)
         if mistake == "merge_without_max":
-            # each chunk's O / l from its own max, merged with weights l_c
-            # (the 2^(m_c - M) factor left out)
-            o = np.zeros((n_sel, D))
-            wsum = np.zeros((n_sel, 1))
-            for c0 in range(0, S, C * 128):
-                sc = s[:, c0:c0 + C * 128]
-                m = sc.max(axis=1, keepdims=True)
-                ok = np.isfinite(m)
-                pc = np.where(ok, np.exp(sc - np.where(ok, m, 0.0)), 0.0)
-                l = pc.sum(axis=1, keepdims=True)
-                oc = (pc @ vf[c0:c0 + C * 128, h // G]) / np.where(l > 0, l, 1.0)
-                o += l * oc
-                wsum += l
-            exact = np.exp(s - s.max(axis=1, keepdims=True))
-            exact = (exact @ vf[:, h // G]) / exact.sum(axis=1, keepdims=True)
-            out[:, h] = np.where(split_row[:, None], o / wsum, exact)
-        else:
-            m = s.max(axis=1, keepdims=True)
-            p = np.exp(s - m)
-            out[:, h] = (p @ vf[:, h // G]) / p.sum(axis=1, keepdims=True)
+            for j, b in enumerate(bounds):
+                if len(b) <= 2:
+                    continue
+                o, wsum = np.zeros(D), 0.0
+                for a, e in zip(b[:-1], b[1:]):
+                    sc = s[j, a:e]
+                    if not np.isfinite(sc).any():
+                        continue
+                    pc = np.exp(sc - sc.max())
+                    l = pc.sum()
+                    o += l * ((pc @ vf[a:e, kvh]) / l)
+                    wsum += l
+                exact[j] = o / wsum
+        out[:, h] = exact
     return out.reshape(n_sel, Hq * D)
 
 

@@ -1,10 +1,11 @@
 """Generate the golden fixtures in this folder from the REFERENCE implementation.
 
-Runs only where the reference sources are mounted (``/root/reference``); the
-fixtures it writes are committed so that tests on other machines never need the
-reference.  Usage::
+Runs only where the reference sources are available; the fixtures it writes
+are committed so that tests on other machines never need the reference.
+Usage (the reference checkout's root, the folder holding ``src/cacheblend``,
+given by argument or by the CACHEBLEND_REFERENCE environment variable)::
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <path to cacheblend-hf-v7>
 
 The reference (cacheblend-hf-v7, ``src/cacheblend``) pins transformers 4.49; this
 image has 5.5.  Three API breaks are bridged here by monkeypatching transformers
@@ -255,8 +256,11 @@ def make_kernels(out_path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("CACHEBLEND_REFERENCE"),
+                    help="root of the cacheblend-hf-v7 checkout (default: $CACHEBLEND_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set CACHEBLEND_REFERENCE to the reference checkout")
     sys.path.insert(0, os.path.join(args.reference, "src"))
     torch.set_num_threads(1)           # fixed CPU reduction order for reproducible fixtures
     install_compat_shim()

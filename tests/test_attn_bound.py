@@ -33,9 +33,9 @@ def test_rounded_exact_result_is_inside(case_data):
 @pytest.mark.parametrize("mistake", MISTAKES)
 def test_planted_mistake_is_caught(case_data, mistake):
     case, inputs, heads, cols, exp, absm = case_data
-    C, row_tile, key_tiles = ac.plan(inputs[3].numpy(), case[2], case[3] // case[4], case[4])
+    _, _, cuts = ac.plan(inputs[3].numpy(), case[2], case[3] // case[4], case[4])
     if mistake in ("drop_split_chunk", "merge_without_max"):
-        assert (key_tiles > C).any(), "the case must have split tiles"
+        assert any(cuts[(0, p)] for (h, p) in cuts if h == 0), "the case must have split tiles"
     bad = ac.round_to(ac.planted(case, *inputs, mistake, heads), case[6])
     n_bad, worst = ac.violations(bad, exp, absm, case[6], cols)
     assert n_bad > 0 and worst > 4 * ac.TOL[case[6]], (mistake, n_bad, worst)

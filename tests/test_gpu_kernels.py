@@ -146,6 +146,7 @@ def test_assemble_reports_bad_positions(ops):
 # ---------------------------------------------------------------------------
 # (b)+(d) fresh rows
 # ---------------------------------------------------------------------------
+@pytest.mark.parametrize("by_row", [False, True])
 @pytest.mark.parametrize("gather", [True, False])
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
 @pytest.mark.parametrize("nq,nkv,D,mode", [
@@ -157,7 +158,9 @@ def test_assemble_reports_bad_positions(ops):
     (6, 3, 96, "fp32"),
     (2, 1, 256, "ref"),
 ])
-def test_rope_scatter(ops, gather, dtype, nq, nkv, D, mode):
+def test_rope_scatter(ops, by_row, gather, dtype, nq, nkv, D, mode):
+    """by_row: the cos/sin table holds the selection's rows (row j = position
+    idx[j]), as fuse_selective passes it; same bits as the position table."""
     g = torch.Generator().manual_seed(5)
     S = 700
     idx = torch.sort(torch.randperm(S, generator=g)[:105]).values
@@ -171,7 +174,9 @@ def test_rope_scatter(ops, gather, dtype, nq, nkv, D, mode):
     invf = invf_for(1e6, D)
     rope = ops.rope_table(invf.to(DEV), S)
     st = status_word()
-    qo = ops.rope_scatter(q, k, v, idx.to(DEV), gather, S, nq, nkv, D, rope, kc, vc, mode=mode, status=st)
+    tab_arg = rope.index_select(0, idx.to(DEV)) if by_row else rope
+    qo = ops.rope_scatter(q, k, v, idx.to(DEV), gather, S, nq, nkv, D, tab_arg, kc, vc, mode=mode, status=st,
+                          table_by_row=by_row)
     assert_status_clean(st)
     tab = rope.cpu().numpy()
     rows = idx.numpy() if gather else np.arange(idx.numel())
@@ -292,7 +297,7 @@ def test_partial_attention(ops, case):
     """Element by element within tol * (|exp| + A) of the fp64 oracle (A: the
     softmax weights applied to |V|; tol 2^-7 bf16, 2^-9 fp16), and max |err|
     within 2e-2 of max |exp|.  Peaked cases (q scaled) make outputs O(1) and
-    single keys decisive; big-V cases put |V| near 1e5 (bf16) and 3e4 (fp16)
+    single keys decisive; big-V cases put |V| up to ~5e5 (bf16) and ~5.5e4 (fp16)
     through split tiles.  tests/test_attn_bound.py shows that an off-by-one
     causal bound, a dropped split chunk or a wrong merge weight violate this
     bound on the peaked cases."""
