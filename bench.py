@@ -608,7 +608,8 @@ def run_kv_microbench(args):
     from cacheblend import ops
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    L, Hkv, S, D, CL, Hq = args.kv_layers, 8, 32768, 128, 2048, 32
+    L, Hkv, S, D, CL = args.kv_layers, args.kv_heads, 32768, 128, 2048
+    Hq = 4 * Hkv
     n_chunks = S // CL
     kv = Hkv * D
     g = torch.Generator(device=device).manual_seed(0)
@@ -622,7 +623,7 @@ def run_kv_microbench(args):
     table = ops.ChunkTable(entries, range(L), device)
     deltas = torch.randint(0, 32768, (n_chunks,), generator=torch.Generator().manual_seed(1))
     positions = (deltas.repeat_interleave(CL) + torch.arange(CL).repeat(n_chunks)).to(device)
-    invf = torch.from_numpy(__import__("oracle.hotpath", fromlist=["x"]).inv_freq(1e6, D)).to(device)
+    invf = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float32, device=device) / D))
     rope = ops.rope_table(invf, int(positions.max()) + 1)
     fk = torch.empty((L, S, kv), dtype=torch.bfloat16, device=device)
     fv = torch.empty_like(fk)
@@ -1319,6 +1320,8 @@ def main():
     ap.add_argument("--attn-dist", default="uniform", choices=["uniform", "tail"])
     ap.add_argument("--sh-layers", type=int, default=80, help="layers of the sharded 128K workload")
     ap.add_argument("--kv-layers", type=int, default=32, help="layers of the KV microbench")
+    ap.add_argument("--kv-heads", type=int, default=8,
+                    help="KV heads of the KV microbench (1: the rows one rank holds with 8 heads over 8 GPUs)")
     ap.add_argument("--kv-arena", action="store_true", help="chunk K/V in one KVArena device pool")
     ap.add_argument("--decode-tokens", type=int, default=32, help="tokens of the decode workload")
     ap.add_argument("--no-cuda-graph", action="store_true",

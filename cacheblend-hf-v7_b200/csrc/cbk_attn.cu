@@ -1139,7 +1139,9 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   if (int rc = check_launch("partial_attn_kernel")) return rc;
   // one CTA per half split tile; at most every tile is split
   const int64_t max_units = static_cast<int64_t>(n_kv_heads) * lay.n_tiles * (kBM / kCombineRows);
-  const int comb_grid = static_cast<int>(std::min<int64_t>(max_units, 2 * sm_count()));
+  // one wave: a CTA per work unit (the plan's split tiles are not known on the host;
+  // CTAs past the plan's units exit at once), up to eight per SM
+  const int comb_grid = static_cast<int>(std::min<int64_t>(max_units, 8 * sm_count()));
   attn_combine_kernel<DT, HD><<<static_cast<unsigned>(comb_grid), kCombineThreads, 0, st>>>(prm);
   return check_launch("attn_combine_kernel");
 }

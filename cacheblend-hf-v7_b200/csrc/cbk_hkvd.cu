@@ -121,6 +121,7 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 constexpr int kTopkThreads = 1024;
 constexpr int kTopkWarps = kTopkThreads / 32;
 constexpr int64_t kTopkSmemKeys = 40960;   // keys cached in shared memory up to this S
+constexpr int kTopkUnroll = 8;             // 32-key tiles whose loads are issued together
 
 // Each warp owns one contiguous chunk of the keys (a multiple of 32 long) and
 // walks it in 32-key tiles, lane = key within the tile: loads are coalesced,
@@ -150,11 +151,17 @@ topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
     const uint32_t prefix = s_prefix, mask = s_mask;
-    for (int64_t b = w_lo; b < w_hi; b += 32) {
-      const int64_t i = b + lane;
-      if (i < w_hi) {
-        const uint32_t key = key_at(i);
-        if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+    for (int64_t b = w_lo; b < w_hi; b += 32 * kTopkUnroll) {
+      uint32_t key[kTopkUnroll];            // all loads of the batch first (L2 round trips overlap)
+#pragma unroll
+      for (int u = 0; u < kTopkUnroll; ++u) {
+        const int64_t i = b + u * 32 + lane;
+        key[u] = i < w_hi ? key_at(i) : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < kTopkUnroll; ++u) {
+        const int64_t i = b + u * 32 + lane;
+        if (i < w_hi && (key[u] & mask) == prefix) atomicAdd(&s_hist[(key[u] >> shift) & 255u], 1u);
       }
     }
     __syncthreads();
@@ -203,11 +210,19 @@ topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
   // ordered compaction: per-warp counts, warp offsets, then each warp writes its keys
   const unsigned lt_mask = (1u << lane) - 1u;
   uint32_t n_gt = 0, n_eq = 0;
-  for (int64_t b = w_lo; b < w_hi; b += 32) {
-    const int64_t i = b + lane;
-    const uint32_t key = i < w_hi ? key_at(i) : 0u;
-    n_gt += __popc(__ballot_sync(0xffffffffu, i < w_hi && key > T));
-    n_eq += __popc(__ballot_sync(0xffffffffu, i < w_hi && key == T));
+  for (int64_t b = w_lo; b < w_hi; b += 32 * kTopkUnroll) {
+    uint32_t key[kTopkUnroll];
+#pragma unroll
+    for (int u = 0; u < kTopkUnroll; ++u) {
+      const int64_t i = b + u * 32 + lane;
+      key[u] = i < w_hi ? key_at(i) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < kTopkUnroll; ++u) {
+      const bool in = b + u * 32 + lane < w_hi;
+      n_gt += __popc(__ballot_sync(0xffffffffu, in && key[u] > T));
+      n_eq += __popc(__ballot_sync(0xffffffffu, in && key[u] == T));
+    }
   }
   if (lane == 0) {
     s_wa[warp] = n_gt;
@@ -241,10 +256,18 @@ topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
   }
   __syncthreads();
   int64_t eq_rank0 = s_wa[warp], out = s_wb[warp];
-  for (int64_t b = w_lo; b < w_hi; b += 32) {
-    const int64_t i = b + lane;
+  for (int64_t b0 = w_lo; b0 < w_hi; b0 += 32 * kTopkUnroll) {
+  uint32_t keys[kTopkUnroll];
+#pragma unroll
+  for (int u = 0; u < kTopkUnroll; ++u) {
+    const int64_t i = b0 + u * 32 + lane;
+    keys[u] = i < w_hi ? key_at(i) : 0u;
+  }
+#pragma unroll
+  for (int u = 0; u < kTopkUnroll; ++u) {
+    const int64_t i = b0 + u * 32 + lane;
     const bool valid = i < w_hi;
-    const uint32_t key = valid ? key_at(i) : 0u;
+    const uint32_t key = keys[u];
     const bool eq = valid && key == T;
     const unsigned eq_bal = __ballot_sync(0xffffffffu, eq);
     const int64_t eq_rank = eq_rank0 + __popc(eq_bal & lt_mask);
@@ -257,6 +280,7 @@ topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
     }
     eq_rank0 += __popc(eq_bal);
     out += __popc(sel_bal);
+  }
   }
 }
 

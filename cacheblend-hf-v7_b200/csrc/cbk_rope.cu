@@ -101,15 +101,18 @@ __device__ __forceinline__ void rope_group(const uint16_t* src_row, uint16_t* ds
 }
 
 // ---------------------------------------------------------------------------
-// (a)+(b) assemble: one layer per blockIdx.y, kAsmRows rows per block, two warps
-// per row: the even warp rotates the row's K (n_kv_heads * head_dim/16 pair
-// groups), the odd warp copies its V (kv_dim/8 16-byte vectors).  Each lane
-// issues all the loads of a batch (2 K groups = 4 vectors, or 4 V vectors)
-// before any arithmetic or store, so a warp keeps 2 KB in flight.
+// (a)+(b) assemble: one layer per blockIdx.y, kAsmRows * kAsmRowIters rows per
+// block, two warps per row set: the even warp rotates the rows' K (pair groups
+// of 8 (lo, hi) elements), the odd warp copies their V (16-byte vectors).  A
+// warp pass covers as many of its rows as fit 32 lanes x a batch (2 K groups =
+// 4 vectors, or 4 V vectors per lane): one row of a 1024-wide K/V, four rows of
+// a 128-wide one (a rank holding one KV head), so a warp keeps ~2 KB in flight
+// whatever the row width.  Each lane issues all the loads of its batch before
+// any arithmetic or store.
 // ---------------------------------------------------------------------------
 constexpr int kAsmThreads = 256;
-constexpr int kAsmRows = kAsmThreads / 64;   // rows in flight per block
-constexpr int kAsmRowIters = 4;               // rows per warp pair, in sequence
+constexpr int kAsmRows = kAsmThreads / 64;   // warp pairs per block
+constexpr int kAsmRowIters = 4;               // rows per warp pair (rows it * kAsmRows + pair)
 constexpr int kMaxChunksSmem = 2048;
 constexpr int kAsmKBatch = 2;     // K pair groups per lane per batch
 constexpr int kAsmVBatch = 4;     // V vectors per lane per batch
@@ -126,71 +129,92 @@ assemble_kernel(const cbk_chunk_src* __restrict__ srcs, const int64_t* __restric
   for (int c = threadIdx.x; c <= n_chunks; c += blockDim.x) s_start[c] = chunk_start[c];
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int it = 0; it < kAsmRowIters; ++it) {
-  const int64_t t = (static_cast<int64_t>(blockIdx.x) * kAsmRowIters + it) * kAsmRows + (warp >> 1);
-  if (t >= S) break;
-  // chunk of row t: largest c with s_start[c] <= t (warp-uniform)
-  int lo = 0, hi = n_chunks - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (s_start[mid] <= t) lo = mid; else hi = mid - 1;
-  }
-  const int64_t local = t - s_start[lo];
   const int kv_dim = n_kv_heads * head_dim;
-  const cbk_chunk_src src = srcs[static_cast<int64_t>(layer) * n_chunks + lo];
-  if ((warp & 1) == 0) {
-    const int64_t p = positions ? positions[t] : t;
-    if (p < 0 || p >= table_rows) {
-      if (lane == 0) report(status, CBK_STATUS_BAD_INDEX);
-      continue;
+  const int gph = head_dim >> 4;               // pair groups per head
+  const int half = head_dim >> 1;
+  const bool is_k = (warp & 1) == 0;
+  const int per_row = is_k ? n_kv_heads * gph : kv_dim >> 3;          // K groups or V vectors
+  const int slots = 32 * (is_k ? kAsmKBatch : kAsmVBatch);            // per lane batch x 32 lanes
+  const int rpp = max(1, min(kAsmRowIters, slots / per_row));          // rows of this warp per pass
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kAsmRowIters * kAsmRows + (warp >> 1);
+  // row it of this warp pair, its chunk and its row inside the chunk
+  auto row_of = [&](int it, int64_t& t, int& c, int64_t& local) {
+    t = row0 + static_cast<int64_t>(it) * kAsmRows;
+    int lo = 0, hi = n_chunks - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_start[mid] <= t) lo = mid; else hi = mid - 1;
     }
-    const int gph = head_dim >> 4;               // pair groups per head
-    const int kgroups = n_kv_heads * gph;
-    const int half = head_dim >> 1;
-    const uint16_t* krow = static_cast<const uint16_t*>(src.k) + local * kv_dim;
-    uint16_t* drow = k_out + layer * layer_stride + t * kv_dim;
-    const float2* cs = table + p * half;
-    for (int g0 = 0; g0 < kgroups; g0 += 32 * kAsmKBatch) {
-      uint4 xl[kAsmKBatch], xh[kAsmKBatch];
+    c = lo;
+    local = t - s_start[lo];
+  };
+  for (int it0 = 0; it0 < kAsmRowIters; it0 += rpp) {
+    const int span = rpp * per_row;                                    // slots of this pass
+    if (is_k) {
+      for (int s0 = 0; s0 < span; s0 += 32 * kAsmKBatch) {
+        // loads first (addresses recomputed for the stores: fewer live registers)
+        uint4 xl[kAsmKBatch], xh[kAsmKBatch];
 #pragma unroll
-      for (int q = 0; q < kAsmKBatch; ++q) {
-        const int g = g0 + q * 32 + lane;
-        if (g < kgroups) {
+        for (int q = 0; q < kAsmKBatch; ++q) {
+          const int sl = s0 + q * 32 + lane;
+          const int it = it0 + sl / per_row, g = sl % per_row;
+          if (sl >= span || it >= kAsmRowIters) continue;
+          int64_t t, local;
+          int c;
+          row_of(it, t, c, local);
+          if (t >= S) continue;
           const int off = (g / gph) * head_dim + (g % gph) * 8;
+          const uint16_t* krow =
+              static_cast<const uint16_t*>(srcs[static_cast<int64_t>(layer) * n_chunks + c].k) + local * kv_dim;
           xl[q] = ld_stream(krow + off);
           xh[q] = ld_stream(krow + off + half);
         }
-      }
 #pragma unroll
-      for (int q = 0; q < kAsmKBatch; ++q) {
-        const int g = g0 + q * 32 + lane;
-        if (g < kgroups) {
+        for (int q = 0; q < kAsmKBatch; ++q) {
+          const int sl = s0 + q * 32 + lane;
+          const int it = it0 + sl / per_row, g = sl % per_row;
+          if (sl >= span || it >= kAsmRowIters) continue;
+          const int64_t t = row0 + static_cast<int64_t>(it) * kAsmRows;
+          if (t >= S) continue;
+          const int64_t p = positions ? positions[t] : t;
+          if (p < 0 || p >= table_rows) {
+            report(status, CBK_STATUS_BAD_INDEX);
+            continue;
+          }
           const int off = (g / gph) * head_dim + (g % gph) * 8;
           uint4 ol, oh;
-          rope8<DT>(xl[q], xh[q], cs + (g % gph) * 8, mode, ol, oh);
-          st_vec(drow + off, ol);
-          st_vec(drow + off + half, oh);
+          rope8<DT>(xl[q], xh[q], table + p * half + (g % gph) * 8, mode, ol, oh);
+          uint16_t* d = k_out + layer * layer_stride + t * kv_dim + off;
+          st_vec(d, ol);
+          st_vec(d + half, oh);
+        }
+      }
+    } else {
+      for (int s0 = 0; s0 < span; s0 += 32 * kAsmVBatch) {
+        uint4 x[kAsmVBatch];
+#pragma unroll
+        for (int q = 0; q < kAsmVBatch; ++q) {
+          const int sl = s0 + q * 32 + lane;
+          const int it = it0 + sl / per_row, v = sl % per_row;
+          if (sl >= span || it >= kAsmRowIters) continue;
+          int64_t t, local;
+          int c;
+          row_of(it, t, c, local);
+          if (t >= S) continue;
+          x[q] = ld_stream(static_cast<const uint16_t*>(srcs[static_cast<int64_t>(layer) * n_chunks + c].v) +
+                           local * kv_dim + v * 8);
+        }
+#pragma unroll
+        for (int q = 0; q < kAsmVBatch; ++q) {
+          const int sl = s0 + q * 32 + lane;
+          const int it = it0 + sl / per_row, v = sl % per_row;
+          if (sl >= span || it >= kAsmRowIters) continue;
+          const int64_t t = row0 + static_cast<int64_t>(it) * kAsmRows;
+          if (t >= S) continue;
+          st_vec(v_out + layer * layer_stride + t * kv_dim + v * 8, x[q]);
         }
       }
     }
-  } else {
-    const int vvecs = kv_dim >> 3;
-    const uint16_t* vrow = static_cast<const uint16_t*>(src.v) + local * kv_dim;
-    uint16_t* drow = v_out + layer * layer_stride + t * kv_dim;
-    for (int v0 = 0; v0 < vvecs; v0 += 32 * kAsmVBatch) {
-      uint4 x[kAsmVBatch];
-#pragma unroll
-      for (int q = 0; q < kAsmVBatch; ++q) {
-        const int v = v0 + q * 32 + lane;
-        if (v < vvecs) x[q] = ld_stream(vrow + v * 8);
-      }
-#pragma unroll
-      for (int q = 0; q < kAsmVBatch; ++q) {
-        const int v = v0 + q * 32 + lane;
-        if (v < vvecs) st_vec(drow + v * 8, x[q]);
-      }
-    }
-  }
   }
 }
 

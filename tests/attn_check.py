@@ -76,12 +76,14 @@ def _f32(t, dtype):
     return DEC[dtype](t.contiguous().view(torch.int16).numpy().view(np.uint16))
 
 
-def oracle(case, q, k, v, pos, heads=None):
-    """(exp, A) of the case from the fp64 oracle."""
+def oracle(case, q, k, v, pos, heads=None, rows=None):
+    """(exp, A) of the case from the fp64 oracle (of the selected rows ``rows``
+    only when given: query rows are independent)."""
     _, S, n_sel, Hq, Hkv, D, dtype, _, _ = case
-    return hp.partial_attention(_f32(q, dtype).reshape(n_sel, Hq, D), _f32(k, dtype).reshape(S, Hkv, D),
-                                _f32(v, dtype).reshape(S, Hkv, D), pos.numpy(), D ** -0.5,
-                                with_abs=True, heads=heads)
+    rows = np.arange(n_sel) if rows is None else np.asarray(rows)
+    qf = _f32(q, dtype).reshape(n_sel, Hq, D)[rows]
+    return hp.partial_attention(qf, _f32(k, dtype).reshape(S, Hkv, D), _f32(v, dtype).reshape(S, Hkv, D),
+                                pos.numpy()[rows], D ** -0.5, with_abs=True, heads=heads)
 
 
 def violations(got, exp, absm, dtype, cols=None):
@@ -149,9 +151,10 @@ def plan(pos, n_sel, G, Hkv, sms=148, c0=2):
     return row_tile, tile_pair, cuts
 
 
-def planted(case, q, k, v, pos, mistake, heads):
+def planted(case, q, k, v, pos, mistake, heads, rows=None):
     """The case's attention (fp64) with one planted mistake, for the q heads
-    in ``heads``; returns (n, Hq*D) with the other columns zero.  The split
+    in ``heads`` (and the selected rows ``rows`` when given); returns
+    (rows, Hq*D) with the other columns zero.  The split
     mistakes act on the kernel's own pieces (``plan``): "drop_split_chunk"
     leaves out a split row's second piece of keys, "merge_without_max" merges
     the pieces' O / l with weights l_c, without the 2^(m_c - M) correction."""
@@ -160,14 +163,17 @@ def planted(case, q, k, v, pos, mistake, heads):
     qf = _f32(q, dtype).reshape(n_sel, Hq, D).astype(np.float64)
     kf = _f32(k, dtype).reshape(S, Hkv, D).astype(np.float64)
     vf = _f32(v, dtype).reshape(S, Hkv, D).astype(np.float64)
-    p_ = pos.numpy()
-    row_tile, tile_pair, cuts = plan(p_, n_sel, G, Hkv)
+    row_tile, tile_pair, cuts = plan(pos.numpy(), n_sel, G, Hkv)
+    rows = np.arange(n_sel) if rows is None else np.asarray(rows)
+    p_ = pos.numpy()[rows]
+    qf = qf[rows]
+    n_r = len(rows)
     t = np.arange(S)
-    out = np.zeros((n_sel, Hq, D))
+    out = np.zeros((n_r, Hq, D))
     for h in heads:
         kvh = h // G
         # key bounds of each row's pieces: [0, c1, c2, ..., end) in keys
-        bounds = [[0] + [c * 128 for c in cuts[(kvh, tile_pair[row_tile[j]])]] + [S] for j in range(n_sel)]
+        bounds = [[0] + [c * 128 for c in cuts[(kvh, tile_pair[row_tile[j]])]] + [S] for j in rows]
         s = (qf[:, h] @ kf[:, kvh].T) * D ** -0.5
         if mistake == "causal_plus_one":
             vis = t[None, :] <= p_[:, None] + 1
@@ -201,7 +207,7 @@ def planted(case, q, k, v, pos, mistake, heads):
                     wsum += l
                 exact[j] = o / wsum
         out[:, h] = exact
-    return out.reshape(n_sel, Hq * D)
+    return out.reshape(n_r, Hq * D)
 
 
 def round_to(x, dtype):
