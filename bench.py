@@ -252,12 +252,21 @@ def run_ours(args):
     spans = list(TIMES.graph_spans)
     TIMES.reset()
     acc = {}
+    inst_ms = 0.0
     for i in range(args.steps):
+        a_ev = torch.cuda.Event(enable_timing=True)
+        b_ev = torch.cuda.Event(enable_timing=True)
+        a_ev.record(stream)
         tg.replay(reqs[i % len(reqs)], store, input_ids=dev_ids[i % len(reqs)])
+        b_ev.record(stream)
         torch.cuda.synchronize()
+        inst_ms += a_ev.elapsed_time(b_ev)
         TIMES.read_graph_spans(spans, acc)
     del tg
     kern = {name: (v[0], v[1]) for name, v in acc.items()}
+    instrumented = {"ms_per_step": round(inst_ms / args.steps, 3), "event_spans_per_step": len(spans),
+                    "note": "the graph with an event pair around every libcbk launch, replayed alone per step "
+                            "(its step time against the plain graph's shows what the event nodes cost)"}
     # the graph's launches plus the dense-logits scatter fuse_selective runs after the replay
     launch_counts = {name: v[2] for name, v in acc.items()}
     launch_counts["scatter_rows"] = launch_counts.get("scatter_rows", 0) + args.steps
@@ -367,6 +376,7 @@ def run_ours(args):
                               "times the steps, plus the dense-logits scatter run after each replay"),
         "clocks": clk,
         "eager_launches": eager_res,
+        "instrumented_graph": instrumented,
         "timed_path": ("fuse_selective default: a CUDA graph of the request geometry, captured on the first "
                        "call, replayed per step" if use_graph else "fuse_selective(cuda_graph=False)"),
     }
@@ -1272,6 +1282,12 @@ def run_attn_layers(args):
         pos = torch.arange(S, device=device)
     elif args.attn_dist == "tail":      # the last k positions (a selection clustered at the end)
         pos = torch.arange(S - k, S, device=device)
+    elif args.attn_dist == "blend":     # like the 7K blend's HKVD picks: none in chunk 0 (its K equals
+        # the cached K), 37 % in the last 1088 positions, the rest uniform over [1024, 5120)
+        n_tail = int(0.373 * k) - 1
+        tail = torch.randperm(S - 1 - 5120, generator=gc)[:n_tail] + 5120
+        mid = torch.randperm(5120 - 1024, generator=gc)[:k - 1 - n_tail] + 1024
+        pos = torch.cat([torch.sort(torch.cat([mid, tail])).values, torch.tensor([S - 1])]).to(device)
     else:
         pos = torch.cat([torch.sort(torch.randperm(S - 1, generator=gc)[:k - 1]).values,
                          torch.tensor([S - 1])]).to(device)
@@ -1317,7 +1333,7 @@ def main():
                              "llama3-8b-32k-x64", "mistral7b-7k-decode", "decode-kernels"])
     ap.add_argument("--attn-layers", type=int, default=31)
     ap.add_argument("--attn-k", type=int, default=931, help="selected rows (6208 = dense causal)")
-    ap.add_argument("--attn-dist", default="uniform", choices=["uniform", "tail"])
+    ap.add_argument("--attn-dist", default="uniform", choices=["uniform", "tail", "blend"])
     ap.add_argument("--sh-layers", type=int, default=80, help="layers of the sharded 128K workload")
     ap.add_argument("--kv-layers", type=int, default=32, help="layers of the KV microbench")
     ap.add_argument("--kv-heads", type=int, default=8,

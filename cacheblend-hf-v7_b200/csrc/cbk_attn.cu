@@ -59,6 +59,22 @@ constexpr int kThreads = 384;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kMaxKvTiles = 2049;          // S <= 262144
 
+// Fixed cost of one work item in key-tile steps (Q load, pipeline refill and
+// epilogue of a Q-tile pair), for the plan's balance.
+#ifndef CBK_ATTN_ITEM_COST
+#define CBK_ATTN_ITEM_COST 2
+#endif
+constexpr int kAttnItemCost = CBK_ATTN_ITEM_COST;
+#ifndef CBK_ATTN_WORKERS_PER_SM
+#define CBK_ATTN_WORKERS_PER_SM 1
+#endif
+constexpr int kAttnWorkersPerSm = CBK_ATTN_WORKERS_PER_SM;
+// Share of the cost (percent) left to a dynamic tail of whole short units.
+#ifndef CBK_ATTN_DYN_PCT
+#define CBK_ATTN_DYN_PCT 0
+#endif
+constexpr int kAttnDynPct = CBK_ATTN_DYN_PCT;
+
 template <int HD>
 struct AttnSmem {
   static constexpr int kQBytes = kBM * HD * 2;     // one Q tile
@@ -359,6 +375,9 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (leader) w = atomicAdd(prm.queue, 1);
         w = __shfl_sync(0xffffffffu, w, leader_lane);
         if (w >= n_workers) {
+          // no work left to hand out: the merge kernel (a programmatic dependent of
+          // this one) may be scheduled as SMs free up; it waits for this grid to finish
+          asm volatile("griddepcontrol.launch_dependents;");
           it = it_end = 0;
           break;
         }
@@ -842,24 +861,40 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
     return;
   }
 
-  // ---- equal ranges of cost: unit u's steps are [Q_u, Q_u + L) in cost space,
-  //      Q_u = (u + 1) c0 + P_u (P_u its first step in step space)
-  auto worker_of = [&](int64_t x) { return ((x + 1) * B + Wc - 1) / Wc - 1; };
-  auto worker_start = [&](int64_t w) { return w * Wc / B; };
-  for (int64_t w = tid; w < B; w += kPlanThreads) first_item[w] = 0x7fffffff;
+  // ---- a dynamic tail: the shortest units (pairs p < p_cut, every head), about
+  //      kAttnDynPct % of the cost, are whole items taken longest first by the CTAs
+  //      that finish their static range early (each is a worker after the B static ones)
+  if (tid == 0) s_lmax = 0;                                   // reused: p_cut
+  __syncthreads();
+  const int64_t dyn_budget = static_cast<int64_t>(kAttnDynPct) * Wc / 100;
+  for (int p = 1 + tid; p < n_pairs; p += kPlanThreads)
+    if (static_cast<int64_t>(n_kv_heads) * (pair_off[p] + c0 * p) <= dyn_budget) atomicMax(&s_lmax, p);
+  __syncthreads();
+  const int p_cut = s_lmax;
+  const int n_ps = n_pairs - p_cut;                           // static pairs (>= 1)
+  const int64_t Wh_s = Wh - pair_off[p_cut];
+  const int64_t W_s = Wh_s * n_kv_heads;
+  const int n_units_s = n_kv_heads * n_ps;
+  const int64_t Wc_s = W_s + c0 * n_units_s;
+  const int64_t Bs = W_s < target_workers ? W_s : target_workers;
+  // ---- the static units as equal ranges of cost: unit u's steps are [Q_u, Q_u + L)
+  //      in cost space, Q_u = (u + 1) c0 + P_u (P_u its first step in step space)
+  auto worker_of = [&](int64_t x) { return ((x + 1) * Bs + Wc_s - 1) / Wc_s - 1; };
+  auto worker_start = [&](int64_t w) { return w * Wc_s / Bs; };
+  for (int64_t w = tid; w < Bs; w += kPlanThreads) first_item[w] = 0x7fffffff;
   __syncthreads();
   int item_carry = 0, slot_carry = 0, split_carry = 0;
-  for (int b0 = 0; b0 < n_units; b0 += kPlanThreads) {
+  for (int b0 = 0; b0 < n_units_s; b0 += kPlanThreads) {
     const int u = b0 + tid;
     int n_pieces = 0, m_a = 0, ta = -1, tb = -1, L = 0, La = 0;
     int64_t Q = 0, wa = 0;
-    if (u < n_units) {
-      const int h = u / n_pairs, p = u % n_pairs;
+    if (u < n_units_s) {
+      const int h = u / n_ps, p = p_cut + u % n_ps;
       ta = pair_tile(n_tiles, p, 0);
       tb = pair_tile(n_tiles, p, 1);
       L = pair_off[p + 1] - pair_off[p];
       La = tile_len(ta);
-      Q = (u + 1) * c0 + h * Wh + pair_off[p];
+      Q = (u + 1) * c0 + h * Wh_s + (pair_off[p] - pair_off[p_cut]);
       wa = worker_of(Q);
       n_pieces = static_cast<int>(worker_of(Q + L - 1) - wa + 1);
       m_a = La > 0 ? static_cast<int>(worker_of(Q + La - 1) - wa + 1) : 0;
@@ -869,8 +904,8 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
     const int item0 = item_carry + block_excl_scan(n_pieces, s_warp, &tot_items);
     const int slot0 = slot_carry + block_excl_scan(slots_a + slots_b, s_warp, &tot_slots);
     const int split0 = split_carry + block_excl_scan((slots_a > 0) + (slots_b > 0), s_warp, &tot_split);
-    if (u < n_units) {
-      const int h = u / n_pairs, p = u % n_pairs;
+    if (u < n_units_s) {
+      const int h = u / n_ps, p = p_cut + u % n_ps;
       for (int i = 0; i < n_pieces; ++i) {
         const int64_t w = wa + i;
         const int64_t sw = worker_start(w), sw1 = worker_start(w + 1);
@@ -890,15 +925,28 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
     slot_carry += tot_slots;
     split_carry += tot_split;
   }
+  // the dynamic units: whole, pairs p_cut - 1 down to 0, each its own worker
+  const int n_dyn = n_kv_heads * p_cut;
+  for (int i = tid; i < n_dyn; i += kPlanThreads) {
+    const int p = p_cut - 1 - i / n_kv_heads, h = i % n_kv_heads;
+    const int at = item_carry + i;
+    if (at < max_items) items[at] = make_int4(h, p, 0, pair_off[p + 1] - pair_off[p]);
+    first_item[Bs + i] = at;
+    const int ta = pair_tile(n_tiles, p, 0), tb = pair_tile(n_tiles, p, 1);
+    if (ta >= 0) tile_base[h * n_tiles + ta] = -1;
+    tile_base[h * n_tiles + tb] = -1;
+  }
   __syncthreads();
   if (tid == 0) {
-    if (item_carry > max_items || slot_carry > max_slots) s_error = 1;
-    // a worker whose range holds no step (it fell inside items' overheads) has no items
-    first_item[B] = item_carry;
-    for (int64_t w = B - 1; w >= 0; --w)
+    const int n_items = item_carry + n_dyn;
+    if (n_items > max_items || slot_carry > max_slots) s_error = 1;
+    // a static worker whose range holds no step (it fell inside items' overheads) has no items
+    first_item[Bs + n_dyn] = n_items;
+    if (n_dyn == 0) first_item[Bs] = item_carry;
+    for (int64_t w = Bs - 1; w >= 0; --w)
       if (first_item[w] == 0x7fffffff) first_item[w] = first_item[w + 1];
-    hdr->n_items = item_carry;
-    hdr->n_workers = static_cast<int>(B);
+    hdr->n_items = n_items;
+    hdr->n_workers = static_cast<int>(Bs) + n_dyn;
     hdr->n_split = split_carry;
     hdr->n_slots = slot_carry;
     hdr->error = s_error;
@@ -929,6 +977,9 @@ attn_combine_kernel(const AttnParams prm) {
   constexpr int kVecThr = kCombineRows * kVecRow / kCombineThreads;  // 4 (HD 128) or 2 (HD 64)
   constexpr int kRowStep = kCombineThreads / kVecRow;                 // rows between a thread's vectors
   const int tid = threadIdx.x;
+  // launched as a programmatic dependent of the attention kernel: wait until that
+  // grid has finished and its partial results are visible (a no-op otherwise)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // every attention CTA has finished: rewind the item queue for the next call
   if (blockIdx.x == 0 && tid == 0) *prm.queue = 0;
   if (prm.plan->error) return;
@@ -1063,12 +1114,6 @@ struct AttnLayout {
 
 static size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-// Fixed cost of one work item in key-tile steps (Q load, pipeline refill and
-// epilogue of a Q-tile pair), for the plan's balance.
-#ifndef CBK_ATTN_ITEM_COST
-#define CBK_ATTN_ITEM_COST 2
-#endif
-constexpr int kAttnItemCost = CBK_ATTN_ITEM_COST;
 
 static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int head_dim) {
   AttnLayout a;
@@ -1076,7 +1121,7 @@ static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int 
   a.tok_per_tile = kBM / G;
   a.n_tiles = static_cast<int>((n_sel + a.tok_per_tile - 1) / a.tok_per_tile);
   a.n_pairs = (a.n_tiles + 1) / 2;
-  a.target = sm_count();                      // workers: one equal range of steps per SM
+  a.target = kAttnWorkersPerSm * sm_count();   // workers: equal ranges of cost, per SM
   // items: one per unit plus one per worker boundary inside a unit
   a.max_items = a.target + n_kv_heads * a.n_pairs;
   // a split unit holds a worker boundary, so split units' pieces number <= 2 (workers - 1),
@@ -1134,7 +1179,7 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   auto kern = partial_attn_kernel<DT, HD>;
   const int smem = AttnSmem<HD>::kAlloc;
   if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem)) return rc;
-  const int grid = lay.target;             // persistent: one CTA per SM (workers beyond the plan's exit)
+  const int grid = sm_count();             // persistent: one CTA per SM, taking workers from the queue
   kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(mq, mk, mv, prm);
   if (int rc = check_launch("partial_attn_kernel")) return rc;
   // one CTA per half split tile; at most every tile is split
@@ -1142,7 +1187,20 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   // one wave: a CTA per work unit (the plan's split tiles are not known on the host;
   // CTAs past the plan's units exit at once), up to eight per SM
   const int comb_grid = static_cast<int>(std::min<int64_t>(max_units, 8 * sm_count()));
-  attn_combine_kernel<DT, HD><<<static_cast<unsigned>(comb_grid), kCombineThreads, 0, st>>>(prm);
+  // programmatic dependent launch: the merge kernel's CTAs can be placed on SMs the
+  // attention kernel has left (each attention CTA signals when the queue is empty)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(comb_grid));
+  cfg.blockDim = dim3(kCombineThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_combine_kernel<DT, HD>, prm);
+  if (e != cudaSuccess) return set_error(CBK_ERR_CUDA, "attn_combine_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("attn_combine_kernel");
 }
 

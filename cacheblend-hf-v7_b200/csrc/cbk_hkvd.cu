@@ -272,7 +272,7 @@ topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
     const unsigned eq_bal = __ballot_sync(0xffffffffu, eq);
     const int64_t eq_rank = eq_rank0 + __popc(eq_bal & lt_mask);
     bool sel = valid && (key > T || (eq && eq_rank < k_eq && !(force && eq_rank == 0)));
-    if (force && i == S - 1) sel = true;
+    if (force && valid && i == S - 1) sel = true;
     const unsigned sel_bal = __ballot_sync(0xffffffffu, sel);
     if (sel) {
       const int64_t at = out + __popc(sel_bal & lt_mask);

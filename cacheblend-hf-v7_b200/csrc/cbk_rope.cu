@@ -148,12 +148,76 @@ assemble_kernel(const cbk_chunk_src* __restrict__ srcs, const int64_t* __restric
     c = lo;
     local = t - s_start[lo];
   };
+  if (rpp == 1) {
+    // wide rows (a warp pass holds one row or less): one row at a time, its chunk,
+    // position and source pointer warp-uniform
+    for (int it = 0; it < kAsmRowIters; ++it) {
+      int64_t t, local;
+      int c;
+      row_of(it, t, c, local);
+      if (t >= S) break;
+      const cbk_chunk_src src = srcs[static_cast<int64_t>(layer) * n_chunks + c];
+      if (is_k) {
+        const int64_t p = positions ? positions[t] : t;
+        if (p < 0 || p >= table_rows) {
+          if (lane == 0) report(status, CBK_STATUS_BAD_INDEX);
+          continue;
+        }
+        const uint16_t* krow = static_cast<const uint16_t*>(src.k) + local * kv_dim;
+        uint16_t* drow = k_out + layer * layer_stride + t * kv_dim;
+        const float2* cs = table + p * half;
+        for (int g0 = 0; g0 < per_row; g0 += 32 * kAsmKBatch) {
+          uint4 xl[kAsmKBatch], xh[kAsmKBatch];
+#pragma unroll
+          for (int q = 0; q < kAsmKBatch; ++q) {
+            const int g = g0 + q * 32 + lane;
+            if (g < per_row) {
+              const int off = (g / gph) * head_dim + (g % gph) * 8;
+              xl[q] = ld_stream(krow + off);
+              xh[q] = ld_stream(krow + off + half);
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < kAsmKBatch; ++q) {
+            const int g = g0 + q * 32 + lane;
+            if (g < per_row) {
+              const int off = (g / gph) * head_dim + (g % gph) * 8;
+              uint4 ol, oh;
+              rope8<DT>(xl[q], xh[q], cs + (g % gph) * 8, mode, ol, oh);
+              st_vec(drow + off, ol);
+              st_vec(drow + off + half, oh);
+            }
+          }
+        }
+      } else {
+        const uint16_t* vrow = static_cast<const uint16_t*>(src.v) + local * kv_dim;
+        uint16_t* drow = v_out + layer * layer_stride + t * kv_dim;
+        for (int v0 = 0; v0 < per_row; v0 += 32 * kAsmVBatch) {
+          uint4 x[kAsmVBatch];
+#pragma unroll
+          for (int q = 0; q < kAsmVBatch; ++q) {
+            const int v = v0 + q * 32 + lane;
+            if (v < per_row) x[q] = ld_stream(vrow + v * 8);
+          }
+#pragma unroll
+          for (int q = 0; q < kAsmVBatch; ++q) {
+            const int v = v0 + q * 32 + lane;
+            if (v < per_row) st_vec(drow + v * 8, x[q]);
+          }
+        }
+      }
+    }
+    return;
+  }
+  // narrow rows: rpp of this warp's rows per pass, each lane on its own (row, group)
   for (int it0 = 0; it0 < kAsmRowIters; it0 += rpp) {
     const int span = rpp * per_row;                                    // slots of this pass
     if (is_k) {
       for (int s0 = 0; s0 < span; s0 += 32 * kAsmKBatch) {
-        // loads first (addresses recomputed for the stores: fewer live registers)
+        // loads first, the rows' positions with them (addresses recomputed for the
+        // stores: fewer live registers)
         uint4 xl[kAsmKBatch], xh[kAsmKBatch];
+        int64_t pq[kAsmKBatch];
 #pragma unroll
         for (int q = 0; q < kAsmKBatch; ++q) {
           const int sl = s0 + q * 32 + lane;
@@ -163,6 +227,7 @@ assemble_kernel(const cbk_chunk_src* __restrict__ srcs, const int64_t* __restric
           int c;
           row_of(it, t, c, local);
           if (t >= S) continue;
+          pq[q] = positions ? positions[t] : t;
           const int off = (g / gph) * head_dim + (g % gph) * 8;
           const uint16_t* krow =
               static_cast<const uint16_t*>(srcs[static_cast<int64_t>(layer) * n_chunks + c].k) + local * kv_dim;
@@ -176,7 +241,7 @@ assemble_kernel(const cbk_chunk_src* __restrict__ srcs, const int64_t* __restric
           if (sl >= span || it >= kAsmRowIters) continue;
           const int64_t t = row0 + static_cast<int64_t>(it) * kAsmRows;
           if (t >= S) continue;
-          const int64_t p = positions ? positions[t] : t;
+          const int64_t p = pq[q];
           if (p < 0 || p >= table_rows) {
             report(status, CBK_STATUS_BAD_INDEX);
             continue;

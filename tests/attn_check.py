@@ -114,14 +114,19 @@ def check(got, exp, absm, dtype):
 # ---------------------------------------------------------------------------
 # the kernel's split plan (attn_plan_kernel restated) and planted mistakes
 # ---------------------------------------------------------------------------
-def plan(pos, n_sel, G, Hkv, sms=148, c0=2):
+PLAN_ITEM_COST = 2      # the kernel's CBK_ATTN_ITEM_COST
+PLAN_DYN_PCT = 0        # the kernel's CBK_ATTN_DYN_PCT
+
+
+def plan(pos, n_sel, G, Hkv, sms=148, c0=PLAN_ITEM_COST, dyn=PLAN_DYN_PCT):
     """The partial-attention work plan (attn_plan_kernel restated): Q tiles of
     128/G tokens aligned to the end of the selection, paired; a pair's steps
     are its later tile's 128-key tiles, and every item costs c0 steps more.
     Small units (longest + c0 at most half an SM's share) are whole items;
-    otherwise the units, each c0 of cost then its steps, are laid end to end
-    and cut into ``sms`` equal ranges of cost, and a unit whose steps cross a
-    cut is split there.  Returns (tile of each selected row, pair of each
+    otherwise the shortest pairs' units (about ``dyn`` % of the cost) are
+    whole items of a dynamic tail, and the other units, each c0 of cost then
+    its steps, are laid end to end and cut into ``sms`` equal ranges of cost;
+    a unit whose steps cross a cut is split there.  Returns (tile of each selected row, pair of each
     tile, cuts) with cuts[(h, pair)] the key-tile indices where that unit is
     split (empty when it is not)."""
     pos = np.asarray(pos, np.int64)
@@ -141,10 +146,16 @@ def plan(pos, n_sel, G, Hkv, sms=148, c0=2):
     off = np.concatenate([[0], np.cumsum(L)])
     cuts = {(h, p): [] for h in range(Hkv) for p in range(n_pairs)}
     if (int(L.max()) + c0) * 2 * B > Wc:
-        starts = [w * Wc // B for w in range(B + 1)]
+        budget = dyn * Wc // 100
+        p_cut = max([0] + [p for p in range(1, n_pairs) if Hkv * (int(off[p]) + c0 * p) <= budget])
+        n_ps = n_pairs - p_cut
+        Wh_s = Wh - int(off[p_cut])
+        Wc_s = Hkv * Wh_s + c0 * Hkv * n_ps
+        B_s = min(Hkv * Wh_s, sms)
+        starts = [w * Wc_s // B_s for w in range(B_s + 1)]
         for h in range(Hkv):
-            for p in range(n_pairs):
-                Q = (h * n_pairs + p + 1) * c0 + h * Wh + int(off[p])
+            for p in range(p_cut, n_pairs):
+                Q = (h * n_ps + (p - p_cut) + 1) * c0 + h * Wh_s + int(off[p]) - int(off[p_cut])
                 cuts[(h, p)] = [s_ - Q for s_ in starts if Q < s_ < Q + int(L[p])]
     row_tile = (np.arange(n_sel) - first) // tpt
     tile_pair = (np.arange(n_tiles) + odd) // 2
