@@ -15,11 +15,15 @@
 // pairs' key ranges (a causal selection makes them range from one tile to all).
 //
 // The attention kernel is persistent: one CTA per SM keeps its TMEM and
-// barriers and takes workers from a queue in the workspace (one each when every
-// CTA is resident), running the items of a worker in order.  The producer
+// barriers; CTA b runs worker b, then takes further workers from a queue in the
+// workspace (none are left when every CTA is resident), running the items of a
+// worker in order.  The producer
 // publishes each item to the other warps through a two-slot ring in shared
 // memory and loads the next item's Q as soon as the current item's last
-// S = Q K^T has been issued, so set-up costs overlap the previous item.
+// S = Q K^T has been issued, so set-up costs overlap the previous item.  The
+// copies go out in the order the first MMAs need them (Q tile 0, K, Q tile 1,
+// V), and the first worker needs no queue round trip, which shortens the
+// start of the call, when every CTA loads at once.
 //
 // TMEM (512 columns): tile t uses S/P at [256t, 256t+128) and O at
 // [256t+128, 256t+128+D).  S lands in fp32; the softmax warps write P back in
@@ -92,7 +96,7 @@ struct AttnSmem {
 
 enum Bar { B_QFULL = 0, B_QEMPTY = 1, B_KFULL = 2, B_KEMPTY = 4, B_VFULL = 6, B_VEMPTY = 8,
            B_SFULL = 10, B_PFULL = 12, B_ODONE = 14, B_OFREE = 16, B_IFULL = 18, B_IEMPTY = 20,
-           B_DRAIN = 22 };
+           B_DRAIN = 22, B_QFULL1 = 23 };   // B_QFULL: Q tile 0 landed, B_QFULL1: Q tile 1
 
 // Work plan in the caller's workspace (written by attn_plan_kernel).
 struct AttnPlanHeader {
@@ -124,6 +128,7 @@ struct AttnParams {
   int tok_per_tile;   // 128 / G
   int n_tiles;        // Q tiles per KV head
   float scale_log2;
+  int store_v8;       // out and workspace are 32-byte aligned: 32-byte epilogue stores
 };
 
 __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
@@ -145,6 +150,28 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   } else {
     const __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&v);
+  }
+}
+
+// 32 fp32 values of a row times inv, rounded to the 16-bit type, stored to dst: as
+// two 32-byte stores (whole sectors) when the caller's buffers are 32-byte aligned,
+// else as four 16-byte stores.  The epilogue's stores are scattered rows (one row
+// per thread), so whole-sector stores halve the requests and leave no partial sector.
+template <int DT>
+__device__ __forceinline__ void store_chunk(uint16_t* dst, const uint32_t (&o)[32], float inv, bool v8) {
+  uint32_t w[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) w[e] = pack2<DT>(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+  if (v8) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+                   :: "l"(dst + 16 * h), "r"(w[8 * h]), "r"(w[8 * h + 1]), "r"(w[8 * h + 2]), "r"(w[8 * h + 3]),
+                      "r"(w[8 * h + 4]), "r"(w[8 * h + 5]), "r"(w[8 * h + 6]), "r"(w[8 * h + 7])
+                   : "memory");
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) st_vec(dst + 8 * q, make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]));
   }
 }
 
@@ -228,6 +255,39 @@ __device__ __forceinline__ void exp2_fma_pair(float x0, float x1, float& y0, flo
 #define CBK_ATTN_EMU_MASK 0x9292
 #endif
 
+// P = 2^(s * sl2 - m) of columns [32 c4, 32 c4 + 32) of a row, packed into 16-bit
+// pairs, with the row sum accumulated in packed fp32 pairs.  6 of the 16 pairs go
+// to the FMA-pipe polynomial.  With kMasked, keys c > lim are invisible: their
+// argument is set to -inf before ex2.approx (which gives 0), and the polynomial's
+// result (clamped at 2^-126) is replaced by 0.
+template <int DT, bool kMasked>
+__device__ __forceinline__ void exp_chunk(const uint32_t (&s)[kBN], int c4, float sl2, float neg_m, int lim,
+                                          float& ra0, float& ra1, float& rb0, float& rb1, uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const int c = c4 * 32 + 2 * e;
+    float x0, x1, p0, p1;
+    fma2(x0, x1, __uint_as_float(s[c]), __uint_as_float(s[c + 1]), sl2, neg_m);
+    if ((CBK_ATTN_EMU_MASK >> e) & 1) {
+      exp2_fma_pair(x0, x1, p0, p1);
+      if (kMasked) {
+        p0 = c <= lim ? p0 : 0.f;
+        p1 = c + 1 <= lim ? p1 : 0.f;
+      }
+    } else {
+      if (kMasked) {
+        x0 = c <= lim ? x0 : -INFINITY;
+        x1 = c + 1 <= lim ? x1 : -INFINITY;
+      }
+      p0 = ex2(x0);
+      p1 = ex2(x1);
+    }
+    if (e & 1) add2(rb0, rb1, p0, p1);
+    else add2(ra0, ra1, p0, p1);
+    pk[e] = pack2<DT>(p0, p1);
+  }
+}
+
 // Pair p holds tiles 2p - o and 2p + 1 - o, o = n_tiles mod 2: with an odd
 // count the tile without a partner is tile 0, the shortest, not the last one.
 __device__ __forceinline__ int pair_tile(int n_tiles, int pair, int t) {
@@ -310,6 +370,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 
   if (threadIdx.x == 0) {
     mbar_init(bar(B_QFULL), 1);
+    mbar_init(bar(B_QFULL1), 1);
     mbar_init(bar(B_QEMPTY), 1);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -365,15 +426,21 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     int last_k[2] = {-1, -1}, last_v[2] = {-1, -1};
     int n_q = 0;                             // Q loads issued
     int it = 0, it_end = 0;                  // items left of the current worker
+    bool first_worker = true;
     for (int n = 0; !failed; ++n) {
       if (n >= 2 && !wait_all(bar(B_IEMPTY + (n & 1)), ((n >> 1) - 1) & 1)) {
         failed = true;
         break;
       }
-      while (it >= it_end) {                 // next worker with items from the queue
-        int w = 0;
-        if (leader) w = atomicAdd(prm.queue, 1);
-        w = __shfl_sync(0xffffffffu, w, leader_lane);
+      while (it >= it_end) {                 // next worker with items
+        // worker b is CTA b's first (no round trip to the queue before the first
+        // copies); the queue hands out workers gridDim.x, gridDim.x + 1, ...
+        int w = blockIdx.x;
+        if (!first_worker) {
+          if (leader) w = static_cast<int>(gridDim.x) + atomicAdd(prm.queue, 1);
+          w = __shfl_sync(0xffffffffu, w, leader_lane);
+        }
+        first_worker = false;
         if (w >= n_workers) {
           // no work left to hand out: the merge kernel (a programmatic dependent of
           // this one) may be scheduled as SMs free up; it waits for this grid to finish
@@ -393,24 +460,37 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         mbar_arrive(bar(B_IFULL + (n & 1)));   // release: the slot is visible to the waiters
       }
       if (item.x < 0) break;
-      const ItemGeom ig = item_geom(item, prm);
+      // The copies need only the item's head, tiles and first key tile; the key-tile
+      // count needs the positions, so it is read once the first copies are in flight.
+      const int kvh = item.x, j0 = item.z;
+      bool has[2];
+      int tok0[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int tile = pair_tile(prm.n_tiles, item.y, t);
+        has[t] = tile >= 0 && tile < prm.n_tiles;
+        tok0[t] = static_cast<int>(tile_tok0(prm.n_sel, prm.n_tiles, prm.tok_per_tile, tile));
+      }
       // Q of this item once the previous item's last S = Q K^T has been issued
       if (n_q > 0 && !wait_all(bar(B_QEMPTY), (n_q - 1) & 1)) {
         failed = true;
         break;
       }
-      if (leader) {
-        mbar_expect_tx(bar(B_QFULL), (ig.has[0] + ig.has[1]) * L::kQBytes);
-        for (int t = 0; t < 2; ++t) {
-          if (!ig.has[t]) continue;
+      // Copies in the order the first MMAs need them: Q tile 0, K, Q tile 1, V (a
+      // missing tile's barrier completes on the arrive alone)
+      auto load_q = [&](int t) {
+        if (!leader) return;
+        const uint32_t b = bar(t ? B_QFULL1 : B_QFULL);
+        mbar_expect_tx(b, has[t] ? L::kQBytes : 0);
+        if (!has[t]) return;
 #pragma unroll
-          for (int h = 0; h < HD / 64; ++h)
-            tma_load_3d(sQ + t * L::kQBytes + h * (kBM * 128), &tm_q, bar(B_QFULL), h * 64,
-                        ig.kvh * prm.group, static_cast<int>(ig.tok0[t]));
-        }
-      }
+        for (int h = 0; h < HD / 64; ++h)
+          tma_load_3d(sQ + t * L::kQBytes + h * (kBM * 128), &tm_q, b, h * 64, kvh * prm.group, tok0[t]);
+      };
+      load_q(0);
       ++n_q;
-      for (int j = 0; j < ig.n_all; ++j, ++g) {
+      int n_all = 1;        // every item holds at least one key tile of its later Q tile
+      for (int j = 0; j < n_all; ++j, ++g) {
         const int st = g & 1;
         if (g >= 2 && !wait_all(bar(B_KEMPTY + st), ((g >> 1) - 1) & 1)) {
           failed = true;
@@ -420,10 +500,11 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           mbar_expect_tx(bar(B_KFULL + st), L::kKVBytes);
 #pragma unroll
           for (int h = 0; h < HD / 64; ++h)
-            tma_load_3d(sK0 + st * L::kKVBytes + h * (kBN * 128), &tm_k, bar(B_KFULL + st), h * 64, ig.kvh,
-                        (ig.j0 + j) * kBN);
+            tma_load_3d(sK0 + st * L::kKVBytes + h * (kBN * 128), &tm_k, bar(B_KFULL + st), h * 64, kvh,
+                        (j0 + j) * kBN);
         }
         last_k[st] = g;
+        if (j == 0) load_q(1);
         if (g >= 2 && !wait_all(bar(B_VEMPTY + st), ((g >> 1) - 1) & 1)) {
           failed = true;
           break;
@@ -432,14 +513,16 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           mbar_expect_tx(bar(B_VFULL + st), L::kKVBytes);
 #pragma unroll
           for (int h = 0; h < HD / 64; ++h)
-            tma_load_3d(sV0 + st * L::kKVBytes + h * (kBN * 128), &tm_v, bar(B_VFULL + st), h * 64, ig.kvh,
-                        (ig.j0 + j) * kBN);
+            tma_load_3d(sV0 + st * L::kKVBytes + h * (kBN * 128), &tm_v, bar(B_VFULL + st), h * 64, kvh,
+                        (j0 + j) * kBN);
         }
         last_v[st] = g;
+        if (j == 0) n_all = item_geom(item, prm).n_all;
       }
     }
     // Drain: every armed copy must land before the CTA can retire.
     if (n_q > 0 && !__all_sync(0xffffffffu, mbar_wait(bar(B_QFULL), (n_q - 1) & 1))) failed = true;
+    if (n_q > 0 && !__all_sync(0xffffffffu, mbar_wait(bar(B_QFULL1), (n_q - 1) & 1))) failed = true;
     for (int st = 0; st < 2; ++st) {
       if (last_k[st] >= 0 && !__all_sync(0xffffffffu, mbar_wait(bar(B_KFULL + st), (last_k[st] >> 1) & 1)))
         failed = true;
@@ -502,6 +585,11 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       // S(0): the previous item's PVs that read P from these columns were issued
       // earlier by this warp, so they complete first
       if (ig.n_kv[0] > 0) issue_s(0, g);
+      if (!wait_all(bar(B_QFULL1), n & 1)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
       if (ig.n_kv[1] > 0) issue_s(1, g);
       if (leader) {
         umma_commit(bar(B_KEMPTY + (g & 1)));
@@ -579,6 +667,8 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       const int64_t tok = (t ? ig.tok0[1] : ig.tok0[0]) + row / prm.group;
       const bool row_valid = tok >= 0 && tok < (t ? ig.tok_end[1] : ig.tok_end[0]);
       const int64_t p_row = row_valid ? prm.pos[tok] : (t ? ig.p_max[1] : ig.p_max[0]);
+      // first partial slot of the tile if its key range is split (read now, used by the epilogue)
+      const int slot0 = prm.tile_base[ig.kvh * prm.n_tiles + (t ? ig.tile[1] : ig.tile[0])];
       float m_used = -INFINITY, l_sum = 0.f;
       for (int j = 0; j < n_t; ++j, ++sc) {
         if (!__all_sync(0xffffffffu, wait_or_abort(bar(B_SFULL + t), sc & 1, abort_flag))) {
@@ -599,7 +689,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const bool full = __all_sync(0xffffffffu, lim >= kBN - 1);
         float mx = -INFINITY;
         if (full) {
-          // four independent chains of three-input max: 64 instructions, short dependency chains
+          // four independent chains of three-input max: 43 instructions, short dependency chains
           float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
           for (int c = 0; c < kBN; c += 8) {
@@ -624,42 +714,19 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           m_used = m_tile;
           rescale = true;
         }
-        float rs = 0.f;
         float ra0 = 0.f, ra1 = 0.f, rb0 = 0.f, rb1 = 0.f;   // packed partial row sums
-        const float neg_m = -m_used;
+        // a row with no visible key so far (m_used = -inf) has every key masked: a finite
+        // offset keeps the masked arguments at -inf (ex2: 0) instead of NaN
+        const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
 #pragma unroll
         for (int c4 = 0; c4 < kBN / 32; ++c4) {
           uint32_t pk[16];
-          if (full) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int c = c4 * 32 + 2 * e;
-              float x0, x1, p0, p1;
-              fma2(x0, x1, __uint_as_float(s[c]), __uint_as_float(s[c + 1]), sl2, neg_m);
-              if ((CBK_ATTN_EMU_MASK >> e) & 1) {
-                exp2_fma_pair(x0, x1, p0, p1);
-              } else {
-                p0 = ex2(x0);
-                p1 = ex2(x1);
-              }
-              if (e & 1) add2(rb0, rb1, p0, p1);
-              else add2(ra0, ra1, p0, p1);
-              pk[e] = pack2<DT>(p0, p1);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int c = c4 * 32 + 2 * e;
-              const float p0 = (c <= lim) ? ex2(__uint_as_float(s[c]) * sl2 - m_used) : 0.f;
-              const float p1 = (c + 1 <= lim) ? ex2(__uint_as_float(s[c + 1]) * sl2 - m_used) : 0.f;
-              rs += p0 + p1;
-              pk[e] = pack2<DT>(p0, p1);
-            }
-          }
+          if (full) exp_chunk<DT, false>(s, c4, sl2, neg_m, lim, ra0, ra1, rb0, rb1, pk);
+          else exp_chunk<DT, true>(s, c4, sl2, neg_m, lim, ra0, ra1, rb0, rb1, pk);
           // P chunk c4 -> columns [16 c4, 16 c4 + 16) (S was read completely above)
           tmem_st16(tS + c4 * 16, pk);
         }
-        rs += (ra0 + ra1) + (rb0 + rb1);
+        const float rs = (ra0 + ra1) + (rb0 + rb1);
         l_sum = l_sum * alpha + rs;
         if (__any_sync(0xffffffffu, rescale)) {
           // O is stable: the commit behind this tile's S(j) covered PV(j-1)
@@ -685,7 +752,6 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       ++oc;
       tc_fence_after();
-      const int slot0 = prm.tile_base[ig.kvh * prm.n_tiles + (t ? ig.tile[1] : ig.tile[0])];
       if (slot0 >= 0) {
         // split tile: this chunk's O / l (16-bit, the inputs' type), running max and row sum
         const int64_t slot = slot0 + ig.piece;
@@ -696,16 +762,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           uint32_t o[32];
           tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 v;
-            uint32_t* w = reinterpret_cast<uint32_t*>(&v);
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              w[e] = pack2<DT>(__uint_as_float(o[q * 8 + 2 * e]) * inv_l,
-                               __uint_as_float(o[q * 8 + 2 * e + 1]) * inv_l);
-            st_vec(po + c * 32 + q * 8, v);
-          }
+          store_chunk<DT>(po + c * 32, o, inv_l, prm.store_v8);
         }
         prm.part_ml[slot * kBM + row] = make_float2(m_used, l_sum);
       } else {
@@ -717,16 +774,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           uint32_t o[32];
           tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
-          if (row_valid) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 v;
-              uint16_t* h = reinterpret_cast<uint16_t*>(&v);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) h[e] = Elem<DT>::from_f(__uint_as_float(o[q * 8 + e]) * inv_l);
-              st_vec(orow + c * 32 + q * 8, v);
-            }
-          }
+          if (row_valid) store_chunk<DT>(orow + c * 32, o, inv_l, prm.store_v8);
         }
       }
       // O has been read: the next item's first PV may overwrite it
@@ -958,20 +1006,21 @@ attn_plan_kernel(const int64_t* __restrict__ pos, int64_t n_sel, int tok_per_til
 // ---------------------------------------------------------------------------
 // Merge the partial results of split tiles:
 //   O = sum_c w_c Ohat_c / sum_c w_c,  w_c = l_c 2^(m_c - M),  Ohat_c = O_c / l_c
-// (a chunk without visible keys has l = 0 and weight 0).  Work unit = half a
-// split tile (64 rows), one CTA; a thread owns kVecThr 8-element vectors of
-// different rows and computes those rows' maxima and weights itself from the
-// (m, l) pairs (no shared memory, no block barriers).  The first kCombinePre
-// chunks' O vectors are loaded together with the (m, l) pairs, so a unit of up
-// to kCombinePre chunks costs one round trip to L2.  Sums run over the chunks in
-// increasing order, so results are deterministic.
+// (a chunk without visible keys has l = 0 and weight 0).  Work unit = a quarter
+// of a split tile (32 rows), one CTA of 128 threads; a thread owns kVecThr
+// 8-element vectors of different rows and computes those rows' maxima and
+// weights itself from the (m, l) pairs (no shared memory, no block barriers).
+// The first kCombinePre chunks' O vectors and (m, l) pairs are loaded together,
+// so a unit of up to kCombinePre chunks costs one round trip to L2; small units
+// and few registers let every unit of a call have its own resident CTA.  Sums run
+// over the chunks in increasing order, so results are deterministic.
 // ---------------------------------------------------------------------------
-constexpr int kCombineThreads = 256;
-constexpr int kCombineRows = 64;        // rows per work unit
-constexpr int kCombinePre = 4;          // chunk rows loaded together
+constexpr int kCombineThreads = 128;
+constexpr int kCombineRows = 32;        // rows per work unit
+constexpr int kCombinePre = 2;          // chunk rows loaded together (most split tiles have two)
 
 template <int DT, int HD>
-__global__ void __launch_bounds__(kCombineThreads, 2)
+__global__ void __launch_bounds__(kCombineThreads, 5)
 attn_combine_kernel(const AttnParams prm) {
   constexpr int kVecRow = HD / 8;                                     // 8-element vectors per row
   constexpr int kVecThr = kCombineRows * kVecRow / kCombineThreads;  // 4 (HD 128) or 2 (HD 64)
@@ -996,17 +1045,27 @@ attn_combine_kernel(const AttnParams prm) {
     };
     auto ml_ptr = [&](int c, int i) { return prm.part_ml + (slot0 + c) * kBM + row0 + i * kRowStep; };
     uint4 raw[kCombinePre][kVecThr];
+    float2 mlp[kCombinePre][kVecThr];
 #pragma unroll
     for (int q = 0; q < kCombinePre; ++q)
       if (q < nc) {
 #pragma unroll
-        for (int i = 0; i < kVecThr; ++i) raw[q][i] = ld_vec(o_ptr(q, i));
+        for (int i = 0; i < kVecThr; ++i) {
+          raw[q][i] = ld_vec(o_ptr(q, i));
+          mlp[q][i] = *ml_ptr(q, i);
+        }
       }
     float M[kVecThr];
 #pragma unroll
     for (int i = 0; i < kVecThr; ++i) M[i] = -INFINITY;
-#pragma unroll 4
-    for (int c = 0; c < nc; ++c)
+#pragma unroll
+    for (int q = 0; q < kCombinePre; ++q)
+      if (q < nc) {
+#pragma unroll
+        for (int i = 0; i < kVecThr; ++i)
+          if (mlp[q][i].y > 0.f) M[i] = fmaxf(M[i], mlp[q][i].x);
+      }
+    for (int c = kCombinePre; c < nc; ++c)
 #pragma unroll
       for (int i = 0; i < kVecThr; ++i) {
         const float2 ml = *ml_ptr(c, i);
@@ -1033,7 +1092,7 @@ attn_combine_kernel(const AttnParams prm) {
         if (c0 + q < nc) {
 #pragma unroll
           for (int i = 0; i < kVecThr; ++i) {
-            const float2 ml = *ml_ptr(c0 + q, i);
+            const float2 ml = c0 == 0 ? mlp[q][i] : *ml_ptr(c0 + q, i);
             const float w = ml.y > 0.f ? ml.y * ex2(ml.x - M[i]) : 0.f;
             sum[i] += w;
             const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw[q][i]);
@@ -1138,6 +1197,23 @@ static AttnLayout attn_layout(int64_t n_sel, int n_q_heads, int n_kv_heads, int 
   return a;
 }
 
+// resident CTAs of attn_combine_kernel per SM (occupancy of its registers), cached
+template <int DT, int HD>
+static int combine_ctas_per_sm() {
+  static int cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_combine_kernel<DT, HD>, kCombineThreads, 0) !=
+            cudaSuccess ||
+        n <= 0)
+      n = 1;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
 template <int DT, int HD>
 static int launch_attn(const void* q, const void* k, const void* v, const int64_t* pos,
                        int64_t n_sel, int64_t S, int n_q_heads, int n_kv_heads, float scale,
@@ -1167,6 +1243,7 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   prm.tok_per_tile = lay.tok_per_tile;
   prm.n_tiles = lay.n_tiles;
   prm.scale_log2 = scale * 1.4426950408889634f;
+  prm.store_v8 = ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(workspace)) & 31u) == 0;
   if (!reuse_plan) {
     attn_plan_kernel<<<1, kPlanThreads, 0, st>>>(
         pos, n_sel, lay.tok_per_tile, lay.n_tiles, n_kv_heads, lay.target, kAttnItemCost, lay.max_items,
@@ -1182,11 +1259,11 @@ static int launch_attn(const void* q, const void* k, const void* v, const int64_
   const int grid = sm_count();             // persistent: one CTA per SM, taking workers from the queue
   kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(mq, mk, mv, prm);
   if (int rc = check_launch("partial_attn_kernel")) return rc;
-  // one CTA per half split tile; at most every tile is split
+  // one CTA per half split tile; at most every tile is split.  One wave: no more
+  // CTAs than fit on the GPU at once (the plan's split tiles are not known on the
+  // host; CTAs past the plan's units exit at once, the others loop over units)
   const int64_t max_units = static_cast<int64_t>(n_kv_heads) * lay.n_tiles * (kBM / kCombineRows);
-  // one wave: a CTA per work unit (the plan's split tiles are not known on the host;
-  // CTAs past the plan's units exit at once), up to eight per SM
-  const int comb_grid = static_cast<int>(std::min<int64_t>(max_units, 8 * sm_count()));
+  const int comb_grid = static_cast<int>(std::min<int64_t>(max_units, combine_ctas_per_sm<DT, HD>() * sm_count()));
   // programmatic dependent launch: the merge kernel's CTAs can be placed on SMs the
   // attention kernel has left (each attention CTA signals when the queue is empty)
   cudaLaunchConfig_t cfg = {};
@@ -1254,3 +1331,4 @@ extern "C" int cbk_partial_attn(const void* q, const void* k, const void* v, con
              ? launch_attn<CBK_F16, 128>(q, k, v, pos, n_sel, S, n_q_heads, n_kv_heads, scale, out, workspace, reuse_plan, status, st)
              : launch_attn<CBK_F16, 64>(q, k, v, pos, n_sel, S, n_q_heads, n_kv_heads, scale, out, workspace, reuse_plan, status, st);
 }
+
