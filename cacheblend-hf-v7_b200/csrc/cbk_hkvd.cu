@@ -19,8 +19,13 @@
 //
 // Top-K: one CTA.  Order keys are the fp32 bit patterns mapped to a monotone
 // unsigned order; four 8-bit radix passes find the k-th largest key T and how
-// many elements equal to T are taken (lowest index first).  A tiled,
-// order-preserving compaction then writes the ascending index list.
+// many elements equal to T are taken (lowest index first).  An order-preserving
+// compaction then writes the ascending index list.  Up to 33792 keys, each
+// thread holds a run of consecutive keys in registers and the compaction is one
+// block-wide scan; above that, keys are cached in shared memory (up to 40960) or
+// re-read, each warp walks a chunk, and the compaction is per warp.  In
+// hkvd_select the top-K kernel is a programmatic dependent of the deviation
+// kernel, so its launch overlaps the deviation's tail.
 #include <mutex>
 
 #include "cbk_common.cuh"
@@ -51,6 +56,9 @@ deviation_kernel(const uint16_t* __restrict__ k_new, int64_t new_stride,
                  const cbk_chunk_src* __restrict__ old_srcs, const int64_t* __restrict__ chunk_start,
                  int n_chunks, int64_t S, int64_t feat, float* __restrict__ dev) {
   const int lane = threadIdx.x & 31;
+  // the top-K kernel that follows in hkvd_select is a programmatic dependent: it may
+  // be placed once every CTA of this grid has started, and waits for this grid's end
+  asm volatile("griddepcontrol.launch_dependents;");
   const int64_t t = (static_cast<int64_t>(blockIdx.x) * kDevThreads + threadIdx.x) >> 5;
   if (t >= S) return;
   // A lane's vectors of a 128-vector group are loaded together (the fresh
@@ -136,6 +144,8 @@ topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
   __shared__ uint32_t s_prefix, s_mask;
   __shared__ int64_t s_krem, s_total_eq;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // launched as a programmatic dependent of the deviation kernel (a no-op otherwise)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const bool cached = S <= kTopkSmemKeys;
   const int64_t chunk = ((S + kTopkWarps - 1) / kTopkWarps + 31) & ~int64_t{31};
   const int64_t w_lo = warp * chunk, w_hi = w_lo + chunk < S ? w_lo + chunk : S;
@@ -284,6 +294,141 @@ topk_kernel(const float* __restrict__ dev, int64_t S, int64_t k, int force_last,
   }
 }
 
+// Top-K for S <= kTopkSmallMax (blended prefills up to ~33K tokens): the
+// same radix select and the same selection, with each thread holding a run of
+// kTopkRun consecutive keys in registers (no shared-memory key array, no re-reads),
+// and the ordered compaction as one block-wide scan of (keys above T, keys equal to
+// T) per thread: a thread's first output slot is
+//   (keys above T before it) + min(keys equal to T before it, k_eq)
+//   - (1 if the last index is forced in and an equal key precedes it),
+// since equal keys are ranked in index order and, when the last index is forced in,
+// the equal key of rank 0 gives up its place.
+constexpr int kTopkRunMax = 33;                                   // keys per thread, at most
+constexpr int64_t kTopkSmallMax = int64_t{kTopkThreads} * kTopkRunMax;   // 33792
+
+template <int kTopkRun>
+__global__ void __launch_bounds__(kTopkThreads, 1)
+topk_small_kernel(const float* __restrict__ dev, int64_t S64, int64_t k64, int force_last,
+                  int64_t* __restrict__ idx, int32_t* status) {
+  __shared__ uint32_t s_hist[256];
+  __shared__ unsigned long long s_scan[kTopkWarps];
+  __shared__ uint32_t s_prefix, s_mask;
+  __shared__ int s_krem, s_total_eq;
+  const int S = static_cast<int>(S64), k = static_cast<int>(k64);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int i0 = tid * kTopkRun;
+  // launched as a programmatic dependent of the deviation kernel (a no-op otherwise)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int n_mine = min(max(S - i0, 0), kTopkRun);
+  uint32_t key[kTopkRun];
+#pragma unroll
+  for (int r = 0; r < kTopkRun; ++r) key[r] = r < n_mine ? order_key(dev[i0 + r]) : 0u;
+  const uint32_t last_key = order_key(dev[S - 1]);
+  for (int b = tid; b < 256; b += kTopkThreads) s_hist[b] = 0;
+  if (tid == 0) {
+    s_prefix = 0;
+    s_mask = 0;
+    s_krem = k;
+  }
+  __syncthreads();
+  // four 8-bit radix passes, high digit first
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    const uint32_t prefix = s_prefix, mask = s_mask;
+#pragma unroll
+    for (int r = 0; r < kTopkRun; ++r)
+      if (r < n_mine && (key[r] & mask) == prefix) atomicAdd(&s_hist[(key[r] >> shift) & 255u], 1u);
+    __syncthreads();
+    if (warp == 0) {
+      // lane l sums the 8 digits 255-8l .. 248-8l (descending digit order)
+      uint32_t c[8], sum = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) { c[e] = s_hist[255 - 8 * lane - e]; sum += c[e]; }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s_hist[255 - 8 * lane - e] = 0;      // ready for the next pass
+      uint32_t incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const uint32_t excl = incl - sum;
+      const int krem = s_krem;
+      const bool here = (static_cast<int>(excl) < krem) && (static_cast<int>(incl) >= krem);
+      const unsigned who = __ballot_sync(0xffffffffu, here);
+      if (here && lane == __ffs(who) - 1) {
+        uint32_t above = excl;
+        for (int e = 0; e < 8; ++e) {
+          if (static_cast<int>(above + c[e]) >= krem) {
+            const uint32_t digit = 255 - 8 * lane - e;
+            s_prefix = prefix | (digit << shift);
+            s_mask = mask | (255u << shift);
+            s_krem = krem - static_cast<int>(above);
+            s_total_eq = static_cast<int>(c[e]);
+            break;
+          }
+          above += c[e];
+        }
+      }
+    }
+    __syncthreads();
+  }
+  const uint32_t T = s_prefix;
+  const int k_eq = s_krem, total_eq = s_total_eq;
+  const bool last_sel = last_key > T || (last_key == T && total_eq <= k_eq);
+  const bool force = force_last && !last_sel;
+  // per-thread counts, one block-wide scan of (above, equal) packed in 64 bits
+  uint32_t n_gt = 0, n_eq = 0;
+#pragma unroll
+  for (int r = 0; r < kTopkRun; ++r) {
+    n_gt += (r < n_mine && key[r] > T) ? 1u : 0u;
+    n_eq += (r < n_mine && key[r] == T) ? 1u : 0u;
+  }
+  const unsigned long long mine = (static_cast<unsigned long long>(n_gt) << 32) | n_eq;
+  unsigned long long incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_scan[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned long long w = s_scan[lane];
+    unsigned long long wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    s_scan[lane] = wi - w;   // exclusive prefix of the warps' totals
+    if (lane == 31) {
+      // the selection's size: every key above T, k_eq equal ones, the forced last index
+      const int gt_all = static_cast<int>(wi >> 32), eq_all = static_cast<int>(wi & 0xffffffffull);
+      const int total = gt_all + min(eq_all, k_eq) + (force ? 1 : 0) - (force && eq_all > 0 ? 1 : 0);
+      if (total != k) report(status, CBK_STATUS_COUNT);
+    }
+  }
+  __syncthreads();
+  const unsigned long long before = s_scan[warp] + incl - mine;
+  const int gt_before = static_cast<int>(before >> 32), e_before = static_cast<int>(before & 0xffffffffull);
+  int out = gt_before + min(e_before, k_eq) - (force && e_before > 0 ? 1 : 0);
+  int eq_rank = e_before;
+#pragma unroll
+  for (int r = 0; r < kTopkRun; ++r) {
+    if (r >= n_mine) break;
+    const int i = i0 + r;
+    const bool eq = key[r] == T;
+    bool sel = key[r] > T || (eq && eq_rank < k_eq && !(force && eq_rank == 0));
+    if (force && i == S - 1) sel = true;
+    if (sel) {
+      if (out < k) idx[out] = i; else report(status, CBK_STATUS_COUNT);
+      ++out;
+    }
+    eq_rank += eq ? 1 : 0;
+  }
+}
+
 int ensure_smem_attr(const void* func, int bytes);   // cbk_api.cu
 
 static size_t topk_smem_bytes(int64_t S) {
@@ -292,10 +437,30 @@ static size_t topk_smem_bytes(int64_t S) {
 
 static int launch_topk(const float* dev, int64_t S, int64_t k, int force_last, int64_t* idx,
                        int32_t* status, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kTopkThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see deviation_kernel
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (S <= kTopkSmallMax) {
+    // keys per thread: 8, 16 or 33
+    auto kern = S <= kTopkThreads * 8 ? topk_small_kernel<8>
+                : S <= kTopkThreads * 16 ? topk_small_kernel<16> : topk_small_kernel<kTopkRunMax>;
+    cfg.dynamicSmemBytes = 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, dev, S, k, force_last, idx, status);
+    if (e != cudaSuccess) return set_error(CBK_ERR_CUDA, "topk_small_kernel launch: %s", cudaGetErrorString(e));
+    return check_launch("topk_small_kernel");
+  }
   if (int rc = ensure_smem_attr(reinterpret_cast<const void*>(topk_kernel),
                                 static_cast<int>(kTopkSmemKeys * sizeof(uint32_t))))
     return rc;
-  topk_kernel<<<1, kTopkThreads, topk_smem_bytes(S), st>>>(dev, S, k, force_last, idx, status);
+  cfg.dynamicSmemBytes = topk_smem_bytes(S);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_kernel, dev, S, k, force_last, idx, status);
+  if (e != cudaSuccess) return set_error(CBK_ERR_CUDA, "topk_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("topk_kernel");
 }
 

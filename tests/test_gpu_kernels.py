@@ -228,8 +228,15 @@ def test_kv_deviation_api_vs_reference_golden():
 def _topk_cases():
     rng = np.random.default_rng(11)
     cases = []
-    for S in (1, 2, 7, 544, 1025, 6208, 40960, 40961, 131328):
+    # sizes at the edges of the kernel's size classes: 8, 16 and 33 keys per thread in
+    # registers (S <= 8192, 16384, 33792), keys in shared memory (S <= 40960), keys
+    # re-read from global memory
+    for S in (1, 2, 7, 544, 1025, 6208, 8192, 8193, 16384, 16385, 33792, 33793, 40960, 40961, 131328):
         cases.append((f"rand{S}", rng.random(S, dtype=np.float32)))
+    for S in (9000, 20000):
+        q = np.round(rng.random(S) * 16).astype(np.float32)
+        q[-1] = 8.0
+        cases.append((f"quantised{S}", q))
     z = rng.random(3000, dtype=np.float32)
     z[:1000] = 0.0
     cases.append(("zeros_prefix", z))
