@@ -192,6 +192,47 @@ def _short_kernels_alone(lw, chunks, store, idx, S, cfg, device, hbm_peak, reps=
     return out
 
 
+def _torch_restatement_gpu(model, chunks, store, idx, S, device, steps=3):
+    """Context for the kernels: the reference's blended prefill restated with stock
+    torch ops (concat, masks, repeat_interleave'd K/V, SDPA, index_put; the module
+    tests/ref_torch.py, which the end-to-end tests compare against) in bf16 on the
+    same GPU, plus its HKVD the same way (fp32 difference, square, sum; topk; sort;
+    the force-include check on the host).  The selection is the device's own, and
+    only the selected rows' logits are formed (the reference's dense (1, S, V)
+    logits are not), so this is a lower bound on the reference's own GPU time."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import ref_torch
+    from cacheblend.fusor import _store_entries
+    entries = _store_entries(store, chunks, "bench")
+    ids = torch.tensor([t for c in chunks for t in c.token_ids], device=device)
+    kv = model.config.num_key_value_heads * (model.config.hidden_size // model.config.num_attention_heads)
+    k_old = torch.cat([e["K"][CHECK_LAYER] for e in entries], dim=1)[0]
+    k_new = (k_old.float() + 0.05 * torch.randn(k_old.shape, device=device,
+                                                generator=torch.Generator(device=device).manual_seed(3))).to(k_old.dtype)
+    k_sel = idx.numel()
+
+    def one():
+        dev = ((k_new.float() - k_old.float()) ** 2).sum(-1)
+        sel = torch.sort(torch.topk(dev, k_sel).indices).values
+        if int(sel[-1].item()) != S - 1:                       # force-include on the host
+            sel = torch.sort(torch.cat([sel[1:], torch.tensor([S - 1], device=device)])).values
+        return ref_torch.selective_logits(model, ids, entries, idx, CHECK_LAYER)
+
+    one()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    return {"ms_per_step": round(ms, 3), "tokens_per_s": round(S / (ms * 1e-3), 1), "steps": steps,
+            "how": "the reference's steps in stock torch ops on the same GPU (tests/ref_torch.py + torch HKVD), "
+                   "bf16, the same selection, selected-row logits only; CUDA events around the steps"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -376,6 +417,7 @@ def run_ours(args):
             traffic = None
 
     alone = _short_kernels_alone(lw, reqs[0], store, idx, S, cfg, device, hbm_peak)
+    torch_ref = _torch_restatement_gpu(model, reqs[0], store, idx, S, device) if world == 1 else None
 
     launches = sum(launch_counts.values())
     res = {
@@ -444,6 +486,8 @@ def run_ours(args):
         "timed_path": ("fuse_selective default: a CUDA graph of the request geometry, captured on the first "
                        "call, replayed per step" if use_graph else "fuse_selective(cuda_graph=False)"),
     }
+    if torch_ref is not None:
+        res["gpu_torch_restatement"] = torch_ref
     if world == 1 and not args.no_cpu_baseline:       # host-core baseline: rank 0 at N=1 only
         res["cpu_baseline"] = cpu_baseline()
     if world > 1:
