@@ -78,6 +78,13 @@ constexpr int kAttnWorkersPerSm = CBK_ATTN_WORKERS_PER_SM;
 #define CBK_ATTN_DYN_PCT 0
 #endif
 constexpr int kAttnDynPct = CBK_ATTN_DYN_PCT;
+// PV of a key tile in two halves: the softmax warps release the first 64 keys'
+// P once it is stored, so PV over them runs while the last 64 are exponentiated,
+// and the next S = QK^T (which overwrites P) follows the second half sooner.
+#ifndef CBK_ATTN_PV_SPLIT
+#define CBK_ATTN_PV_SPLIT 1
+#endif
+constexpr bool kPvSplit = CBK_ATTN_PV_SPLIT != 0;
 
 template <int HD>
 struct AttnSmem {
@@ -96,7 +103,9 @@ struct AttnSmem {
 
 enum Bar { B_QFULL = 0, B_QEMPTY = 1, B_KFULL = 2, B_KEMPTY = 4, B_VFULL = 6, B_VEMPTY = 8,
            B_SFULL = 10, B_PFULL = 12, B_ODONE = 14, B_OFREE = 16, B_IFULL = 18, B_IEMPTY = 20,
-           B_DRAIN = 22, B_QFULL1 = 23 };   // B_QFULL: Q tile 0 landed, B_QFULL1: Q tile 1
+           B_DRAIN = 22, B_QFULL1 = 23, B_PHALF = 24 };
+// B_QFULL: Q tile 0 landed, B_QFULL1: Q tile 1; B_PHALF + t: the first half of
+// tile t's P (keys 0-63 of the key tile) is in TMEM
 
 // Work plan in the caller's workspace (written by attn_plan_kernel).
 struct AttnPlanHeader {
@@ -380,6 +389,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_init(bar(B_VEMPTY + i), 1);
       mbar_init(bar(B_SFULL + i), 1);
       mbar_init(bar(B_PFULL + i), 4);     // one arrive per softmax warp of the tile
+      mbar_init(bar(B_PHALF + i), 4);
       mbar_init(bar(B_ODONE + i), 1);
       mbar_init(bar(B_OFREE + i), 4);
       mbar_init(bar(B_IFULL + i), 1);
@@ -557,10 +567,11 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       if (leader) umma_commit(bar(B_SFULL + t));
     };
-    auto issue_pv = [&](int t, int g, bool acc) {
+    // O (+)= P V over the keys [16 kk_lo, 16 kk_hi) of the key tile
+    auto issue_pv = [&](int t, int g, bool acc, int kk_lo, int kk_hi) {
       const uint64_t v0 = (g & 1) ? dv[1] : dv[0];
 #pragma unroll
-      for (int kk = 0; kk < kBN / 16; ++kk)
+      for (int kk = kk_lo; kk < kk_hi; ++kk)
         if (leader)
           umma_f16_ts(tmem + 256 * t + kBN, tmem + 256 * t + kk * 8, v0 + ((kk * 16 * 128) >> 4), idesc_o,
                       (acc || kk > 0) ? 1u : 0u);
@@ -610,18 +621,33 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int t = 0; t < 2; ++t) {
           const int n_t = ig.n_kv[t];
           if (j >= n_t) continue;
-          if (!wait_all(bar(B_PFULL + t), pc[t] & 1)) {
+          if (kPvSplit) {
+            if (!wait_all(bar(B_PHALF + t), pc[t] & 1)) {
+              failed = true;
+              break;
+            }
+          } else if (!wait_all(bar(B_PFULL + t), pc[t] & 1)) {
             failed = true;
             break;
           }
-          ++pc[t];
           // the first PV of an item overwrites O: the previous epilogue must have read it
           if (j == 0 && oc[t] > 0 && !wait_all(bar(B_OFREE + t), (oc[t] - 1) & 1)) {
             failed = true;
             break;
           }
           tc_fence_after();
-          issue_pv(t, gj, j > 0);
+          if (kPvSplit) {
+            issue_pv(t, gj, j > 0, 0, kBN / 32);
+            if (!wait_all(bar(B_PFULL + t), pc[t] & 1)) {
+              failed = true;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, gj, true, kBN / 32, kBN / 16);
+          } else {
+            issue_pv(t, gj, j > 0, 0, kBN / 16);
+          }
+          ++pc[t];
           if (j + 1 < n_t) {
             issue_s(t, gj + 1);
           } else {
@@ -714,6 +740,21 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           m_used = m_tile;
           rescale = true;
         }
+        // O is rescaled before any P of this step is released, since PV(j) must see
+        // it (O is stable: the commit behind this tile's S(j) covered PV(j-1))
+        auto rescale_o = [&]() {
+          if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+            for (int c = 0; c < HD / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(tO + c * 32, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st32(tO + c * 32, o);
+            }
+          }
+        };
         float ra0 = 0.f, ra1 = 0.f, rb0 = 0.f, rb1 = 0.f;   // packed partial row sums
         // a row with no visible key so far (m_used = -inf) has every key masked: a finite
         // offset keeps the masked arguments at -inf (ex2: 0) instead of NaN
@@ -725,21 +766,19 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           else exp_chunk<DT, true>(s, c4, sl2, neg_m, lim, ra0, ra1, rb0, rb1, pk);
           // P chunk c4 -> columns [16 c4, 16 c4 + 16) (S was read completely above)
           tmem_st16(tS + c4 * 16, pk);
+          if (kPvSplit && c4 == kBN / 64 - 1) {
+            // keys 0-63 of P stored (their S registers are free for the rescale of O):
+            // their PV may start
+            rescale_o();
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_PHALF + t));
+          }
         }
         const float rs = (ra0 + ra1) + (rb0 + rb1);
         l_sum = l_sum * alpha + rs;
-        if (__any_sync(0xffffffffu, rescale)) {
-          // O is stable: the commit behind this tile's S(j) covered PV(j-1)
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(tO + c * 32, o);
-          }
-        }
+        if (!kPvSplit) rescale_o();
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
