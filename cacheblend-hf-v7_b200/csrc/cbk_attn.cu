@@ -4,7 +4,8 @@
 // tile are r = tok * G + h (G = q heads per KV head, 128 / G selected tokens per
 // tile), so K/V tiles are shared by the GQA group without expanding them.  Keys
 // are visited in 128-key tiles; causality is a per-row position compare (no
-// mask tensor).
+// mask tensor): on a diagonal key tile the invisible scores are set to -inf in
+// registers, and the tile then runs the same code as a fully visible one.
 //
 // Work plan (attn_plan_kernel, on the device from the positions, so no host
 // synchronisation; reusable by every layer that attends with the same
@@ -34,11 +35,12 @@
 //   warp 0        producer: fetches items, loads both Q tiles, then K and V tiles
 //                 into two separate 2-stage rings (TMA; one elected lane issues)
 //   warp 1        MMA issuer (one elected lane of the converged warp): per key
-//                 tile j, for t = 0, 1: O_t += P_t(j) V(j),
-//                 then S_t(j+1) = Q_t K(j+1)^T.  MMAs issued by one lane run
-//                 in order, so S_t(j+1) overwrites P_t(j) only after the PV
-//                 that reads it; while one tile's softmax runs, the tensor core
-//                 works on the other tile.
+//                 tile j, for t = 0, 1: O_t += P_t(j) V(j) over keys 0-63 as
+//                 soon as the softmax has stored that half of P, over keys
+//                 64-127 once all of P is stored, then S_t(j+1) = Q_t K(j+1)^T.
+//                 MMAs issued by one lane run in order, so S_t(j+1) overwrites
+//                 P_t(j) only after the PV that reads it; while one tile's
+//                 softmax runs, the tensor core works on the other tile.
 //   warp 2        TMEM allocator
 //   warps 4..7    softmax of tile 0; warps 8..11 softmax of tile 1.  Thread i of
 //                 warp w owns TMEM lane 32*(w%4)+i, i.e. one row: max / exp / sum
@@ -266,11 +268,10 @@ __device__ __forceinline__ void exp2_fma_pair(float x0, float x1, float& y0, flo
 
 // P = 2^(s * sl2 - m) of columns [32 c4, 32 c4 + 32) of a row, packed into 16-bit
 // pairs, with the row sum accumulated in packed fp32 pairs.  4 of the 16 pairs go
-// to the FMA-pipe polynomial.  With kMasked, keys c > lim are invisible: their
-// argument is set to -inf before ex2.approx (which gives 0), and the polynomial's
-// result (clamped at 2^-126) is replaced by 0.
-template <int DT, bool kMasked>
-__device__ __forceinline__ void exp_chunk(const uint32_t (&s)[kBN], int c4, float sl2, float neg_m, int lim,
+// to the FMA-pipe polynomial.  Invisible keys arrive as s = -inf: ex2.approx gives
+// 0 for them, the polynomial (its argument clamped at -126) 2^-126.
+template <int DT>
+__device__ __forceinline__ void exp_chunk(const uint32_t (&s)[kBN], int c4, float sl2, float neg_m,
                                           float& ra0, float& ra1, float& rb0, float& rb1, uint32_t (&pk)[16]) {
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
@@ -279,15 +280,7 @@ __device__ __forceinline__ void exp_chunk(const uint32_t (&s)[kBN], int c4, floa
     fma2(x0, x1, __uint_as_float(s[c]), __uint_as_float(s[c + 1]), sl2, neg_m);
     if ((CBK_ATTN_EMU_MASK >> e) & 1) {
       exp2_fma_pair(x0, x1, p0, p1);
-      if (kMasked) {
-        p0 = c <= lim ? p0 : 0.f;
-        p1 = c + 1 <= lim ? p1 : 0.f;
-      }
     } else {
-      if (kMasked) {
-        x0 = c <= lim ? x0 : -INFINITY;
-        x1 = c + 1 <= lim ? x1 : -INFINITY;
-      }
       p0 = ex2(x0);
       p1 = ex2(x1);
     }
@@ -711,25 +704,26 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int c4 = 0; c4 < kBN / 32; ++c4)
           tmem_ld32(tS + c4 * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c4 * 32]));
         tmem_wait_ld();
-        // whole tile visible to every row of the warp: no masking work
-        const bool full = __all_sync(0xffffffffu, lim >= kBN - 1);
-        float mx = -INFINITY;
-        if (full) {
-          // four independent chains of three-input max: 43 instructions, short dependency chains
-          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+        if (!__all_sync(0xffffffffu, lim >= kBN - 1)) {
+          // a key tile on the diagonal: keys past the row's position become -inf in
+          // place, and the tile takes the same max and exponential code as a fully
+          // visible one (the max ignores them; their P is 0 from ex2.approx, or
+          // 2^-126 from the clamped polynomial: a weight of ~1e-38 against the row's
+          // largest, 1).  A separate masked path, with its own max loop and selects
+          // inside the exponentials, cost ~50 % more per step than a full tile.
 #pragma unroll
-          for (int c = 0; c < kBN; c += 8) {
-            m0 = max3f(m0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
-            m1 = max3f(m1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
-            m2 = max3f(m2, __uint_as_float(s[c + 4]), __uint_as_float(s[c + 5]));
-            m3 = max3f(m3, __uint_as_float(s[c + 6]), __uint_as_float(s[c + 7]));
-          }
-          mx = max3f(m0, m1, fmaxf(m2, m3));
-        } else {
-#pragma unroll
-          for (int c = 0; c < kBN; ++c)
-            if (c <= lim) mx = fmaxf(mx, __uint_as_float(s[c]));
+          for (int c = 0; c < kBN; ++c) s[c] = c <= lim ? s[c] : 0xff800000u;
         }
+        // four independent chains of three-input max: 43 instructions, short dependency chains
+        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kBN; c += 8) {
+          m0 = max3f(m0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+          m1 = max3f(m1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
+          m2 = max3f(m2, __uint_as_float(s[c + 4]), __uint_as_float(s[c + 5]));
+          m3 = max3f(m3, __uint_as_float(s[c + 6]), __uint_as_float(s[c + 7]));
+        }
+        const float mx = max3f(m0, m1, fmaxf(m2, m3));
         const float m_tile = mx * sl2;
         float alpha = 1.f;
         bool rescale = false;
@@ -762,8 +756,7 @@ partial_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 #pragma unroll
         for (int c4 = 0; c4 < kBN / 32; ++c4) {
           uint32_t pk[16];
-          if (full) exp_chunk<DT, false>(s, c4, sl2, neg_m, lim, ra0, ra1, rb0, rb1, pk);
-          else exp_chunk<DT, true>(s, c4, sl2, neg_m, lim, ra0, ra1, rb0, rb1, pk);
+          exp_chunk<DT>(s, c4, sl2, neg_m, ra0, ra1, rb0, rb1, pk);
           // P chunk c4 -> columns [16 c4, 16 c4 + 16) (S was read completely above)
           tmem_st16(tS + c4 * 16, pk);
           if (kPvSplit && c4 == kBN / 64 - 1) {
