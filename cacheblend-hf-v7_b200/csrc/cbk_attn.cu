@@ -259,15 +259,15 @@ __device__ __forceinline__ void exp2_fma_pair(float x0, float x1, float& y0, flo
   y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
-// Pairs e (of the 16 per 32 columns; 4 of 16, the best of a 19-50 % sweep with
-// PV split in halves; 6 of 16 was best before that) whose exponentials go to the
-// FMA pipe; the others use ex2.approx.
+// Pairs e (of the 16 per 32 columns; 3 of 16, the best of a 12-50 % sweep with PV
+// split in halves and diagonal tiles masked in place; 6 of 16 was best before
+// those) whose exponentials go to the FMA pipe; the others use ex2.approx.
 #ifndef CBK_ATTN_EMU_MASK
-#define CBK_ATTN_EMU_MASK 0x8888
+#define CBK_ATTN_EMU_MASK 0x0421
 #endif
 
 // P = 2^(s * sl2 - m) of columns [32 c4, 32 c4 + 32) of a row, packed into 16-bit
-// pairs, with the row sum accumulated in packed fp32 pairs.  4 of the 16 pairs go
+// pairs, with the row sum accumulated in packed fp32 pairs.  3 of the 16 pairs go
 // to the FMA-pipe polynomial.  Invisible keys arrive as s = -inf: ex2.approx gives
 // 0 for them, the polynomial (its argument clamped at -126) 2^-126.
 template <int DT>
