@@ -221,6 +221,56 @@ def planted(case, q, k, v, pos, mistake, heads, rows=None):
     return out.reshape(n_r, Hq * D)
 
 
+def in_place_masked(case, q, k, v, pos, heads, rows=None):
+    """The case's attention (fp64) as the kernel forms it on diagonal key tiles:
+    the scores of keys past a row's position are set to -inf and the tile runs the
+    full-tile code, whose polynomial exponentials clamp the argument at -126, so a
+    masked key in a polynomial slot weighs 2^-126 (ex2.approx gives 0).  Here every
+    masked key of the key tiles the row's Q tile visits gets 2^-126 (an upper bound
+    on the kernel's residual).  Split rows are formed per piece of the kernel's plan
+    and merged as attn_combine_kernel does (w = l 2^(m - M)); a piece in which the
+    row sees no key has m = -inf and weight 0."""
+    _, S, n_sel, Hq, Hkv, D, dtype, _, _ = case
+    G = Hq // Hkv
+    qf = _f32(q, dtype).reshape(n_sel, Hq, D).astype(np.float64)
+    kf = _f32(k, dtype).reshape(S, Hkv, D).astype(np.float64)
+    vf = _f32(v, dtype).reshape(S, Hkv, D).astype(np.float64)
+    row_tile, tile_pair, cuts = plan(pos.numpy(), n_sel, G, Hkv)
+    tpt = 128 // G
+    n_tiles = -(-n_sel // tpt)
+    first = n_sel - n_tiles * tpt
+    pos_np = pos.numpy()
+    rows = np.arange(n_sel) if rows is None else np.asarray(rows)
+    out = np.zeros((len(rows), Hq, D))
+    lg2 = math.log2(math.e)
+    for h in heads:
+        kvh = h // G
+        for r, j in enumerate(rows):
+            t = row_tile[j]
+            end = (pos_np[min(first + (t + 1) * tpt, n_sel) - 1] // 128 + 1) * 128   # keys the tile visits
+            end = min(end, S)
+            x = (kf[:end, kvh] @ qf[j, h]) * D ** -0.5 * lg2                    # log2 units
+            vis = np.arange(end) <= pos_np[j]
+            # the pair's cuts are in its later tile's key tiles: pieces past this tile's
+            # last key tile hold none of its keys
+            bounds = [0] + [min(c * 128, end) for c in cuts[(kvh, tile_pair[t])]] + [end]
+            ms, ls, os_ = [], [], []
+            for a, e in zip(bounds[:-1], bounds[1:]):
+                if a >= e:
+                    continue
+                xv, sv = x[a:e], vis[a:e]
+                m = xv[sv].max() if sv.any() else -np.inf
+                p = np.where(sv, np.exp2(xv - (m if np.isfinite(m) else 0.0)), 2.0 ** -126)
+                l = p.sum()
+                ms.append(m)
+                ls.append(l)
+                os_.append((p @ vf[a:e, kvh]) / l)
+            M = max(ms)
+            w = np.array([l * 2.0 ** (m - M) if np.isfinite(m) else 0.0 for m, l in zip(ms, ls)])
+            out[r, h] = (w[:, None] * np.array(os_)).sum(axis=0) / w.sum()
+    return out.reshape(len(rows), Hq * D)
+
+
 def round_to(x, dtype):
     """Round fp64/fp32 values to the 16-bit type (what a kernel would store)."""
     return torch.from_numpy(np.asarray(x, np.float32)).to(TDT[dtype]).float().numpy()

@@ -53,3 +53,16 @@ def test_planted_mistake_is_caught(case_data, mistake):
     bad = ac.round_to(ac.planted(case, *inputs, mistake, heads, rows=rows), case[6])
     n_bad, worst = ac.violations(bad, exp, absm, case[6], cols)
     assert n_bad > 0 and worst > 4 * ac.TOL[case[6]], (mistake, n_bad, worst)
+
+
+def test_in_place_masking_stays_inside(case_data):
+    """The kernel masks diagonal key tiles in place (scores -inf, then the
+    full-tile code): masked keys may keep a weight of 2^-126 and a split piece
+    in which a row sees no key merges with weight 0.  Restated on the CPU with
+    every masked key at 2^-126, the rounded result stays as far inside the
+    bound as the exact result does."""
+    case, inputs, heads, cols, exp, absm, rows = case_data
+    got = ac.round_to(ac.in_place_masked(case, *inputs, heads, rows=rows), case[6])
+    n_bad, worst = ac.violations(got, exp, absm, case[6], cols)
+    _, worst_exact = ac.violations(ac.round_to(exp, case[6]), exp, absm, case[6], cols)
+    assert n_bad == 0 and worst <= worst_exact * (1 + 1e-6) + 1e-12, (worst, worst_exact)
